@@ -1,0 +1,183 @@
+// Device-side helpers shared by the EMA / SSD scan kernels (sm_100a).
+//
+//  * mbarrier + TMA (cp.async.bulk.tensor) wrappers, no cluster multicast;
+//  * acquire/release accessors for the inter-CTA look-back protocol;
+//  * bounded waits: every spin gives up after a wall-clock limit, sets a bit
+//    in the workspace status word and returns, so a lost producer can never
+//    hang the GPU;
+//  * float <-> element-type packs for bf16 / fp16 / fp32 tiles.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace emab {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---- workspace header words (uint32 each) --------------------------------
+constexpr int kHdrEpoch = 0;   // launch generation; tags look-back flags
+constexpr int kHdrTicket = 1;  // dynamic tile counter (reset by the last CTA)
+constexpr int kHdrDone = 2;    // finished-CTA counter (reset by the last CTA)
+constexpr int kHdrStatus = 3;  // sticky error bits, read by the host
+constexpr int kHdrWords = 64;  // header occupies 256 bytes
+
+constexpr uint32_t kStatusLookbackTimeout = 1u;
+constexpr uint32_t kStatusTmaTimeout = 2u;
+constexpr uint32_t kStatusBadTicket = 4u;  // workspace counters were not reset (misuse)
+
+constexpr uint32_t kFlagAgg = 1u;   // tile aggregate published
+constexpr uint32_t kFlagIncl = 2u;  // inclusive prefix published
+constexpr uint32_t kEpochMask = 0x3fffffffu;
+
+// Wall-clock limit of every spin-wait (nanoseconds).
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier -------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase; returns false (and sets the status bit)
+// when the limit passes.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, uint32_t* status) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, phase)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(status, kStatusTmaTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- TMA (tensor) copies; plain CTA-local forms only ---------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Make generic-proxy shared-memory writes visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- acquire / release ----------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ float ld_relaxed_gpu(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+
+// ---- element packs --------------------------------------------------------
+template <int BYTES>
+struct RawVec;
+template <>
+struct RawVec<2> { using type = uint16_t; };
+template <>
+struct RawVec<4> { using type = uint32_t; };
+template <>
+struct RawVec<8> { using type = uint2; };
+template <>
+struct RawVec<16> { using type = uint4; };
+template <>
+struct RawVec<32> { struct type { uint4 a, b; }; };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// Load N consecutive elements (N * sizeof(T) bytes, naturally aligned) as floats.
+template <typename T, int N>
+__device__ __forceinline__ void load_pack(const T* p, float (&f)[N]) {
+  using R = typename RawVec<sizeof(T) * N>::type;
+  R r = *reinterpret_cast<const R*>(p);
+  const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+  for (int k = 0; k < N; ++k) f[k] = to_f32(e[k]);
+}
+template <typename T, int N>
+__device__ __forceinline__ void store_pack(T* p, const float (&f)[N]) {
+  using R = typename RawVec<sizeof(T) * N>::type;
+  R r;
+  T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+  for (int k = 0; k < N; ++k) e[k] = from_f32<T>(f[k]);
+  *reinterpret_cast<R*>(p) = r;
+}
+
+}  // namespace emab

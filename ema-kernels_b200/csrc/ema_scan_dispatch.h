@@ -1,0 +1,49 @@
+// Host-side dispatch from runtime (dtype, block headdim, chunk size, mode) to
+// the compiled EMA scan kernel instantiations.  One definition per element
+// type lives in ema_scan_{bf16,f16,f32}.cu so the instantiations compile in
+// parallel.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "ema_scan_kernels.cuh"
+
+namespace emab {
+
+struct FwdLaunch {
+  const CUtensorMap* map_x;
+  const CUtensorMap* map_y;
+  FwdParams params;
+  int block_p, chunk, mode;
+  bool seq;
+  long long tiles;
+  cudaStream_t stream;
+};
+
+struct BwdLaunch {
+  const CUtensorMap* map_x;
+  const CUtensorMap* map_dy;
+  const CUtensorMap* map_dx;
+  BwdParams params;
+  int block_p, chunk, mode;
+  long long tiles;
+  cudaStream_t stream;
+};
+
+// Return values: 0 launched, -1 no instantiation for this combination,
+// -2 the combination needs more shared memory than a CTA may have,
+// otherwise a cudaError_t from the launch.
+int fwd_dispatch_f32(const FwdLaunch& l);
+int fwd_dispatch_bf16(const FwdLaunch& l);
+int fwd_dispatch_f16(const FwdLaunch& l);
+int bwd_dispatch_f32(const BwdLaunch& l);
+int bwd_dispatch_bf16(const BwdLaunch& l);
+int bwd_dispatch_f16(const BwdLaunch& l);
+
+constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
+
+// Set the dynamic shared-memory opt-in of `fn` once per device.
+int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask);
+
+}  // namespace emab

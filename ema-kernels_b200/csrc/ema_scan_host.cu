@@ -1,0 +1,368 @@
+// C ABI of the EMA scan library: argument validation, TMA tensor maps,
+// workspace carving and kernel dispatch.  Nothing here allocates memory.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "ema_scan_dispatch.h"
+#include "ema_ssd_b200.h"
+
+namespace emab {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+int elem_size(int dtype) { return dtype == EMA_DTYPE_F32 ? 4 : 2; }
+
+CUtensorMapDataType map_dtype(int dtype) {
+  switch (dtype) {
+    case EMA_DTYPE_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case EMA_DTYPE_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+// 4-D map over a (B, L, H, P) tensor with unit channel stride; box = one
+// (chunk, batch, head) tile of BP channels x Q tokens.
+int make_tile_map(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t L, int64_t H,
+                  int64_t P, const int64_t st[3], int BP, int Q, const char* name) {
+  const int es = elem_size(dtype);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "%s: base address must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i) {
+    if (st[i] <= 0 || (st[i] * es) % 16 != 0)
+      return fail(EMA_ERR_INVALID_ARGUMENT,
+                  "%s: stride %d (%lld elements) must be positive and a multiple of 16 bytes", name, i,
+                  static_cast<long long>(st[i]));
+  }
+  auto enc = encode_fn();
+  if (!enc) return fail(EMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(P), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[2] * es), static_cast<cuuint64_t>(st[1] * es),
+                           static_cast<cuuint64_t>(st[0] * es)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(BP), 1u, static_cast<cuuint32_t>(Q), 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(m, map_dtype(dtype), 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EMA_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return EMA_OK;
+}
+
+int block_p_for(int64_t P) {
+  if (P <= 32) return 32;
+  if (P <= 64) return 64;
+  if (P <= 128) return 128;
+  return 0;
+}
+
+struct WsLayout {
+  size_t partial, flags, decay, vals, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+WsLayout ws_layout(int64_t tiles, int BP) {
+  WsLayout l;
+  size_t off = static_cast<size_t>(kHdrWords) * 4;
+  l.partial = off;
+  off = align256(off + tiles * 4);
+  l.flags = off;
+  off = align256(off + tiles * 4);
+  l.decay = off;
+  off = align256(off + tiles * 4);
+  l.vals = off;
+  off = align256(off + static_cast<size_t>(tiles) * 2 * BP * 4);
+  l.total = off;
+  return l;
+}
+
+int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace* out) {
+  if (ws == nullptr) return fail(EMA_ERR_WORKSPACE, "workspace is NULL");
+  if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
+    return fail(EMA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  const WsLayout l = ws_layout(tiles, BP);
+  if (bytes < l.total)
+    return fail(EMA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", bytes, l.total);
+  char* base = static_cast<char*>(ws);
+  out->hdr = reinterpret_cast<uint32_t*>(base);
+  out->partial = reinterpret_cast<float*>(base + l.partial);
+  out->flags = reinterpret_cast<uint32_t*>(base + l.flags);
+  out->decay = reinterpret_cast<float*>(base + l.decay);
+  out->vals = reinterpret_cast<float*>(base + l.vals);
+  return EMA_OK;
+}
+
+int check_shape(int64_t B, int64_t L, int64_t H, int64_t P, int64_t Q, int dtype) {
+  if (B < 0 || L < 0 || H <= 0 || P <= 0)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "bad shape batch=%lld seqlen=%lld nheads=%lld headdim=%lld",
+                (long long)B, (long long)L, (long long)H, (long long)P);
+  if (Q != 64 && Q != 128 && Q != 256)
+    return fail(EMA_ERR_UNSUPPORTED, "chunk_size must be 64, 128 or 256 (got %lld)", (long long)Q);
+  if (dtype != EMA_DTYPE_F32 && dtype != EMA_DTYPE_BF16 && dtype != EMA_DTYPE_F16)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "unknown dtype code %d", dtype);
+  if (block_p_for(P) == 0)
+    return fail(EMA_ERR_UNSUPPORTED, "headdim must be <= 128 (got %lld)", (long long)P);
+  if ((P * elem_size(dtype)) % 16 != 0)
+    return fail(EMA_ERR_UNSUPPORTED, "headdim * element size must be a multiple of 16 bytes (headdim=%lld)",
+                (long long)P);
+  const int64_t nc = (L + Q - 1) / Q;
+  if (B > INT32_MAX || L > INT32_MAX || H > INT32_MAX || B * H * nc > INT32_MAX)
+    return fail(EMA_ERR_UNSUPPORTED, "problem too large for 32-bit tile indices");
+  return EMA_OK;
+}
+
+int map_dispatch_result(int r, const char* what) {
+  if (r == 0) return EMA_OK;
+  if (r == -1) return fail(EMA_ERR_UNSUPPORTED, "%s: no kernel for this combination", what);
+  if (r == -2) return fail(EMA_ERR_UNSUPPORTED, "%s: tile needs more shared memory than a CTA has", what);
+  return fail(EMA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(static_cast<cudaError_t>(r)));
+}
+
+}  // namespace
+
+int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const unsigned long long bit = (dev < 64) ? (1ull << dev) : 0ull;
+  auto* m = reinterpret_cast<std::atomic<unsigned long long>*>(device_mask);
+  if (bit && (m->load(std::memory_order_acquire) & bit)) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (bit) m->fetch_or(bit, std::memory_order_acq_rel);
+  return 0;
+}
+
+}  // namespace emab
+
+using namespace emab;
+
+extern "C" {
+
+size_t ema_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                               int64_t chunk_size) {
+  if (batch <= 0 || seqlen <= 0 || nheads <= 0 || headdim <= 0 || chunk_size <= 0) return 256;
+  const int BP = block_p_for(headdim) ? block_p_for(headdim) : 128;
+  const int64_t nc = (seqlen + chunk_size - 1) / chunk_size;
+  return ws_layout(batch * nheads * nc, BP).total;
+}
+
+int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
+  if (a == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "args is NULL");
+  int r = check_shape(a->batch, a->seqlen, a->nheads, a->headdim, a->chunk_size, a->dtype);
+  if (r) return r;
+  if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
+  if (a->x == nullptr || a->out == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "x and out are required");
+  const bool ref_form = a->dA != nullptr;
+  const bool dt_form = a->dt != nullptr || a->A != nullptr;
+  if (ref_form == dt_form || (dt_form && (a->dt == nullptr || a->A == nullptr)))
+    return fail(EMA_ERR_INVALID_ARGUMENT, "give either dA, or both dt and A");
+  if (dt_form && (a->da_cs != nullptr || a->da_cs_sum != nullptr))
+    return fail(EMA_ERR_INVALID_ARGUMENT, "da_cs / da_cs_sum are outputs of the dA form only");
+  const bool seq = a->seq_idx != nullptr;
+  if (seq && (a->seq_idx_type < EMA_IDX_I8 || a->seq_idx_type > EMA_IDX_I64))
+    return fail(EMA_ERR_INVALID_ARGUMENT, "seq_idx_type must be EMA_IDX_I8/I32/I64");
+  if (seq && dt_form) return fail(EMA_ERR_UNSUPPORTED, "seq_idx is supported with the dA form only");
+
+  const int Q = static_cast<int>(a->chunk_size);
+  const int BP = block_p_for(a->headdim);
+  const int64_t nc = (a->seqlen + Q - 1) / Q;
+  const int64_t tiles = a->batch * a->nheads * nc;
+
+  FwdLaunch l{};
+  FwdParams& p = l.params;
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
+  if (r) return r;
+  CUtensorMap mx, my;
+  r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
+  if (r) return r;
+  r = make_tile_map(&my, a->out, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->out_stride, BP,
+                    Q, "out");
+  if (r) return r;
+  p.B = static_cast<int>(a->batch);
+  p.L = static_cast<int>(a->seqlen);
+  p.H = static_cast<int>(a->nheads);
+  p.P = static_cast<int>(a->headdim);
+  p.nc = static_cast<int>(nc);
+  p.dA = a->dA;
+  p.dt = a->dt;
+  p.A = a->A;
+  p.seq_idx = a->seq_idx;
+  p.seq_idx_type = a->seq_idx_type;
+  p.init = a->initial_state;
+  p.states = a->states;
+  p.st_b = a->states_stride[0];
+  p.st_c = a->states_stride[1];
+  p.st_h = a->states_stride[2];
+  p.st_p = a->states_stride[3];
+  p.da_cs = a->da_cs;
+  p.da_cs_sum = a->da_cs_sum;
+  p.final_state = a->final_state;
+  l.map_x = &mx;
+  l.map_y = &my;
+  l.block_p = BP;
+  l.chunk = Q;
+  l.mode = ref_form ? kFwdLog2 : kFwdDt;
+  l.seq = seq;
+  l.tiles = tiles;
+  l.stream = static_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case EMA_DTYPE_BF16: r = fwd_dispatch_bf16(l); break;
+    case EMA_DTYPE_F16: r = fwd_dispatch_f16(l); break;
+    default: r = fwd_dispatch_f32(l); break;
+  }
+  return map_dispatch_result(r, "ema_fwd");
+}
+
+int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
+  if (a == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "args is NULL");
+  int r = check_shape(a->batch, a->seqlen, a->nheads, a->headdim, a->chunk_size, a->dtype);
+  if (r) return r;
+  if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
+  if (a->x == nullptr || a->dout == nullptr || a->dx == nullptr || a->states == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "x, dout, dx and states are required");
+  const bool ref_form = a->da_cs != nullptr;
+  const bool dt_form = a->dt != nullptr || a->A != nullptr;
+  if (ref_form == dt_form || (dt_form && (a->dt == nullptr || a->A == nullptr)))
+    return fail(EMA_ERR_INVALID_ARGUMENT, "give either da_cs, or both dt and A");
+  if (ref_form && a->dl == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "dl output is required with da_cs");
+  if (dt_form && (a->ddt == nullptr || a->dA_out == nullptr))
+    return fail(EMA_ERR_INVALID_ARGUMENT, "ddt and dA_out outputs are required with dt/A");
+
+  const int Q = static_cast<int>(a->chunk_size);
+  const int BP = block_p_for(a->headdim);
+  const int64_t nc = (a->seqlen + Q - 1) / Q;
+  const int64_t tiles = a->batch * a->nheads * nc;
+
+  BwdLaunch l{};
+  BwdParams& p = l.params;
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
+  if (r) return r;
+  CUtensorMap mx, mdy, mdx;
+  r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
+  if (r) return r;
+  r = make_tile_map(&mdy, a->dout, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dout_stride, BP,
+                    Q, "dout");
+  if (r) return r;
+  r = make_tile_map(&mdx, a->dx, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dx_stride, BP, Q,
+                    "dx");
+  if (r) return r;
+  p.B = static_cast<int>(a->batch);
+  p.L = static_cast<int>(a->seqlen);
+  p.H = static_cast<int>(a->nheads);
+  p.P = static_cast<int>(a->headdim);
+  p.nc = static_cast<int>(nc);
+  p.da_cs = a->da_cs;
+  p.da_cs_sum = a->da_cs_sum;
+  p.dt = a->dt;
+  p.A = a->A;
+  p.states = a->states;
+  p.st_b = a->states_stride[0];
+  p.st_c = a->states_stride[1];
+  p.st_h = a->states_stride[2];
+  p.st_p = a->states_stride[3];
+  p.d_final = a->d_final_state;
+  p.d_last = a->d_last_token;
+  p.dl = a->dl;
+  p.ddt = a->ddt;
+  p.dA_out = a->dA_out;
+  p.d_init = a->d_initial_state;
+  l.map_x = &mx;
+  l.map_dy = &mdy;
+  l.map_dx = &mdx;
+  l.block_p = BP;
+  l.chunk = Q;
+  l.mode = ref_form ? kBwdCumsum : kBwdDt;
+  l.tiles = tiles;
+  l.stream = static_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;
+    case EMA_DTYPE_F16: r = bwd_dispatch_f16(l); break;
+    default: r = bwd_dispatch_f32(l); break;
+  }
+  return map_dispatch_result(r, "ema_bwd");
+}
+
+int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], float* dA_cs, const int64_t cs_stride[3],
+                        float* dA_cs_rev, const int64_t rev_stride[3], int64_t batch, int64_t nheads,
+                        int64_t seqlen, int64_t chunk_size, int32_t exp2, void* stream) {
+  if (dA == nullptr || dA_cs == nullptr || dA_cs_rev == nullptr || dA_stride == nullptr ||
+      cs_stride == nullptr || rev_stride == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "chunk_cumsum: NULL argument");
+  if (batch < 0 || nheads < 0 || seqlen < 0 || chunk_size <= 0)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "chunk_cumsum: bad shape");
+  if (chunk_size > 1024) return fail(EMA_ERR_UNSUPPORTED, "chunk_cumsum: chunk_size must be <= 1024");
+  if (batch == 0 || nheads == 0 || seqlen == 0) return EMA_OK;
+  const int64_t nc = (seqlen + chunk_size - 1) / chunk_size;
+  if (nc > INT32_MAX || nheads > 65535 || batch > 65535)
+    return fail(EMA_ERR_UNSUPPORTED, "chunk_cumsum: grid too large");
+  dim3 grid(static_cast<unsigned>(nc), static_cast<unsigned>(nheads), static_cast<unsigned>(batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int L = static_cast<int>(seqlen), Q = static_cast<int>(chunk_size);
+#define EMA_CC_LAUNCH(NTH)                                                                            \
+  chunk_cumsum_kernel<NTH><<<grid, NTH, 0, s>>>(dA, dA_stride[0], dA_stride[1], dA_stride[2], dA_cs,  \
+                                                cs_stride[0], cs_stride[1], cs_stride[2], dA_cs_rev,  \
+                                                rev_stride[0], rev_stride[1], rev_stride[2], L, Q, exp2)
+  if (Q <= 64) EMA_CC_LAUNCH(64);
+  else if (Q <= 128) EMA_CC_LAUNCH(128);
+  else if (Q <= 256) EMA_CC_LAUNCH(256);
+  else if (Q <= 512) EMA_CC_LAUNCH(512);
+  else EMA_CC_LAUNCH(1024);
+#undef EMA_CC_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "chunk_cumsum: launch failed: %s", cudaGetErrorString(e));
+  return EMA_OK;
+}
+
+int ema_workspace_status(const void* workspace, uint32_t* status, void* stream) {
+  if (workspace == nullptr || status == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t* word = static_cast<const uint32_t*>(workspace) + kHdrStatus;
+  cudaError_t e = cudaMemcpyAsync(status, word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "status read failed: %s", cudaGetErrorString(e));
+  return EMA_OK;
+}
+
+int ema_workspace_clear_status(void* workspace, void* stream) {
+  if (workspace == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "NULL workspace");
+  uint32_t* word = static_cast<uint32_t*>(workspace) + kHdrStatus;
+  cudaError_t e = cudaMemsetAsync(word, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "status clear failed: %s", cudaGetErrorString(e));
+  return EMA_OK;
+}
+
+const char* ema_last_error(void) { return g_last_error.c_str(); }
+
+const char* ema_version(void) { return "ema_ssd_b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

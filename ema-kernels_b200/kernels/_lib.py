@@ -1,0 +1,159 @@
+"""ctypes binding of libema_ssd_b200.so (the C ABI in include/ema_ssd_b200.h).
+
+The shared library is the only compute path: there is no Triton, no PyTorch
+fallback and no CPU path.  Importing this module raises ImportError when the
+library has not been built (``python ema-kernels_b200/build.py``).
+
+Scratch memory: the EMA scan kernels need a zero-initialised workspace for
+their inter-CTA look-back.  :func:`workspace` keeps one per (device, stream),
+allocated through PyTorch's caching allocator and grown on demand.  Buffers
+are never freed while the process lives, so CUDA graphs that captured them stay
+valid; launches on different streams never share one.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libema_ssd_b200.so")
+
+if not os.path.exists(_LIB_PATH):
+    raise ImportError(
+        f"{_LIB_PATH} is missing: build the CUDA library with `python ema-kernels_b200/build.py` "
+        "(there is no fallback implementation)")
+
+lib = ctypes.CDLL(_LIB_PATH)
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+IDX_CODES = {torch.int8: 1, torch.int32: 2, torch.int64: 3}
+
+EMA_OK = 0
+ERR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "workspace", 4: "CUDA error"}
+DEVSTATUS_LOOKBACK_TIMEOUT = 1
+DEVSTATUS_TMA_TIMEOUT = 2
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_ptr = ctypes.c_void_p
+
+
+class EmaFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64), ("chunk_size", _i64),
+        ("dtype", _i32), ("seq_idx_type", _i32),
+        ("x", _ptr), ("x_stride", _i64 * 3),
+        ("out", _ptr), ("out_stride", _i64 * 3),
+        ("dA", _ptr), ("dt", _ptr), ("A", _ptr), ("seq_idx", _ptr), ("initial_state", _ptr),
+        ("states", _ptr), ("states_stride", _i64 * 4),
+        ("da_cs", _ptr), ("da_cs_sum", _ptr), ("final_state", _ptr),
+        ("workspace", _ptr), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class EmaBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64), ("chunk_size", _i64),
+        ("dtype", _i32), ("reserved", _i32),
+        ("x", _ptr), ("x_stride", _i64 * 3),
+        ("dout", _ptr), ("dout_stride", _i64 * 3),
+        ("dx", _ptr), ("dx_stride", _i64 * 3),
+        ("da_cs", _ptr), ("da_cs_sum", _ptr), ("dt", _ptr), ("A", _ptr),
+        ("states", _ptr), ("states_stride", _i64 * 4),
+        ("d_final_state", _ptr), ("d_last_token", _ptr),
+        ("dl", _ptr), ("ddt", _ptr), ("dA_out", _ptr), ("d_initial_state", _ptr),
+        ("workspace", _ptr), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+lib.ema_scan_workspace_size.restype = ctypes.c_size_t
+lib.ema_scan_workspace_size.argtypes = [_i64] * 5
+lib.ema_fwd_launch.restype = ctypes.c_int
+lib.ema_fwd_launch.argtypes = [ctypes.POINTER(EmaFwdArgs), _ptr]
+lib.ema_bwd_launch.restype = ctypes.c_int
+lib.ema_bwd_launch.argtypes = [ctypes.POINTER(EmaBwdArgs), _ptr]
+lib.chunk_cumsum_launch.restype = ctypes.c_int
+lib.chunk_cumsum_launch.argtypes = [_ptr, ctypes.POINTER(_i64), _ptr, ctypes.POINTER(_i64), _ptr,
+                                    ctypes.POINTER(_i64), _i64, _i64, _i64, _i64, _i32, _ptr]
+lib.ema_workspace_status.restype = ctypes.c_int
+lib.ema_workspace_status.argtypes = [_ptr, ctypes.POINTER(ctypes.c_uint32), _ptr]
+lib.ema_workspace_clear_status.restype = ctypes.c_int
+lib.ema_workspace_clear_status.argtypes = [_ptr, _ptr]
+lib.ema_last_error.restype = ctypes.c_char_p
+lib.ema_version.restype = ctypes.c_char_p
+
+
+class EmaLaunchError(RuntimeError):
+    pass
+
+
+def check(code: int, what: str):
+    if code != EMA_OK:
+        msg = lib.ema_last_error().decode(errors="replace")
+        raise EmaLaunchError(f"{what}: {ERR_NAMES.get(code, code)}: {msg}")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+# --------------------------------------------------------------------------
+# workspaces
+# --------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_ws: dict = {}
+_ws_retired: list = []
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch of at least ``nbytes`` for the current stream of ``device``."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            if buf is not None:
+                _ws_retired.append(buf)
+            size = max(nbytes, 1 << 20)
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+def device_status(clear: bool = False) -> int:
+    """OR of the status words of every workspace (synchronises).  Non-zero means a
+    device-side wait timed out (EMA_DEVSTATUS_* bits) and results are invalid."""
+    st = 0
+    with _ws_lock:
+        bufs = list(_ws.items())
+    for (dev, sp), buf in bufs:
+        with torch.cuda.device(dev):
+            torch.cuda.synchronize(dev)
+            v = int(buf[12:16].view(torch.int32).item())
+            st |= v
+            if clear and v:
+                buf[12:16].zero_()
+    return st
+
+
+def tma_ok(t: torch.Tensor) -> bool:
+    """True when ``t`` (B, L, H, P) can be addressed by a TMA tile map as is."""
+    if t.stride(-1) != 1 or t.data_ptr() % 16:
+        return False
+    es = t.element_size()
+    return all(s > 0 and (s * es) % 16 == 0 for s in t.stride()[:3])
+
+
+def tma_ready(t: torch.Tensor) -> torch.Tensor:
+    return t if tma_ok(t) else t.contiguous()
+
+
+def strides3(t: torch.Tensor):
+    s = t.stride()
+    return (_i64 * 3)(s[0], s[1], s[2])

@@ -1,0 +1,154 @@
+"""dt-parameterised EMA chunked scan (no counterpart in the reference's own code).
+
+    h_t = exp(dt_t * A_h) * h_{t-1} + dt_t * x_t,     y_t = h_t
+
+per (batch, head, channel).  This is the reference EMA with X = dt * x and
+log2 decay dA = dt * A * log2(e), i.e. Mamba-2 SSD with d_state = 1 and
+B = C = 1; the call form follows the SSD op the reference benchmarks against
+(``mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, ...)``,
+kernels/benchmarks/bench_ema_total.py:72-76) without B, C.
+
+Shapes: x (batch, seqlen, nheads, headdim) bf16/fp16/fp32; dt (batch, seqlen,
+nheads); A (nheads,); initial/final states (batch, nheads, headdim) fp32.
+Gradients: dx = dt * G, ddt = sum_p G x + A * dl, dA = sum_{b,t} dt * dl with
+G the state gradient and dl the per-token natural-log-decay gradient.
+
+The forward stores only the chunk START states (batch, nchunks, nheads,
+headdim) fp32 for the backward; everything else is recomputed on chip, so a
+forward + backward moves the minimum HBM bytes: x twice, y, dy, dx once,
+dt twice and ddt once.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = ["ema_chunk_scan_fwd", "ema_chunk_scan_bwd", "ema_chunk_scan_combined"]
+
+
+def _check_inputs(x, dt, A, chunk_size):
+    assert x.is_cuda and dt.is_cuda and A.is_cuda, "All tensors must be on CUDA"
+    assert x.ndim == 4, "x must be (batch, seqlen, nheads, headdim)"
+    B, L, H, P = x.shape
+    assert dt.shape == (B, L, H), f"dt must be (batch, seqlen, nheads), got {tuple(dt.shape)}"
+    assert A.shape == (H,), f"A must be (nheads,), got {tuple(A.shape)}"
+    assert chunk_size in (64, 128, 256), "chunk_size must be 64, 128 or 256"
+    assert x.dtype in _lib.DTYPE_CODES, f"unsupported dtype {x.dtype}"
+    return B, L, H, P
+
+
+def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
+                       initial_states: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                       return_final_states: bool = False):
+    """Forward.  Returns (y, chunk_start_states (B, nchunks, H, P) fp32, final_states or None)."""
+    B, L, H, P = _check_inputs(x, dt, A, chunk_size)
+    dev = x.device
+    nc = -(-L // chunk_size)
+    x_k = _lib.tma_ready(x)
+    dt_k = dt.to(torch.float32).contiguous()
+    A_k = A.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    assert out.shape == x.shape and out.dtype == x.dtype and _lib.tma_ok(out), "out must match x"
+    states = torch.empty(B, nc, H, P, dtype=torch.float32, device=dev)
+    final = torch.empty(B, H, P, dtype=torch.float32, device=dev) if return_final_states else None
+    init = None
+    if initial_states is not None:
+        assert initial_states.shape == (B, H, P), "initial_states must be (batch, nheads, headdim)"
+        init = initial_states.to(torch.float32).contiguous()
+    if x.numel() == 0:
+        if final is not None:
+            final.copy_(init if init is not None else torch.zeros_like(final))
+        return out, states, final
+    ws = _lib.workspace(dev, _lib.lib.ema_scan_workspace_size(B, L, H, P, chunk_size))
+    a = _lib.EmaFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
+    a.dtype = _lib.DTYPE_CODES[x.dtype]
+    a.x, a.x_stride = x_k.data_ptr(), _lib.strides3(x_k)
+    a.out, a.out_stride = out.data_ptr(), _lib.strides3(out)
+    a.dt, a.A = dt_k.data_ptr(), A_k.data_ptr()
+    a.initial_state = _lib.ptr(init)
+    s = states.stride()
+    a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
+    a.final_state = _lib.ptr(final)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib.ema_fwd_launch(a, _lib.stream_ptr(dev)), "ema_chunk_scan_fwd")
+    return out, states, final
+
+
+def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, states: torch.Tensor,
+                       dy: torch.Tensor, chunk_size: int = 256,
+                       d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False):
+    """Backward.  Returns (dx, ddt fp32 (B,L,H), dA fp32 (H,), d_initial_states or None)."""
+    B, L, H, P = _check_inputs(x, dt, A, chunk_size)
+    dev = x.device
+    nc = -(-L // chunk_size)
+    assert states.shape == (B, nc, H, P), "states must be the forward's chunk start states"
+    assert dy.shape == x.shape
+    x_k = _lib.tma_ready(x)
+    dy_k = _lib.tma_ready(dy if dy.dtype == x.dtype else dy.to(x.dtype))
+    dt_k = dt.to(torch.float32).contiguous()
+    A_k = A.to(torch.float32).contiguous()
+    dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+    ddt = torch.empty(B, L, H, dtype=torch.float32, device=dev)
+    dA = torch.empty(H, dtype=torch.float32, device=dev)
+    d_init = torch.empty(B, H, P, dtype=torch.float32, device=dev) if need_d_initial else None
+    dfin = None if d_final_states is None else d_final_states.to(torch.float32).contiguous()
+    if x.numel() == 0:
+        dA.zero_()
+        if d_init is not None:
+            d_init.copy_(dfin if dfin is not None else torch.zeros_like(d_init))
+        return dx, ddt, dA, d_init
+    ws = _lib.workspace(dev, _lib.lib.ema_scan_workspace_size(B, L, H, P, chunk_size))
+    a = _lib.EmaBwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
+    a.dtype = _lib.DTYPE_CODES[x.dtype]
+    a.x, a.x_stride = x_k.data_ptr(), _lib.strides3(x_k)
+    a.dout, a.dout_stride = dy_k.data_ptr(), _lib.strides3(dy_k)
+    a.dx, a.dx_stride = dx.data_ptr(), _lib.strides3(dx)
+    a.dt, a.A = dt_k.data_ptr(), A_k.data_ptr()
+    s = states.stride()
+    a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
+    a.d_final_state = _lib.ptr(dfin)
+    a.ddt, a.dA_out = ddt.data_ptr(), dA.data_ptr()
+    a.d_initial_state = _lib.ptr(d_init)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib.ema_bwd_launch(a, _lib.stream_ptr(dev)), "ema_chunk_scan_bwd")
+    return dx, ddt, dA, d_init
+
+
+class EmaChunkScanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dt, A, chunk_size, initial_states, return_final_states):
+        y, states, final = ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states,
+                                              return_final_states=return_final_states)
+        ctx.save_for_backward(x, dt, A, states)
+        ctx.chunk_size = chunk_size
+        ctx.has_init = initial_states is not None
+        ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
+        if return_final_states:
+            return y, final
+        return y
+
+    @staticmethod
+    def backward(ctx, dy, *rest):
+        x, dt, A, states = ctx.saved_tensors
+        dfin = rest[0] if rest else None
+        if dy is None:
+            dy = torch.zeros_like(x)
+        dx, ddt, dA, d_init = ema_chunk_scan_bwd(x, dt, A, states, dy, ctx.chunk_size,
+                                                 d_final_states=dfin, need_d_initial=ctx.has_init)
+        return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, d_init, None
+
+
+def ema_chunk_scan_combined(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
+                            initial_states: Optional[torch.Tensor] = None,
+                            return_final_states: bool = False):
+    """Autograd op: y (and the final state when ``return_final_states``)."""
+    return EmaChunkScanFn.apply(x, dt, A, chunk_size, initial_states, return_final_states)

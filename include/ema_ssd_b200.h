@@ -1,0 +1,165 @@
+/*
+ * ema_ssd_b200.h -- C ABI of the B200 (sm_100a) EMA / Mamba-2 SSD chunked-scan library
+ * (libema_ssd_b200.so).
+ *
+ * Plain pointers and sizes only: no framework types cross this boundary.  Every
+ * launcher is asynchronous on the given CUDA stream (a cudaStream_t passed as
+ * void*; NULL = legacy default stream), allocates nothing, and returns an
+ * EMA_* status code.  Device pointers must be 16-byte aligned; tensors are
+ * row-major with the innermost (headdim / channel) stride equal to 1 unless a
+ * stride array says otherwise.
+ *
+ * Scratch ("workspace"): the single-pass kernels publish per-chunk aggregates
+ * to later CTAs (decoupled look-back).  The caller provides a device buffer of
+ * at least ema_scan_workspace_size() bytes, ZERO-FILLED ONCE when allocated.
+ * The kernels keep it consistent across calls by themselves (a generation
+ * counter in its header tags every flag; the last CTA of each launch resets
+ * the counters), so no per-call clearing is needed.  Two launches that may run
+ * at the same time on the device must use different workspaces.  Bit flags in
+ * the header's status word report device-side wait timeouts
+ * (EMA_DEVSTATUS_*); read them with ema_workspace_status().
+ */
+#ifndef EMA_SSD_B200_H_
+#define EMA_SSD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EMA_API __attribute__((visibility("default")))
+#else
+#define EMA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- codes -------------------------------------------------------------- */
+#define EMA_DTYPE_F32 0
+#define EMA_DTYPE_BF16 1
+#define EMA_DTYPE_F16 2
+
+#define EMA_IDX_NONE 0
+#define EMA_IDX_I8 1
+#define EMA_IDX_I32 2
+#define EMA_IDX_I64 3
+
+#define EMA_OK 0
+#define EMA_ERR_INVALID_ARGUMENT 1 /* null pointer, bad shape, misaligned stride */
+#define EMA_ERR_UNSUPPORTED 2      /* shape/dtype combination without a kernel */
+#define EMA_ERR_WORKSPACE 3        /* workspace missing, too small or misaligned */
+#define EMA_ERR_CUDA 4             /* CUDA runtime/driver call failed */
+
+#define EMA_DEVSTATUS_LOOKBACK_TIMEOUT 1u /* a look-back wait gave up */
+#define EMA_DEVSTATUS_TMA_TIMEOUT 2u      /* a TMA completion wait gave up */
+#define EMA_DEVSTATUS_BAD_TICKET 4u       /* workspace counters not reset: overlapping launches */
+
+/* ---- EMA forward ----------------------------------------------------------
+ * Z[t] = a[t] * Z[t-1] + w[t] * x[t] per (batch, head, channel), Z[-1] = initial_state or 0.
+ * Decay, one of:
+ *   reference form: dA (B,H,L) float32 log2 decay, a = exp2(dA), w = 1;
+ *   dt form:        dt (B,L,H) float32 and A (H,) float32, a = exp(dt*A), w = dt.
+ * seq_idx (B,L) restarts the state where the id differs from the previous token.
+ * Outputs other than `out` are optional (NULL).
+ * Replaces the launch of `ema_fwd_kernel` in `ema_fwd_triton`
+ * (kernels/forward/ema_ssd_fwd.py:474-500; kernel :236-398).
+ */
+typedef struct EmaFwdArgs {
+  int64_t batch, seqlen, nheads, headdim, chunk_size;
+  int32_t dtype;         /* EMA_DTYPE_* of x and out */
+  int32_t seq_idx_type;  /* EMA_IDX_* (EMA_IDX_NONE when seq_idx is NULL) */
+  const void* x;         /* (B,L,H,P) */
+  int64_t x_stride[3];   /* element strides of batch, seqlen, head */
+  void* out;             /* (B,L,H,P), dtype */
+  int64_t out_stride[3];
+  const float* dA;       /* reference form, (B,H,L) contiguous, or NULL */
+  const float* dt;       /* dt form, (B,L,H) contiguous, or NULL */
+  const float* A;        /* dt form, (H,) */
+  const void* seq_idx;   /* (B,L) contiguous or NULL */
+  const float* initial_state; /* (B,H,P) contiguous or NULL */
+  float* states;         /* chunk START states or NULL; element strides below */
+  int64_t states_stride[4]; /* batch, chunk, head, channel */
+  float* da_cs;          /* reference form only: (B,H,L) within-chunk cumsum of dA, or NULL */
+  float* da_cs_sum;      /* reference form only: (B,H,nchunks) chunk totals of dA, or NULL */
+  float* final_state;    /* (B,H,P) contiguous or NULL */
+  void* workspace;
+  size_t workspace_bytes;
+} EmaFwdArgs;
+
+/* ---- EMA backward ---------------------------------------------------------
+ * Adjoint of the forward.  G[t] = dout[t] + a[t+1] G[t+1], G[L-1] seeded with
+ * d_final_state; dx = w * G (+ d_last_token at t = L-1); the per-token gradient
+ * of the natural-log decay is dl[t] = sum_p G[t] a[t] Z[t-1].
+ * Decay, one of:
+ *   reference form: da_cs (B,H,L) within-chunk cumsum of the log2 decay and
+ *                   da_cs_sum (B,H,nchunks), as the forward stores them;
+ *                   output dl (B,H,L) float32;
+ *   dt form:        dt (B,L,H), A (H,); outputs ddt (B,L,H) and dA_out (H,)
+ *                   (= sum over batch and tokens of dt * dl).
+ * `states` are the forward's chunk START states (chunk 0 = the initial state).
+ * Replaces the launch of `ema_ssd_bwd_kernel_dpx` in `compute_dpx`
+ * (kernels/backward/ema_ssd_combined.py:128-167; kernel
+ * kernels/backward/ema_ssd_bwd.py:38-295).
+ */
+typedef struct EmaBwdArgs {
+  int64_t batch, seqlen, nheads, headdim, chunk_size;
+  int32_t dtype;          /* EMA_DTYPE_* of x, dout, dx */
+  int32_t reserved;
+  const void* x;
+  int64_t x_stride[3];
+  const void* dout;
+  int64_t dout_stride[3];
+  void* dx;
+  int64_t dx_stride[3];
+  const float* da_cs;     /* reference form */
+  const float* da_cs_sum; /* reference form */
+  const float* dt;        /* dt form */
+  const float* A;         /* dt form */
+  const float* states;    /* chunk start states */
+  int64_t states_stride[4]; /* batch, chunk, head, channel */
+  const float* d_final_state; /* (B,H,P) contiguous or NULL */
+  const float* d_last_token;  /* (B,H,P) contiguous or NULL; added to dx[:, L-1] */
+  float* dl;              /* reference form output (B,H,L) */
+  float* ddt;             /* dt form output (B,L,H) */
+  float* dA_out;          /* dt form output (H,) */
+  float* d_initial_state; /* (B,H,P) contiguous or NULL */
+  void* workspace;
+  size_t workspace_bytes;
+} EmaBwdArgs;
+
+/* Bytes of workspace the EMA launchers need for this shape. */
+EMA_API size_t ema_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                               int64_t chunk_size);
+
+EMA_API int ema_fwd_launch(const EmaFwdArgs* args, void* stream);
+EMA_API int ema_bwd_launch(const EmaBwdArgs* args, void* stream);
+
+/* ---- chunk cumsum ----------------------------------------------------------
+ * dA (B,H,L) float32 with element strides dA_stride[3];
+ * dA_cs[t]     = sum of dA over [chunk start, t]           (inclusive);
+ * dA_cs_rev[t] = sum of dA over (t, chunk end]              (exclusive, 0 at the chunk's last token);
+ * with exp2 != 0 both are exponentiated (the last token's reverse value is then 1).
+ * Replaces the launch of `chunk_cumsum_kernel` in `chunk_cumsum_triton`
+ * (kernels/forward/ema_ssd_fwd.py:194-211; kernel :109-157).
+ */
+EMA_API int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], float* dA_cs,
+                        const int64_t cs_stride[3], float* dA_cs_rev, const int64_t rev_stride[3],
+                        int64_t batch, int64_t nheads, int64_t seqlen, int64_t chunk_size, int32_t exp2,
+                        void* stream);
+
+/* ---- utilities ------------------------------------------------------------ */
+/* Copies the workspace status word to *status (synchronises with `stream`). */
+EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);
+/* Clears the workspace status word (asynchronously on `stream`). */
+EMA_API int ema_workspace_clear_status(void* workspace, void* stream);
+/* Human-readable detail of the last error returned on the calling thread. */
+EMA_API const char* ema_last_error(void);
+/* Library version string. */
+EMA_API const char* ema_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMA_SSD_B200_H_ */

@@ -66,17 +66,19 @@ def scan_forward(u, a, z0=None, resets=None):
     """Sequential ``z_t = a_t z_{t-1} + u_t``.
 
     u: (B, L, H, P); a: (B, L, H); z0: (B, H, P) or None; resets: (B, L) bool.
-    Returns (z (B,L,H,P), zprev (B,L,H,P) = a_t-undecayed z_{t-1}, final (B,H,P)).
+    Returns (z (B,L,H,P), zprev (B,L,H,P), final (B,H,P)); zprev[:, t] is the
+    carried state z_{t-1} before any restart at t (a restart acts as a_t = 0).
     """
     B, L, H, P = u.shape
     z = np.zeros((B, H, P)) if z0 is None else z0.copy()
     out = np.empty_like(u)
     prev = np.empty_like(u)
     for t in range(L):
-        if resets is not None and t > 0:
-            z = z * (~resets[:, t])[:, None, None]
         prev[:, t] = z
-        z = a[:, t, :, None] * z + u[:, t]
+        at = a[:, t, :, None]
+        if resets is not None and t > 0:
+            at = at * (~resets[:, t])[:, None, None]
+        z = at * z + u[:, t]
         out[:, t] = z
     return out, prev, z
 
@@ -122,8 +124,9 @@ def ema_fwd(x, dA, chunk_size=64, seq_idx=None, initial_state=None):
     states = np.zeros((B, nc, H, 1, P))
     for c in range(nc):
         states[:, c, :, 0, :] = prev[:, c * Q]  # state before the chunk's first token
-    # note: with seq_idx the stored start state is the carried state before any
-    # reset at the chunk's first token, exactly as prev[] records it.
+    # with seq_idx the stored start state is the carried state before any
+    # restart at the chunk's first token (what the reference kernel stores,
+    # ema_ssd_fwd.py:379-382, for chunk-aligned segments)
     da_cs = np.empty((B, H, L))
     da_cs_sum = np.empty((B, H, nc))
     for c in range(nc):

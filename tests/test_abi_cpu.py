@@ -1,0 +1,128 @@
+"""The C-ABI library, checked without a GPU: it loads, exports every entry point
+include/ema_ssd_b200.h declares, and its host-side validation rejects bad
+arguments before touching CUDA."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "ema_ssd_b200.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return re.findall(r"EMA_API\s+[\w\s\*]+?\b(\w+)\s*\(", src)
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("ema_fwd_launch", "ema_bwd_launch", "chunk_cumsum_launch", "ema_scan_workspace_size",
+              "ema_workspace_status", "ema_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from kernels import _lib
+    for n in _declared():
+        assert hasattr(_lib.lib, n), f"{n} not exported by {_lib._LIB_PATH}"
+
+
+def test_struct_layouts_match_header():
+    """ctypes mirrors of EmaFwdArgs / EmaBwdArgs have the C sizes (compiled with gcc here)."""
+    import subprocess
+    import tempfile
+    from kernels import _lib
+    code = ('#include "ema_ssd_b200.h"\n#include <stdio.h>\n#include <stddef.h>\n'
+            'int main(){printf("%zu %zu %zu %zu\\n", sizeof(EmaFwdArgs), sizeof(EmaBwdArgs),'
+            ' offsetof(EmaFwdArgs, workspace), offsetof(EmaBwdArgs, workspace));return 0;}\n')
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        open(c, "w").write(code)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+    sizes = [int(v) for v in out]
+    assert sizes[0] == ctypes.sizeof(_lib.EmaFwdArgs)
+    assert sizes[1] == ctypes.sizeof(_lib.EmaBwdArgs)
+    assert sizes[2] == _lib.EmaFwdArgs.workspace.offset
+    assert sizes[3] == _lib.EmaBwdArgs.workspace.offset
+
+
+def test_workspace_size_grows_with_tiles():
+    from kernels import _lib
+    f = _lib.lib.ema_scan_workspace_size
+    small = f(1, 256, 1, 64, 256)
+    big = f(8, 4096, 32, 64, 256)
+    assert 256 < small < big
+    assert big % 256 == 0
+
+
+def _fwd_args(**kw):
+    from kernels import _lib
+    a = _lib.EmaFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = 1, 256, 1, 64, 256
+    a.dtype = 1
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(chunk_size=100), 2),          # unsupported chunk
+    (dict(headdim=256), 2),             # headdim > 128
+    (dict(headdim=60), 2),              # 120 bytes not a multiple of 16
+    (dict(dtype=7), 1),                 # unknown dtype
+    (dict(nheads=0), 1),                # bad shape
+    (dict(), 1),                        # x / out missing
+])
+def test_forward_validation_without_gpu(kw, code):
+    from kernels import _lib
+    rc = _lib.lib.ema_fwd_launch(_fwd_args(**kw), None)
+    assert rc == code, _lib.lib.ema_last_error()
+
+
+def test_forward_needs_a_decay_and_a_workspace():
+    from kernels import _lib
+    fake = 1 << 20  # never dereferenced: validation fails first
+    a = _fwd_args(x=fake, out=fake)
+    assert _lib.lib.ema_fwd_launch(a, None) == 1  # neither dA nor dt/A
+    a = _fwd_args(x=fake, out=fake, dA=fake, dt=fake, A=fake)
+    assert _lib.lib.ema_fwd_launch(a, None) == 1  # both forms
+    a = _fwd_args(x=fake, out=fake, dt=fake, A=fake, seq_idx=fake, seq_idx_type=2)
+    assert _lib.lib.ema_fwd_launch(a, None) == 2  # seq_idx with the dt form
+    a = _fwd_args(x=fake, out=fake, dA=fake)
+    assert _lib.lib.ema_fwd_launch(a, None) == 3  # no workspace
+    a = _fwd_args(x=fake, out=fake, dA=fake, workspace=fake, workspace_bytes=64)
+    assert _lib.lib.ema_fwd_launch(a, None) == 3  # workspace too small
+    assert b"workspace" in _lib.lib.ema_last_error()
+
+
+def test_backward_validation_without_gpu():
+    from kernels import _lib
+    fake = 1 << 20
+    a = _lib.EmaBwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size, a.dtype = 1, 256, 1, 64, 256, 1
+    assert _lib.lib.ema_bwd_launch(a, None) == 1
+    a.x = a.dout = a.dx = a.states = fake
+    a.da_cs = fake
+    assert _lib.lib.ema_bwd_launch(a, None) == 1  # dl output missing
+    a.dl = fake
+    assert _lib.lib.ema_bwd_launch(a, None) == 3  # workspace missing
+
+
+def test_empty_problem_is_a_no_op():
+    from kernels import _lib
+    a = _fwd_args(seqlen=0)
+    assert _lib.lib.ema_fwd_launch(a, None) == 0
+
+
+def test_chunk_cumsum_validation_without_gpu():
+    from kernels import _lib
+    st = (_lib._i64 * 3)(1, 1, 1)
+    assert _lib.lib.chunk_cumsum_launch(None, st, None, st, None, st, 1, 1, 1, 64, 0, None) == 1
+    fake = 1 << 20
+    assert _lib.lib.chunk_cumsum_launch(fake, st, fake, st, fake, st, 1, 1, 1, 2048, 0, None) == 2

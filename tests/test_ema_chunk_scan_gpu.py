@@ -1,0 +1,194 @@
+"""GPU parity of the dt-parameterised EMA (benchmark configs 1, 2, 4 form)
+against the float64 oracle, plus launch-protocol checks (many launches in a
+row, CUDA-graph replay, concurrent streams)."""
+
+import numpy as np
+import pytest
+import torch
+
+from _tol import assert_fp32_close, assert_lowp_close
+from oracle import ema_oracle as eo
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    from kernels import _lib
+    yield
+    assert _lib.device_status(clear=True) == 0, "a device-side wait timed out"
+
+
+def _inputs(B, L, H, P, seed, dtype, dt_range=(1e-3, 1e-1), a_log=(0.0, np.log(16.0))):
+    x, dt, A, dy = eo.make_dt_inputs(B, L, H, P, seed=seed, dt_range=dt_range, a_log_range=a_log)
+    tx = torch.from_numpy(x).to(dtype)
+    tdy = torch.from_numpy(dy).to(dtype)
+    return tx, torch.from_numpy(dt), torch.from_numpy(A), tdy
+
+
+def _run(tx, tdt, tA, tdy, Q, init=None, dfin=None):
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    y, states, fin = ema_chunk_scan_fwd(x, dt, A, Q, initial_states=init, return_final_states=True)
+    dx, ddt, dA, dinit = ema_chunk_scan_bwd(x, dt, A, states, dy, Q, d_final_states=dfin,
+                                            need_d_initial=True)
+    return y, fin, dx, ddt, dA, dinit, states
+
+
+def test_config1_fp32_forward():
+    """B2 L512 H4 P64 chunk 64, fp32, dt = softplus(N(0,1) - 4),
+    A = -exp(U(log 1, log 16)); y against the sequential recurrence."""
+    rng = np.random.default_rng(0)
+    B, L, H, P, Q = 2, 512, 4, 64, 64
+    x = rng.standard_normal((B, L, H, P)).astype(np.float32)
+    dt = np.logaddexp(0.0, rng.standard_normal((B, L, H)) - 4.0).astype(np.float32)
+    A = (-np.exp(rng.uniform(0.0, np.log(16.0), H))).astype(np.float32)
+    dy = rng.standard_normal((B, L, H, P)).astype(np.float32)
+    y, fin, dx, ddt, dA, dinit, _ = _run(*(torch.from_numpy(v) for v in (x, dt, A, dy)), Q)
+    r = eo.ema_dt_fwd(x, dt, A)
+    g = eo.ema_dt_bwd(x, dt, A, dy)
+    assert_fp32_close(y, r["y"], "y")
+    assert_fp32_close(fin, r["final_state"], "final")
+    assert_fp32_close(dx, g["dx"], "dx")
+    assert_fp32_close(ddt, g["ddt"], "ddt")
+    assert_fp32_close(dA, g["dA"], "dA")
+
+
+def test_config2_bf16_full_size():
+    """BASELINE config 2 at full size: B8 L4096 H32 P64 chunk 256, bf16 I/O,
+    fp32 accumulation; y, dx, ddt and dA within 2e-2 rel / 1e-2 abs."""
+    B, L, H, P, Q = 8, 4096, 32, 64, 256
+    tx, tdt, tA, tdy = _inputs(B, L, H, P, 7, torch.bfloat16)
+    y, fin, dx, ddt, dA, _, _ = _run(tx, tdt, tA, tdy, Q)
+    xf = tx.float().numpy()
+    dyf = tdy.float().numpy()
+    r = eo.ema_dt_fwd(xf, tdt.numpy(), tA.numpy())
+    g = eo.ema_dt_bwd(xf, tdt.numpy(), tA.numpy(), dyf)
+    assert_lowp_close(y, r["y"], "y")
+    assert_lowp_close(dx, g["dx"], "dx")
+    assert_lowp_close(ddt, g["ddt"], "ddt")
+    assert_lowp_close(dA, g["dA"], "dA")
+    assert_fp32_close(ddt, g["ddt"], "ddt (fp32 accumulation)")
+
+
+@pytest.mark.parametrize("Q", [64, 128, 256])
+@pytest.mark.parametrize("P", [32, 64, 128])
+def test_fp32_states_and_boundaries(Q, P):
+    B, L, H = 2, 777, 3
+    tx, tdt, tA, tdy = _inputs(B, L, H, P, Q + P, torch.float32, dt_range=(1e-3, 0.5))
+    rng = np.random.default_rng(1)
+    init = rng.standard_normal((B, H, P)).astype(np.float32)
+    dfin = rng.standard_normal((B, H, P)).astype(np.float32)
+    y, fin, dx, ddt, dA, dinit, states = _run(tx, tdt, tA, tdy, Q, init=torch.from_numpy(init).to(DEV),
+                                              dfin=torch.from_numpy(dfin).to(DEV))
+    r = eo.ema_dt_fwd(tx.numpy(), tdt.numpy(), tA.numpy(), initial_state=init)
+    g = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy(), initial_state=init,
+                      d_final_state=dfin)
+    assert_fp32_close(y, r["y"], "y")
+    assert_fp32_close(fin, r["final_state"], "final")
+    assert_fp32_close(dx, g["dx"], "dx")
+    assert_fp32_close(ddt, g["ddt"], "ddt")
+    assert_fp32_close(dA, g["dA"], "dA")
+    assert_fp32_close(dinit, g["d_initial_state"], "d_initial")
+    # chunk start states: chunk 0 is the initial state, chunk k the state after token k*Q-1
+    st = states.cpu().numpy()
+    np.testing.assert_allclose(st[:, 0].transpose(0, 1, 2), init, rtol=0, atol=0)
+    for k in range(1, st.shape[1]):
+        assert_fp32_close(st[:, k], r["y"][:, k * Q - 1], f"state {k}")
+
+
+@pytest.mark.parametrize("L", [1, 63, 256, 257])
+def test_short_and_ragged_sequences(L):
+    tx, tdt, tA, tdy = _inputs(3, L, 2, 64, L, torch.float32)
+    y, fin, dx, ddt, dA, _, _ = _run(tx, tdt, tA, tdy, 256)
+    r = eo.ema_dt_fwd(tx.numpy(), tdt.numpy(), tA.numpy())
+    g = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy())
+    assert_fp32_close(y, r["y"], "y")
+    assert_fp32_close(dx, g["dx"], "dx")
+    assert_fp32_close(ddt, g["ddt"], "ddt")
+    assert_fp32_close(dA, g["dA"], "dA")
+
+
+def test_autograd_matches_oracle_and_reuses_workspace():
+    from kernels.ema_chunk_scan import ema_chunk_scan_combined
+    tx, tdt, tA, tdy = _inputs(2, 600, 4, 64, 11, torch.bfloat16)
+    x = tx.to(DEV).requires_grad_()
+    dt = tdt.to(DEV).requires_grad_()
+    A = tA.to(DEV).requires_grad_()
+    for _ in range(3):  # repeated launches on one workspace
+        x.grad = dt.grad = A.grad = None
+        y = ema_chunk_scan_combined(x, dt, A, chunk_size=128)
+        (y * tdy.to(DEV)).sum().backward()
+    g = eo.ema_dt_bwd(tx.float().numpy(), tdt.numpy(), tA.numpy(), tdy.float().numpy())
+    assert_lowp_close(x.grad, g["dx"], "dx")
+    assert_lowp_close(dt.grad, g["ddt"], "ddt")
+    assert_lowp_close(A.grad, g["dA"], "dA")
+
+
+def test_final_state_gradient_through_autograd():
+    from kernels.ema_chunk_scan import ema_chunk_scan_combined
+    tx, tdt, tA, tdy = _inputs(1, 300, 2, 32, 12, torch.float32)
+    rng = np.random.default_rng(3)
+    init = torch.from_numpy(rng.standard_normal((1, 2, 32)).astype(np.float32)).to(DEV).requires_grad_()
+    dfin = rng.standard_normal((1, 2, 32)).astype(np.float32)
+    x, dt, A = (t.to(DEV).requires_grad_() for t in (tx, tdt, tA))
+    y, fin = ema_chunk_scan_combined(x, dt, A, 64, initial_states=init, return_final_states=True)
+    ((y * tdy.to(DEV)).sum() + (fin * torch.from_numpy(dfin).to(DEV)).sum()).backward()
+    g = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy(),
+                      initial_state=init.detach().cpu().numpy(), d_final_state=dfin)
+    assert_fp32_close(x.grad, g["dx"], "dx")
+    assert_fp32_close(dt.grad, g["ddt"], "ddt")
+    assert_fp32_close(A.grad, g["dA"], "dA")
+    assert_fp32_close(init.grad, g["d_initial_state"], "d_init")
+
+
+def test_many_launches_and_cuda_graph_replay():
+    """The self-resetting workspace protocol: 200 back-to-back launches, then a
+    captured graph replayed 50 times, all equal to the first result up to the
+    rounding of the look-back path (a tile may combine its predecessor's
+    aggregate or its inclusive prefix, whichever is published first)."""
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    tx, tdt, tA, tdy = _inputs(2, 1024, 8, 64, 13, torch.bfloat16)
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    y0, st0, _ = ema_chunk_scan_fwd(x, dt, A, 256)
+    dx0, ddt0, dA0, _ = ema_chunk_scan_bwd(x, dt, A, st0, dy, 256)
+    for _ in range(200):
+        y, st, _ = ema_chunk_scan_fwd(x, dt, A, 256)
+    dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, st, dy, 256)
+    close = dict(rtol=1e-2, atol=1e-3)  # one bf16 ulp
+    torch.testing.assert_close(y, y0, **close)
+    torch.testing.assert_close(dx, dx0, **close)
+    torch.testing.assert_close(ddt, ddt0, rtol=1e-4, atol=1e-4)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ema_chunk_scan_fwd(x, dt, A, 256)  # warm the side stream's workspace
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        yg, stg, _ = ema_chunk_scan_fwd(x, dt, A, 256)
+        dxg, ddtg, dAg, _ = ema_chunk_scan_bwd(x, dt, A, stg, dy, 256)
+    for _ in range(50):
+        g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(yg, y0, **close)
+    torch.testing.assert_close(dxg, dx0, **close)
+    torch.testing.assert_close(dAg, dA0, rtol=1e-4, atol=1e-4)
+
+
+def test_concurrent_streams_use_separate_workspaces():
+    from kernels.ema_chunk_scan import ema_chunk_scan_fwd
+    tx, tdt, tA, _ = _inputs(4, 2048, 16, 64, 14, torch.bfloat16)
+    x, dt, A = (t.to(DEV) for t in (tx, tdt, tA))
+    ref, _, _ = ema_chunk_scan_fwd(x, dt, A, 256)
+    streams = [torch.cuda.Stream() for _ in range(3)]
+    outs = []
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            outs.append(ema_chunk_scan_fwd(x, dt, A, 256)[0])
+    for s in streams:
+        torch.cuda.current_stream().wait_stream(s)
+    for o in outs:
+        torch.testing.assert_close(o, ref, rtol=1e-2, atol=1e-3)
