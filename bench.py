@@ -203,6 +203,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["bench", "profile"], default="bench",
+                    help="profile: run --steps eager fwd+bwd steps and exit (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -226,6 +228,14 @@ def main():
 
     hx, hdt, hA, hdy = _inputs(rank, dev)
     x, dt, A, dy = (t.to(dev) for t in (hx, hdt, hA, hdy))
+    if args.mode == "profile":
+        for _ in range(max(1, args.steps)):
+            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q)
+            ema_chunk_scan_bwd(x, dt, A, states, dy, Q)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     # eager warm-up (allocates the workspace of this stream), then two graphs
     side = torch.cuda.Stream(dev)
