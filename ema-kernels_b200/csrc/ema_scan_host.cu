@@ -149,6 +149,8 @@ int map_dispatch_result(int r, const char* what) {
 
 }  // namespace
 
+void set_last_error(const char* msg) { g_last_error = msg; }
+
 int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -148,6 +148,21 @@ EMA_API int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], flo
                         int64_t batch, int64_t nheads, int64_t seqlen, int64_t chunk_size, int32_t exp2,
                         void* stream);
 
+/* ---- EMA forward without a caller-provided workspace ------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory (an FFI host with no device allocator, a runtime whose memory plan is
+ * fixed after start-up): same arguments and results as ema_fwd_launch, but the
+ * look-back scratch is a static device array of EMA_NOALLOC_SCRATCH_BYTES
+ * compiled into the library (held on every GPU that loads it until exit);
+ * args->workspace / workspace_bytes are ignored.  Shapes needing more scratch
+ * than that (ema_scan_workspace_size) are rejected with EMA_ERR_WORKSPACE.
+ * The first call on a device looks up the array's address and clears it, so
+ * make it before any stream capture.  Every call on a device shares the array:
+ * calls that overlap on the GPU race.  Allocates nothing.
+ */
+#define EMA_NOALLOC_SCRATCH_BYTES (4u << 20)
+EMA_API int ema_fwd_launch_noalloc(const EmaFwdArgs* args, void* stream);
+
 /* ---- utilities ------------------------------------------------------------ */
 /* Copies the workspace status word to *status (synchronises with `stream`). */
 EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);
