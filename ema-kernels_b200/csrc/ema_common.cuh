@@ -114,6 +114,32 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---- cp.async (4-byte element gathers into shared memory) ----------------
+__device__ __forceinline__ void cp_async_4(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem)
+               : "memory");
+}
+// Arrive on `bar` once all prior cp.async of this thread have landed; counts
+// against the barrier's expected arrivals (.noinc).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Barrier over the first `nthreads` threads (the consumer warps) only.
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- acquire / release ----------------------------------------------------
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
@@ -128,6 +154,22 @@ __device__ __forceinline__ float ld_relaxed_gpu(const float* p) {
   asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
   return v;
 }
+// Self-validating look-back words: {float value, uint32 tag} in one 64-bit
+// single-copy-atomic access, so a reader that sees the tag sees the value.
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t tag_word(float v, uint32_t tag) {
+  return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ uint32_t word_tag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ float word_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
 __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
 }

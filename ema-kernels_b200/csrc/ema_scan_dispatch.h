@@ -18,6 +18,7 @@ struct FwdLaunch {
   int block_p, chunk, mode;
   bool seq;
   long long tiles;
+  int num_sms;
   cudaStream_t stream;
 };
 
@@ -28,6 +29,7 @@ struct BwdLaunch {
   BwdParams params;
   int block_p, chunk, mode;
   long long tiles;
+  int num_sms;
   cudaStream_t stream;
 };
 

@@ -84,8 +84,10 @@ int block_p_for(int64_t P) {
   return 0;
 }
 
+// Workspace: 256-byte header | dA partials [tiles] f32 | aggregate records
+// [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64.
 struct WsLayout {
-  size_t partial, flags, decay, vals, total;
+  size_t partial, agg, incl, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -95,12 +97,10 @@ WsLayout ws_layout(int64_t tiles, int BP) {
   size_t off = static_cast<size_t>(kHdrWords) * 4;
   l.partial = off;
   off = align256(off + tiles * 4);
-  l.flags = off;
-  off = align256(off + tiles * 4);
-  l.decay = off;
-  off = align256(off + tiles * 4);
-  l.vals = off;
-  off = align256(off + static_cast<size_t>(tiles) * 2 * BP * 4);
+  l.agg = off;
+  off = align256(off + static_cast<size_t>(tiles) * (BP + 1) * 8);
+  l.incl = off;
+  off = align256(off + static_cast<size_t>(tiles) * BP * 8);
   l.total = off;
   return l;
 }
@@ -115,9 +115,23 @@ int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace
   char* base = static_cast<char*>(ws);
   out->hdr = reinterpret_cast<uint32_t*>(base);
   out->partial = reinterpret_cast<float*>(base + l.partial);
-  out->flags = reinterpret_cast<uint32_t*>(base + l.flags);
-  out->decay = reinterpret_cast<float*>(base + l.decay);
-  out->vals = reinterpret_cast<float*>(base + l.vals);
+  out->agg = reinterpret_cast<uint64_t*>(base + l.agg);
+  out->incl = reinterpret_cast<uint64_t*>(base + l.incl);
+  return EMA_OK;
+}
+
+int num_sms_of_current_device(int* n) {
+  static int cache[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *n = cache[dev];
+    return EMA_OK;
+  }
+  e = cudaDeviceGetAttribute(n, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) cache[dev] = *n;
   return EMA_OK;
 }
 
@@ -236,6 +250,8 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   l.mode = ref_form ? kFwdLog2 : kFwdDt;
   l.seq = seq;
   l.tiles = tiles;
+  r = num_sms_of_current_device(&l.num_sms);
+  if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = fwd_dispatch_bf16(l); break;
@@ -305,6 +321,8 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   l.chunk = Q;
   l.mode = ref_form ? kBwdCumsum : kBwdDt;
   l.tiles = tiles;
+  r = num_sms_of_current_device(&l.num_sms);
+  if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;

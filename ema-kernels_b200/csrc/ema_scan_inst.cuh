@@ -8,35 +8,40 @@
 namespace emab {
 namespace inst {
 
+// Persistent grid: every SM runs C::CTAS CTAs, never more CTAs than tiles.
+inline unsigned persistent_grid(long long tiles, int num_sms, int ctas_per_sm) {
+  const long long g = static_cast<long long>(num_sms) * ctas_per_sm;
+  return static_cast<unsigned>(tiles < g ? tiles : g);
+}
+
 template <typename T, int BP, int Q, int MODE, bool SEQ>
 int launch_fwd(const FwdLaunch& l) {
-  using S = FwdSmem<T, BP, Q>;
-  using G = ScanGeo<BP, Q>;
-  if constexpr (S::kBytes > kMaxDynSmem) {
+  using C = FwdCfg<T, BP, Q>;
+  if constexpr (!C::R::OK || C::kBytes > kMaxDynSmem) {
     return -2;
   } else {
     static unsigned long long mask = 0;
     auto fn = ema_fwd_kernel<T, BP, Q, MODE, SEQ>;
-    int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), S::kBytes, &mask);
+    int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), C::kBytes, &mask);
     if (e) return e;
-    fn<<<static_cast<unsigned>(l.tiles), G::NT, S::kBytes, l.stream>>>(*l.map_x, *l.map_y, l.params);
+    fn<<<persistent_grid(l.tiles, l.num_sms, C::CTAS), C::NT, C::kBytes, l.stream>>>(*l.map_x, *l.map_y,
+                                                                                     l.params);
     return static_cast<int>(cudaGetLastError());
   }
 }
 
 template <typename T, int BP, int Q, int MODE>
 int launch_bwd(const BwdLaunch& l) {
-  using S = BwdSmem<T, BP, Q>;
-  using G = ScanGeo<BP, Q>;
-  if constexpr (S::kBytes > kMaxDynSmem) {
+  using C = BwdCfg<T, BP, Q>;
+  if constexpr (!C::R::OK || C::kBytes > kMaxDynSmem) {
     return -2;
   } else {
     static unsigned long long mask = 0;
     auto fn = ema_bwd_kernel<T, BP, Q, MODE>;
-    int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), S::kBytes, &mask);
+    int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), C::kBytes, &mask);
     if (e) return e;
-    fn<<<static_cast<unsigned>(l.tiles), G::NT, S::kBytes, l.stream>>>(*l.map_x, *l.map_dy, *l.map_dx,
-                                                                        l.params);
+    fn<<<persistent_grid(l.tiles, l.num_sms, C::CTAS), C::NT, C::kBytes, l.stream>>>(
+        *l.map_x, *l.map_dy, *l.map_dx, l.params);
     return static_cast<int>(cudaGetLastError());
   }
 }

@@ -1,16 +1,26 @@
-// EMA chunked scan, forward and backward, as single-pass decoupled look-back
-// kernels for sm_100a.
+// EMA chunked scan, forward and backward, for sm_100a: persistent,
+// warp-specialised, single-pass decoupled look-back kernels.
 //
 // Work unit ("tile"): one chunk of Q tokens x one (batch, head) -- a [Q, P]
-// slab of x, fetched with one TMA box {P, 1, Q, 1} of the (B, L, H, P) tensor.
-// CTAs take tiles from a ticket counter in chunk-major order (forward: chunk
-// 0 first; backward: last chunk first), so every tile a CTA waits on belongs
-// to a CTA that already started: the look-back cannot deadlock.
+// slab of x (and dy), fetched with one TMA box {BP, 1, Q, 1} of the
+// (B, L, H, P) tensor.  Each CTA is persistent:
 //
-// Inside a tile, warp w owns the token segment [w*SEG, (w+1)*SEG) and lane l
-// owns channels [l*CPT, (l+1)*CPT).  Each thread runs the recurrence
-// sequentially over its segment (one FMA per element), segments are chained
-// in shared memory, tiles are chained through global memory:
+//   producer warp   takes tiles from a ticket counter (chunk-major: forward
+//                   from chunk 0, backward from the last chunk) and streams
+//                   them into an S-stage shared-memory ring -- TMA for the
+//                   x / dy tiles, cp.async for the per-token decay row, the
+//                   head's A and (backward) the chunk start state -- with one
+//                   "full" mbarrier per stage;
+//   consumer warps  scan the tile in the stage: warp w owns a token segment,
+//                   lane l owns BP/32 channels; the recurrence runs
+//                   sequentially per thread (one FMA per element), segments
+//                   are chained in shared memory, tiles through global memory.
+//
+// The tile's incoming state (forward) or outgoing gradient (backward) comes
+// from a decoupled look-back over earlier tiles of the same (batch, head)
+// chain.  Records are arrays of self-validating 64-bit words {value, tag},
+// tag = launch generation + 1, so a reader that sees the tag sees the value:
+// no flags, no fences, one round trip per hop.  Every wait is bounded.
 //
 //   forward  z_t = a_t z_{t-1} + w_t x_t          (reference form: w = 1)
 //   backward G_t = dy_t + a_{t+1} G_{t+1},  dx = w G,
@@ -18,8 +28,7 @@
 //
 // HBM traffic is the algorithmic minimum: the forward reads x and the decay
 // once and writes y once; the backward reads x, dy and the decay once and
-// writes dx and the per-token decay gradient once.  The only extra traffic is
-// the per-chunk start states (P floats per tile) and the look-back slots.
+// writes dx and the per-token decay gradient once.
 #pragma once
 
 #include "ema_common.cuh"
@@ -29,26 +38,46 @@ namespace emab {
 enum FwdMode : int { kFwdLog2 = 0, kFwdDt = 1 };
 enum BwdMode : int { kBwdCumsum = 0, kBwdDt = 1 };
 
-template <int BP, int Q>
-struct ScanGeo {
-  static constexpr int CPT = BP / 32;              // channels per lane
-  static constexpr int SEG = (BP <= 64) ? 32 : 16;  // tokens per warp segment
-  static constexpr int NW = Q / SEG;                // warps per CTA
-  static constexpr int NT = NW * 32;                // threads per CTA
-  static constexpr int RB = 8;                      // backward recompute block
-  // Backward CTAs hold two [Q, BP] tiles; aim for >= 768 resident threads per
-  // SM so several tiles stream at once (caps registers at ~85 per thread).
-  static constexpr int BWD_MIN_BLOCKS = (768 / NT) > 0 ? (768 / NT) : 1;
-  static_assert(BP % 32 == 0 && BP <= 128, "block headdim");
-  static_assert(Q % SEG == 0 && NT >= Q && NT >= BP, "geometry");
+constexpr int kSmemPerSM = 233472;      // 228 KB of shared memory per SM
+constexpr int kSmemPerCtaMax = 232448;  // 227 KB opt-in per CTA
+constexpr int kCtaReserve = 1024;       // per-CTA system reservation
+constexpr int kMaxStages = 8;
+
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// Stage count and CTAs per SM for a ring of `stage`-byte stages plus `priv`
+// bytes of per-CTA state: two CTAs per SM when each still gets >= 3 stages
+// (one computing, one draining its store, one loading), else one CTA.
+template <int STAGE, int PRIV>
+struct Ring {
+  static constexpr int S2 = ((kSmemPerSM / 2 - kCtaReserve) - PRIV) / STAGE;
+  static constexpr int S1 = (kSmemPerCtaMax - PRIV) / STAGE;
+  static constexpr bool TWO = S2 >= 3;
+  static constexpr int S = TWO ? (S2 > kMaxStages ? kMaxStages : S2) : (S1 > kMaxStages ? kMaxStages : S1);
+  static constexpr int CTAS = TWO ? 2 : 1;
+  static constexpr bool OK = S >= 1;
+  // with >= 3 stages a stage is handed back one tile late (its TMA store has
+  // surely finished reading it); with fewer, right after the store's read
+  static constexpr bool DEFERRED = S >= 3;
 };
 
+// Consumer thread 0, after committing the TMA store of tile k from stage k % S.
+template <int S, bool DEFERRED>
+__device__ __forceinline__ void release_stage(uint64_t* empty, int k) {
+  if (DEFERRED) {
+    bulk_wait_read<1>();
+    if (k > 0) mbar_arrive(&empty[(k - 1) % S]);
+  } else {
+    bulk_wait_read<0>();
+    mbar_arrive(&empty[k % S]);
+  }
+}
+
 struct ScanWorkspace {
-  uint32_t* hdr;    // kHdrWords header words
-  float* partial;   // [tiles] per-tile dA partial sums (dt-form backward)
-  uint32_t* flags;  // [tiles] look-back flags: (epoch << 2) | {0, AGG, INCL}
-  float* decay;     // [tiles] tile aggregate decay
-  float* vals;      // [tiles][2][BP] aggregate / inclusive vectors
+  uint32_t* hdr;   // kHdrWords header words
+  float* partial;  // [tiles] per-tile dA partial sums (dt-form backward)
+  uint64_t* agg;   // [tiles][BP + 1] aggregate words (index BP: decay)
+  uint64_t* incl;  // [tiles][BP] inclusive words
 };
 
 struct FwdParams {
@@ -70,7 +99,7 @@ struct FwdParams {
 struct BwdParams {
   int B, L, H, P, nc;
   const float* da_cs;      // (B,H,L)
-  const float* da_cs_sum;  // (B,H,nc) (unused by the kernel; chunk decay is the token product)
+  const float* da_cs_sum;  // (B,H,nc) (the chunk decay is the product of the token decays)
   const float* dt;         // (B,L,H)
   const float* A;          // (H,)
   const float* states;
@@ -92,91 +121,65 @@ __device__ __forceinline__ long long load_seq_id(const void* base, int type, siz
   }
 }
 
-// Walk the chain from tile `c` in direction `step` (-1: towards chunk 0,
-// +1: towards the last chunk), combining published aggregates until an
-// inclusive prefix (or the chain end) is found.  Executed by one full warp;
-// lane l returns channels [l*CPT, (l+1)*CPT) of the incoming vector in `run`
-// and the accumulated decay in `rdec`.  Returns true when the chain end was
-// reached (the caller then adds rdec * boundary value).  Waits are bounded.
+// Walk the chain from tile `c` in direction `step` (-1: towards chunk 0, +1:
+// towards the last chunk), combining published aggregates until an inclusive
+// record (or the chain end).  One full warp; lane l returns channels
+// [l*CPT, (l+1)*CPT) of the incoming vector in `run` and the accumulated
+// decay in `rdec`.  Returns true when the chain end was reached (the caller
+// adds rdec * boundary value).  A record is used only when every lane saw all
+// of its words.  Waits are bounded.
 template <int BP>
-__device__ __forceinline__ bool lookback_warp(const ScanWorkspace& ws, uint32_t epoch, int bh, int BH,
-                                              int c, int step, int nc, int lane,
-                                              float (&run)[BP / 32], float& rdec) {
+__device__ __forceinline__ bool lookback_warp(const ScanWorkspace& ws, uint32_t tag, int bh, int BH, int c,
+                                              int step, int nc, int lane, float (&run)[BP / 32],
+                                              float& rdec) {
   constexpr int CPT = BP / 32;
+  const unsigned FULL = 0xffffffffu;
 #pragma unroll
   for (int k = 0; k < CPT; ++k) run[k] = 0.f;
   rdec = 1.f;
-  const unsigned FULL = 0xffffffffu;
   for (int j = c + step; j >= 0 && j < nc; j += step) {
     const size_t slot = static_cast<size_t>(j) * BH + bh;
-    uint32_t st = 0;
-    bool timed_out = false;
+    const uint64_t* inc = ws.incl + slot * BP + lane * CPT;
+    const uint64_t* agg = ws.agg + slot * (BP + 1);
     unsigned long long t_start = 0;
     for (int it = 0;; ++it) {
-      const uint32_t f = ld_acquire_gpu(&ws.flags[slot]);
-      st = ((f >> 2) == epoch) ? (f & 3u) : 0u;
-      if (__all_sync(FULL, st != 0u)) break;
+      uint64_t wi[CPT], wa[CPT];
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) {
+        wi[k] = ld_relaxed_u64(inc + k);
+        wa[k] = ld_relaxed_u64(agg + lane * CPT + k);
+      }
+      const uint64_t wd = ld_relaxed_u64(agg + BP);
+      bool iok = true, aok = word_tag(wd) == tag;
+#pragma unroll
+      for (int k = 0; k < CPT; ++k) {
+        iok &= word_tag(wi[k]) == tag;
+        aok &= word_tag(wa[k]) == tag;
+      }
+      if (__all_sync(FULL, iok)) {
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) run[k] = fmaf(rdec, word_val(wi[k]), run[k]);
+        return false;
+      }
+      if (__all_sync(FULL, aok)) {
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) run[k] = fmaf(rdec, word_val(wa[k]), run[k]);
+        rdec *= word_val(wd);
+        break;
+      }
       if (it == 0) t_start = global_timer_ns();
       // the give-up decision is warp-uniform so every lane leaves together
       if (__any_sync(FULL, global_timer_ns() - t_start > kWaitLimitNs)) {
-        timed_out = true;
-        break;
+        if (lane == 0) atomicOr(&ws.hdr[kHdrStatus], kStatusLookbackTimeout);
+        return false;
       }
-      __nanosleep(40);
+      __nanosleep(32);
     }
-    if (timed_out) {
-      if (lane == 0) atomicOr(&ws.hdr[kHdrStatus], kStatusLookbackTimeout);
-      return false;  // leave run as accumulated so far; result is flagged invalid
-    }
-    // Every lane acquired at least the aggregate; use the inclusive prefix only
-    // when every lane acquired it (each lane reads only what it acquired).
-    const bool incl = __all_sync(FULL, st == kFlagIncl);
-    const float* v = ws.vals + slot * (2 * BP) + (incl ? BP : 0) + lane * CPT;
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) run[k] = fmaf(rdec, ld_relaxed_gpu(v + k), run[k]);
-    if (incl) return false;
-    rdec *= ld_relaxed_gpu(&ws.decay[slot]);
   }
   return true;
 }
 
-// Publish a vector (BP floats from smem) + optional decay into the tile's
-// slot, then raise the flag.  Called by all threads of the CTA.
-template <int BP>
-__device__ __forceinline__ void publish_cta(const ScanWorkspace& ws, size_t slot, int which,
-                                            const float* s_vec, float dec, uint32_t flag, int tid) {
-  if (tid < BP) {
-    ws.vals[slot * (2 * BP) + which * BP + tid] = s_vec[tid];
-    if (tid == 0 && which == 0) ws.decay[slot] = dec;
-    __threadfence();
-  }
-  __syncthreads();
-  if (tid == 0) st_release_gpu(&ws.flags[slot], flag);
-}
-
-// Last-CTA bookkeeping: count this CTA as finished; the final one resets the
-// ticket/done counters and advances the epoch for the next launch.  Returns
-// true in the last CTA (all threads), after a block barrier.
-__device__ __forceinline__ bool finish_cta(const ScanWorkspace& ws, uint32_t epoch, int tid,
-                                           uint32_t* s_flag) {
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(&ws.hdr[kHdrDone], 1u);
-    *s_flag = (prev == gridDim.x - 1) ? 1u : 0u;
-  }
-  __syncthreads();
-  return *s_flag != 0u;
-}
-__device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t epoch) {
-  __threadfence();
-  ws.hdr[kHdrTicket] = 0u;
-  ws.hdr[kHdrDone] = 0u;
-  __threadfence();
-  ws.hdr[kHdrEpoch] = (epoch + 1u) & kEpochMask;
-}
-
-// Sum of v[j] over the 32 lanes, transposed: after the call lane l holds the
-// total of index j = (l >> 2) & 7 (lanes 4j..4j+3 agree).  9 shuffles for 8 values.
+// Transposed warp sum: v[j] summed over the 32 lanes lands in lanes 4j..4j+3.
 __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
   const unsigned FULL = 0xffffffffu;
   {
@@ -209,564 +212,712 @@ __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
   return r;
 }
 
+// Completion bookkeeping, by consumer thread 0 after all of its CTA's stores:
+// true in the last CTA of the launch.
+__device__ __forceinline__ bool count_cta_done(const ScanWorkspace& ws) {
+  __threadfence();
+  const uint32_t prev = atomicAdd(&ws.hdr[kHdrDone], 1u);
+  return prev == gridDim.x - 1;
+}
+// Every CTA's producer draws exactly one ticket past the last tile, so a
+// launch that started from reset counters ends at total + gridDim.x; anything
+// else means the workspace was shared by overlapping launches.
+__device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t epoch, int total) {
+  __threadfence();
+  if (ld_volatile_u32(&ws.hdr[kHdrTicket]) != static_cast<uint32_t>(total) + gridDim.x)
+    atomicOr(&ws.hdr[kHdrStatus], kStatusBadTicket);
+  ws.hdr[kHdrTicket] = 0u;
+  ws.hdr[kHdrDone] = 0u;
+  __threadfence();
+  ws.hdr[kHdrEpoch] = (epoch + 1u) & kEpochMask;
+}
+
+// Producer-side end of stream: mark the stage as "no more tiles" with the
+// 33 arrivals its full barrier expects.
+__device__ __forceinline__ void post_sentinel(uint64_t* full_s, int* tile_s, int lane) {
+  if (lane == 0) {
+    *tile_s = -1;
+    mbar_arrive(full_s);
+  }
+  mbar_arrive(full_s);
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
-struct FwdSmem {
-  using G = ScanGeo<BP, Q>;
-  static constexpr int kX = 0;
-  static constexpr int kXBytes = Q * BP * static_cast<int>(sizeof(T));
-  static constexpr int kA = kXBytes;                 // float[Q]
-  static constexpr int kW = kA + Q * 4;              // float[Q]
-  static constexpr int kL2 = kW + Q * 4;             // float[Q]
-  static constexpr int kE = kL2 + Q * 4;             // float[NW][BP]
-  static constexpr int kD = kE + G::NW * BP * 4;     // float[NW]
-  static constexpr int kG0 = kD + G::NW * 4;         // float[NW]
-  static constexpr int kSin = kG0 + G::NW * 4;       // float[BP]
-  static constexpr int kEt = kSin + BP * 4;          // float[BP]
-  static constexpr int kMisc = kEt + BP * 4;         // float[32]
-  static constexpr int kBar = (kMisc + 32 * 4 + 15) / 16 * 16;  // uint64
-  static constexpr int kBytes = kBar + 16;
+struct FwdCfg {
+  static constexpr int CPT = BP / 32;
+  static constexpr int SEG = (BP <= 64) ? 32 : 16;
+  static constexpr int NW = Q / SEG;  // consumer warps
+  static constexpr int NC = NW * 32;  // consumer threads
+  static constexpr int NT = NC + 32;  // + producer warp
+  static_assert(BP % 32 == 0 && BP <= 128 && Q % SEG == 0 && NC >= Q && NC >= BP, "geometry");
+  static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
+  static constexpr int kStage = align_up(kX + (Q + 4) * 4, 128);  // x tile | decay row | A_h
+  // per-CTA state after the ring
+  static constexpr int oA = 0;                  // float[Q]   token decay
+  static constexpr int oW = oA + Q * 4;         // float[Q]   token weight
+  static constexpr int oL2 = oW + Q * 4;        // float[Q]   log2 decay
+  static constexpr int oE = oL2 + Q * 4;        // float[NW][BP]
+  static constexpr int oD = oE + NW * BP * 4;   // float[NW]
+  static constexpr int oG0 = oD + NW * 4;       // float[NW]
+  static constexpr int oSin = oG0 + NW * 4;     // float[BP]
+  static constexpr int oEt = oSin + BP * 4;     // float[BP]
+  static constexpr int oMisc = oEt + BP * 4;    // float[32]
+  static constexpr int oTile = oMisc + 32 * 4;  // int[kMaxStages]
+  static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);  // uint64 full[], empty[]
+  static constexpr int kPriv = oBar + 2 * kMaxStages * 8;
+  using R = Ring<kStage, kPriv>;
+  static constexpr int S = R::S;
+  static constexpr int CTAS = R::CTAS;
+  static constexpr int kPrivBase = S * kStage;
+  static constexpr int kBytes = kPrivBase + kPriv;
 };
 
 template <typename T, int BP, int Q, int MODE, bool SEQ>
-__global__ void __launch_bounds__(ScanGeo<BP, Q>::NT)
+__global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     ema_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                    const FwdParams p) {
-  using G = ScanGeo<BP, Q>;
-  using S = FwdSmem<T, BP, Q>;
-  constexpr int CPT = G::CPT, SEG = G::SEG, NW = G::NW;
+  using C = FwdCfg<T, BP, Q>;
+  constexpr int CPT = C::CPT, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
   extern __shared__ __align__(128) unsigned char smem[];
-  T* s_x = reinterpret_cast<T*>(smem + S::kX);
-  float* s_a = reinterpret_cast<float*>(smem + S::kA);
-  float* s_w = reinterpret_cast<float*>(smem + S::kW);
-  float* s_l2 = reinterpret_cast<float*>(smem + S::kL2);
-  float* s_E = reinterpret_cast<float*>(smem + S::kE);
-  float* s_D = reinterpret_cast<float*>(smem + S::kD);
-  float* s_G0 = reinterpret_cast<float*>(smem + S::kG0);
-  float* s_Sin = reinterpret_cast<float*>(smem + S::kSin);
-  float* s_Et = reinterpret_cast<float*>(smem + S::kEt);
-  float* s_misc = reinterpret_cast<float*>(smem + S::kMisc);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  __shared__ uint32_t s_tile, s_epoch, s_last;
+  unsigned char* priv = smem + C::kPrivBase;
+  float* s_a = reinterpret_cast<float*>(priv + C::oA);
+  float* s_w = reinterpret_cast<float*>(priv + C::oW);
+  float* s_l2 = reinterpret_cast<float*>(priv + C::oL2);
+  float* s_E = reinterpret_cast<float*>(priv + C::oE);
+  float* s_D = reinterpret_cast<float*>(priv + C::oD);
+  float* s_G0 = reinterpret_cast<float*>(priv + C::oG0);
+  float* s_Sin = reinterpret_cast<float*>(priv + C::oSin);
+  float* s_Et = reinterpret_cast<float*>(priv + C::oEt);
+  float* s_misc = reinterpret_cast<float*>(priv + C::oMisc);
+  int* s_tile = reinterpret_cast<int*>(priv + C::oTile);
+  uint64_t* full = reinterpret_cast<uint64_t*>(priv + C::oBar);
+  uint64_t* empty = full + kMaxStages;
+  __shared__ uint32_t s_epoch;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const ScanWorkspace& ws = p.ws;
+  uint32_t* status = &ws.hdr[kHdrStatus];
   if (tid == 0) {
-    tma_prefetch_desc(&tm_x);
-    s_tile = atomicAdd(&ws.hdr[kHdrTicket], 1u);
     s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
-    mbar_init(bar, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 33);  // producer lane 0 (expect_tx) + 32 cp.async arrivals
+      mbar_init(&empty[s], 1);  // consumer thread 0
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  if (s_tile >= gridDim.x) {  // counters not reset: workspace shared by overlapping launches
-    if (tid == 0) atomicOr(&ws.hdr[kHdrStatus], kStatusBadTicket);
+  const uint32_t epoch = s_epoch;
+  const uint32_t tag = epoch + 1u;
+  const int BH = p.B * p.H;
+  const int total = BH * p.nc;
+
+  if (warp == NW) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) tma_prefetch_desc(&tm_x);
+    for (int k = 0;; ++k) {
+      const int s = k % S;
+      if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status)) break;
+      uint32_t ticket = 0;
+      if (lane == 0) ticket = atomicAdd(&ws.hdr[kHdrTicket], 1u);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket >= static_cast<uint32_t>(total)) {
+        post_sentinel(&full[s], &s_tile[s], lane);
+        break;
+      }
+      const int c = static_cast<int>(ticket) / BH, bh = static_cast<int>(ticket) % BH;
+      const int b = bh / p.H, h = bh % p.H, t0 = c * Q;
+      unsigned char* st = smem + s * C::kStage;
+      float* raw = reinterpret_cast<float*>(st + C::kX);
+      if (lane == 0) {
+        s_tile[s] = static_cast<int>(ticket);
+        mbar_arrive_expect_tx(&full[s], C::kX);
+        tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
+      }
+      for (int i = lane; i < Q; i += 32) {
+        const int t = t0 + i;
+        if (t < p.L) {
+          if (MODE == kFwdLog2)
+            cp_async_4(raw + i, p.dA + (static_cast<size_t>(b) * p.H + h) * p.L + t);
+          else
+            cp_async_4(raw + i, p.dt + (static_cast<size_t>(b) * p.L + t) * p.H + h);
+        }
+      }
+      if (MODE == kFwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
+      cp_async_mbar_arrive_noinc(&full[s]);
+    }
+    cp_async_wait_all();
     return;
   }
-  const uint32_t epoch = s_epoch;
-  const int BH = p.B * p.H;
-  const int c = static_cast<int>(s_tile) / BH;
-  const int bh = static_cast<int>(s_tile) % BH;
-  const int b = bh / p.H, h = bh % p.H;
-  const int t0 = c * Q;
-  const size_t slot = static_cast<size_t>(c) * BH + bh;
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar, S::kXBytes);
-    tma_load_4d(s_x, &tm_x, bar, 0, h, t0, b);
-  }
 
-  // ---- per-token decay a_t and input weight w_t -------------------------
-  if (tid < Q) {
-    const int t = t0 + tid;
-    float a = 1.f, w = 0.f, l2 = 0.f;
-    if (t < p.L) {
-      if (MODE == kFwdLog2) {
-        l2 = p.dA[(static_cast<size_t>(b) * p.H + h) * p.L + t];
-        w = 1.f;
-      } else {
-        const float d = p.dt[(static_cast<size_t>(b) * p.L + t) * p.H + h];
-        l2 = d * p.A[h] * kLog2e;
-        w = d;
-      }
-      a = exp2f(l2);
-      if (SEQ && t > 0) {
-        const size_t i = static_cast<size_t>(b) * p.L + t;
-        if (load_seq_id(p.seq_idx, p.seq_idx_type, i) != load_seq_id(p.seq_idx, p.seq_idx_type, i - 1))
-          a = 0.f;
-      }
-    }
-    s_a[tid] = a;
-    s_w[tid] = w;
-    s_l2[tid] = l2;
-  }
-  // within-chunk cumsum of the log2 decay (reference outputs da_cs / da_cs_sum)
-  if (MODE == kFwdLog2 && (p.da_cs != nullptr || p.da_cs_sum != nullptr)) {
-    float v = (tid < Q) ? s_l2[tid] : 0.f;
-    // (s_l2 written by this same thread above)
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float n = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += n;
-    }
-    if (lane == 31) s_misc[warp] = v;
-    __syncthreads();
-    float pre = 0.f;
-    for (int k = 0; k < warp; ++k) pre += s_misc[k];
-    v += pre;
-    if (tid < Q && t0 + tid < p.L && p.da_cs != nullptr)
-      p.da_cs[(static_cast<size_t>(b) * p.H + h) * p.L + t0 + tid] = v;
-    if (tid == Q - 1 && p.da_cs_sum != nullptr)
-      p.da_cs_sum[(static_cast<size_t>(b) * p.H + h) * p.nc + c] = v;
-  }
-  __syncthreads();
-
-  mbar_wait_bounded(bar, 0, &ws.hdr[kHdrStatus]);
-
-  // ---- pass 1: per-segment end state from zero input, and segment decay ----
+  // ------------------------------ consumers -------------------------------
   const int s0 = warp * SEG;
   const int ch = lane * CPT;
-  {
-    float z[CPT];
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) z[k] = 0.f;
-    float D = 1.f;
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-      const float a = s_a[s0 + i], w = s_w[s0 + i];
-      float xv[CPT];
-      load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) z[k] = fmaf(a, z[k], w * xv[k]);
-      D *= a;
-    }
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) s_E[warp * BP + ch + k] = z[k];
-    if (lane == 0) s_D[warp] = D;
-  }
-  __syncthreads();
+  for (int k = 0;; ++k) {
+    const int s = k % S;
+    if (!mbar_wait_bounded(&full[s], (k / S) & 1, status)) break;
+    const int tile = s_tile[s];
+    if (tile < 0) break;
+    const int c = tile / BH, bh = tile % BH;
+    const int b = bh / p.H, h = bh % p.H, t0 = c * Q;
+    const size_t slot = static_cast<size_t>(tile);
+    T* s_x = reinterpret_cast<T*>(smem + s * C::kStage);
+    const float* raw = reinterpret_cast<const float*>(smem + s * C::kStage + C::kX);
 
-  // ---- chain the segments of this tile --------------------------------------
-  if (tid < BP) {
-    float Sv = 0.f, Gd = 1.f;
-#pragma unroll
-    for (int s = 0; s < NW; ++s) {
-      const float e = s_E[s * BP + tid];
-      s_E[s * BP + tid] = Sv;  // state before segment s (zero tile input)
-      if (tid == 0) s_G0[s] = Gd;
-      Sv = fmaf(s_D[s], Sv, e);
-      Gd *= s_D[s];
+    // ---- per-token decay a_t and input weight w_t ---------------------------
+    if (tid < Q) {
+      const int t = t0 + tid;
+      float a = 1.f, w = 0.f, l2 = 0.f;
+      if (t < p.L) {
+        if (MODE == kFwdLog2) {
+          l2 = raw[tid];
+          w = 1.f;
+        } else {
+          const float d = raw[tid];
+          l2 = d * raw[Q] * kLog2e;
+          w = d;
+        }
+        a = exp2f(l2);
+        if (SEQ && t > 0) {
+          const size_t i = static_cast<size_t>(b) * p.L + t;
+          if (load_seq_id(p.seq_idx, p.seq_idx_type, i) != load_seq_id(p.seq_idx, p.seq_idx_type, i - 1))
+            a = 0.f;
+        }
+      }
+      s_a[tid] = a;
+      s_w[tid] = w;
+      s_l2[tid] = l2;
     }
-    s_Et[tid] = Sv;
-    if (tid == 0) s_misc[0] = Gd;
-  }
-  __syncthreads();
-  const float Dtile = s_misc[0];
-  const bool has_succ = (c + 1 < p.nc);
-  if (c > 0 && has_succ) publish_cta<BP>(ws, slot, 0, s_Et, Dtile, (epoch << 2) | kFlagAgg, tid);
+    if (MODE == kFwdLog2 && (p.da_cs != nullptr || p.da_cs_sum != nullptr)) {
+      // within-chunk cumsum of the log2 decay (reference outputs da_cs / da_cs_sum)
+      float v = (tid < Q) ? s_l2[tid] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (lane == 31) s_misc[warp] = v;
+      named_sync(1, NC);
+      float pre = 0.f;
+      for (int w = 0; w < warp; ++w) pre += s_misc[w];
+      v += pre;
+      if (tid < Q && t0 + tid < p.L && p.da_cs != nullptr)
+        p.da_cs[(static_cast<size_t>(b) * p.H + h) * p.L + t0 + tid] = v;
+      if (tid == Q - 1 && p.da_cs_sum != nullptr)
+        p.da_cs_sum[(static_cast<size_t>(b) * p.H + h) * p.nc + c] = v;
+    }
+    named_sync(1, NC);
 
-  // ---- look-back for the state entering this tile ---------------------------
-  if (warp == 0) {
-    float run[CPT], rdec = 1.f;
-    bool at_start = true;
-    if (c > 0) {
-      at_start = lookback_warp<BP>(ws, epoch, bh, BH, c, -1, p.nc, lane, run, rdec);
-    } else {
+    // ---- pass 1: per-segment end state from zero input, and segment decay ---
+    {
+      float z[CPT];
 #pragma unroll
-      for (int k = 0; k < CPT; ++k) run[k] = 0.f;
+      for (int q = 0; q < CPT; ++q) z[q] = 0.f;
+      float D = 1.f;
+#pragma unroll
+      for (int i = 0; i < SEG; ++i) {
+        const float a = s_a[s0 + i], w = s_w[s0 + i];
+        float xv[CPT];
+        load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) z[q] = fmaf(a, z[q], w * xv[q]);
+        D *= a;
+      }
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) s_E[warp * BP + ch + q] = z[q];
+      if (lane == 0) s_D[warp] = D;
     }
-    if (at_start && p.init != nullptr) {
-      const float* iv = p.init + (static_cast<size_t>(b) * p.H + h) * p.P;
+    named_sync(1, NC);
+
+    // ---- chain the segments; publish the tile aggregate ---------------------
+    const bool has_succ = (c + 1 < p.nc);
+    if (tid < BP) {
+      float Sv = 0.f, Gd = 1.f;
 #pragma unroll
-      for (int k = 0; k < CPT; ++k)
-        if (ch + k < p.P) run[k] = fmaf(rdec, iv[ch + k], run[k]);
+      for (int q = 0; q < NW; ++q) {
+        const float e = s_E[q * BP + tid];
+        s_E[q * BP + tid] = Sv;  // state before segment q (zero tile input)
+        if (tid == 0) s_G0[q] = Gd;
+        Sv = fmaf(s_D[q], Sv, e);
+        Gd *= s_D[q];
+      }
+      s_Et[tid] = Sv;
+      if (tid == 0) s_misc[0] = Gd;
+      if (c > 0 && has_succ) {
+        uint64_t* agg = ws.agg + slot * (BP + 1);
+        st_relaxed_u64(agg + tid, tag_word(Sv, tag));
+        if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Gd, tag));
+      }
     }
+    named_sync(1, NC);
+    const float Dtile = s_misc[0];
+
+    // ---- look-back for the state entering this tile -------------------------
+    if (warp == 0) {
+      float run[CPT], rdec = 1.f;
+      bool at_start = true;
+      if (c > 0) {
+        at_start = lookback_warp<BP>(ws, tag, bh, BH, c, -1, p.nc, lane, run, rdec);
+      } else {
 #pragma unroll
-    for (int k = 0; k < CPT; ++k) {
-      s_Sin[ch + k] = run[k];
-      run[k] = fmaf(Dtile, run[k], s_Et[ch + k]);  // inclusive (state at the tile end)
+        for (int q = 0; q < CPT; ++q) run[q] = 0.f;
+      }
+      if (at_start && p.init != nullptr) {
+        const float* iv = p.init + (static_cast<size_t>(b) * p.H + h) * p.P;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
+          if (ch + q < p.P) run[q] = fmaf(rdec, iv[ch + q], run[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        s_Sin[ch + q] = run[q];
+        run[q] = fmaf(Dtile, run[q], s_Et[ch + q]);  // inclusive: state at the tile end
+      }
+      if (has_succ) {
+        uint64_t* inc = ws.incl + slot * BP + ch;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) st_relaxed_u64(inc + q, tag_word(run[q], tag));
+      } else if (p.final_state != nullptr) {
+        float* fo = p.final_state + (static_cast<size_t>(b) * p.H + h) * p.P;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
+          if (ch + q < p.P) fo[ch + q] = run[q];
+      }
     }
-    if (has_succ) {
+    named_sync(1, NC);
+
+    if (p.states != nullptr && tid < p.P)
+      p.states[b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h + tid * p.st_p] = s_Sin[tid];
+
+    // ---- pass 2: exact outputs, written over the x tile ---------------------
+    {
+      const float g0 = s_G0[warp];
+      float z[CPT];
 #pragma unroll
-      for (int k = 0; k < CPT; ++k) ws.vals[slot * (2 * BP) + BP + ch + k] = run[k];
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release_gpu(&ws.flags[slot], (epoch << 2) | kFlagIncl);
-    } else if (p.final_state != nullptr) {
-      float* fo = p.final_state + (static_cast<size_t>(b) * p.H + h) * p.P;
+      for (int q = 0; q < CPT; ++q) z[q] = fmaf(g0, s_Sin[ch + q], s_E[warp * BP + ch + q]);
 #pragma unroll
-      for (int k = 0; k < CPT; ++k)
-        if (ch + k < p.P) fo[ch + k] = run[k];
+      for (int i = 0; i < SEG; ++i) {
+        const float a = s_a[s0 + i], w = s_w[s0 + i];
+        T* px = s_x + (s0 + i) * BP + ch;
+        float xv[CPT];
+        load_pack<T, CPT>(px, xv);
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) z[q] = fmaf(a, z[q], w * xv[q]);
+        store_pack<T, CPT>(px, z);
+      }
+    }
+    fence_proxy_async_smem();
+    named_sync(1, NC);
+    if (tid == 0) {
+      tma_store_4d(&tm_y, s_x, 0, h, t0, b);
+      bulk_commit();
+      release_stage<S, C::R::DEFERRED>(empty, k);
     }
   }
-  __syncthreads();
-
-  if (p.states != nullptr && tid < p.P)
-    p.states[b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h + tid * p.st_p] = s_Sin[tid];
-
-  // ---- pass 2: exact outputs, written over the x tile -----------------------
-  {
-    const float g0 = s_G0[warp];
-    float z[CPT];
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) z[k] = fmaf(g0, s_Sin[ch + k], s_E[warp * BP + ch + k]);
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-      const float a = s_a[s0 + i], w = s_w[s0 + i];
-      T* px = s_x + (s0 + i) * BP + ch;
-      float xv[CPT];
-      load_pack<T, CPT>(px, xv);
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) z[k] = fmaf(a, z[k], w * xv[k]);
-      store_pack<T, CPT>(px, z);
-    }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
   if (tid == 0) {
-    tma_store_4d(&tm_y, s_x, 0, h, t0, b);
-    bulk_commit();
-    bulk_wait_read_all();
+    bulk_wait_all();
+    if (count_cta_done(ws)) reset_counters(ws, epoch, total);
   }
-  if (finish_cta(ws, epoch, tid, &s_last) && tid == 0) reset_counters(ws, epoch);
 }
 
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
-struct BwdSmem {
-  using G = ScanGeo<BP, Q>;
-  static constexpr int kXBytes = Q * BP * static_cast<int>(sizeof(T));
-  static constexpr int kX = 0;
-  static constexpr int kDy = kXBytes;
-  static constexpr int kA = 2 * kXBytes;          // float[Q]
-  static constexpr int kW = kA + Q * 4;           // float[Q]
-  static constexpr int kE = kW + Q * 4;           // float[NW][BP]  forward prefix -> Zin
-  static constexpr int kR = kE + G::NW * BP * 4;  // float[NW][BP]  reverse aggregate -> Rloc
-  static constexpr int kD = kR + G::NW * BP * 4;  // float[NW]
-  static constexpr int kHs = kD + G::NW * 4;      // float[NW]
-  static constexpr int kSin = kHs + G::NW * 4;    // float[BP]
-  static constexpr int kGn = kSin + BP * 4;       // float[BP]
-  static constexpr int kRt = kGn + BP * 4;        // float[BP]
-  static constexpr int kMisc = kRt + BP * 4;      // float[32]
-  static constexpr int kCk = kMisc + 32 * 4;      // float[NW][SEG/RB][BP] recompute checkpoints
-  static constexpr int kBar = (kCk + G::NW * (G::SEG / G::RB) * BP * 4 + 15) / 16 * 16;
-  static constexpr int kBytes = kBar + 16;
+struct BwdCfg {
+  static constexpr int CPT = BP / 32;
+  static constexpr int SEG = 16;  // tokens per warp segment
+  static constexpr int RB = 8;    // reverse recompute block
+  static constexpr int NB = SEG / RB;
+  static constexpr int NW = Q / SEG;
+  static constexpr int NC = NW * 32;
+  static constexpr int NT = NC + 32;
+  static_assert(BP % 32 == 0 && BP <= 128 && Q % SEG == 0 && NC >= Q && NC >= BP && NT <= 1024, "geometry");
+  static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
+  // stage: x tile | dy tile | decay row [Q] | A_h [4] | chunk start state [BP]
+  static constexpr int oRaw = 2 * kX;
+  static constexpr int oSt = oRaw + (Q + 4) * 4;
+  static constexpr int kStage = align_up(oSt + BP * 4, 128);
+  static constexpr int oA = 0;                 // float[Q]
+  static constexpr int oW = oA + Q * 4;        // float[Q]
+  static constexpr int oE = oW + Q * 4;        // float[NW][BP]  forward prefix -> Zin
+  static constexpr int oR = oE + NW * BP * 4;  // float[NW][BP]  reverse aggregate -> Rloc
+  static constexpr int oD = oR + NW * BP * 4;  // float[NW]
+  static constexpr int oHs = oD + NW * 4;      // float[NW]
+  static constexpr int oGn = oHs + NW * 4;     // float[BP]
+  static constexpr int oRt = oGn + BP * 4;     // float[BP]
+  static constexpr int oMisc = oRt + BP * 4;   // float[48]
+  static constexpr int oCk = oMisc + 48 * 4;   // float[NW][NB][BP] recompute checkpoints
+  static constexpr int oTile = oCk + NW * NB * BP * 4;
+  static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);
+  static constexpr int kPriv = oBar + 2 * kMaxStages * 8;
+  using R = Ring<kStage, kPriv>;
+  static constexpr int S = R::S;
+  static constexpr int CTAS = R::CTAS;
+  static constexpr int kPrivBase = S * kStage;
+  static constexpr int kBytes = kPrivBase + kPriv;
 };
 
 template <typename T, int BP, int Q, int MODE>
-__global__ void __launch_bounds__(ScanGeo<BP, Q>::NT, ScanGeo<BP, Q>::BWD_MIN_BLOCKS)
+__global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     ema_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_dy,
                    const __grid_constant__ CUtensorMap tm_dx, const BwdParams p) {
-  using G = ScanGeo<BP, Q>;
-  using S = BwdSmem<T, BP, Q>;
-  constexpr int CPT = G::CPT, SEG = G::SEG, NW = G::NW, RB = G::RB, NB = SEG / RB;
-  static_assert(SEG % RB == 0, "recompute block");
+  using C = BwdCfg<T, BP, Q>;
+  constexpr int CPT = C::CPT, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S, RB = C::RB, NB = C::NB;
   extern __shared__ __align__(128) unsigned char smem[];
-  T* s_x = reinterpret_cast<T*>(smem + S::kX);
-  T* s_dy = reinterpret_cast<T*>(smem + S::kDy);
-  float* s_a = reinterpret_cast<float*>(smem + S::kA);
-  float* s_w = reinterpret_cast<float*>(smem + S::kW);
-  float* s_E = reinterpret_cast<float*>(smem + S::kE);
-  float* s_R = reinterpret_cast<float*>(smem + S::kR);
-  float* s_D = reinterpret_cast<float*>(smem + S::kD);
-  float* s_Hs = reinterpret_cast<float*>(smem + S::kHs);
-  float* s_Sin = reinterpret_cast<float*>(smem + S::kSin);
-  float* s_Gn = reinterpret_cast<float*>(smem + S::kGn);
-  float* s_Rt = reinterpret_cast<float*>(smem + S::kRt);
-  float* s_misc = reinterpret_cast<float*>(smem + S::kMisc);
-  float* s_ck = reinterpret_cast<float*>(smem + S::kCk);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  __shared__ uint32_t s_tile, s_epoch, s_last;
+  unsigned char* priv = smem + C::kPrivBase;
+  float* s_a = reinterpret_cast<float*>(priv + C::oA);
+  float* s_w = reinterpret_cast<float*>(priv + C::oW);
+  float* s_E = reinterpret_cast<float*>(priv + C::oE);
+  float* s_R = reinterpret_cast<float*>(priv + C::oR);
+  float* s_D = reinterpret_cast<float*>(priv + C::oD);
+  float* s_Hs = reinterpret_cast<float*>(priv + C::oHs);
+  float* s_Gn = reinterpret_cast<float*>(priv + C::oGn);
+  float* s_Rt = reinterpret_cast<float*>(priv + C::oRt);
+  float* s_misc = reinterpret_cast<float*>(priv + C::oMisc);
+  float* s_ck = reinterpret_cast<float*>(priv + C::oCk);
+  int* s_tile = reinterpret_cast<int*>(priv + C::oTile);
+  uint64_t* full = reinterpret_cast<uint64_t*>(priv + C::oBar);
+  uint64_t* empty = full + kMaxStages;
+  __shared__ uint32_t s_epoch, s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const ScanWorkspace& ws = p.ws;
+  uint32_t* status = &ws.hdr[kHdrStatus];
   if (tid == 0) {
-    tma_prefetch_desc(&tm_x);
-    tma_prefetch_desc(&tm_dy);
-    s_tile = atomicAdd(&ws.hdr[kHdrTicket], 1u);
     s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
-    mbar_init(bar, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 33);
+      mbar_init(&empty[s], 1);
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  if (s_tile >= gridDim.x) {  // counters not reset: workspace shared by overlapping launches
-    if (tid == 0) atomicOr(&ws.hdr[kHdrStatus], kStatusBadTicket);
+  const uint32_t epoch = s_epoch;
+  const uint32_t tag = epoch + 1u;
+  const int BH = p.B * p.H;
+  const int total = BH * p.nc;
+
+  if (warp == NW) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_dy);
+    }
+    for (int k = 0;; ++k) {
+      const int s = k % S;
+      if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status)) break;
+      uint32_t ticket = 0;
+      if (lane == 0) ticket = atomicAdd(&ws.hdr[kHdrTicket], 1u);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket >= static_cast<uint32_t>(total)) {
+        post_sentinel(&full[s], &s_tile[s], lane);
+        break;
+      }
+      const int c = p.nc - 1 - static_cast<int>(ticket) / BH, bh = static_cast<int>(ticket) % BH;
+      const int b = bh / p.H, h = bh % p.H, t0 = c * Q;
+      unsigned char* st = smem + s * C::kStage;
+      float* raw = reinterpret_cast<float*>(st + C::oRaw);
+      float* sst = reinterpret_cast<float*>(st + C::oSt);
+      if (lane == 0) {
+        s_tile[s] = c * BH + bh;
+        mbar_arrive_expect_tx(&full[s], 2 * C::kX);
+        tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
+        tma_load_4d(st + C::kX, &tm_dy, &full[s], 0, h, t0, b);
+      }
+      for (int i = lane; i < Q; i += 32) {
+        const int t = t0 + i;
+        if (t < p.L) {
+          if (MODE == kBwdCumsum)
+            cp_async_4(raw + i, p.da_cs + (static_cast<size_t>(b) * p.H + h) * p.L + t);
+          else
+            cp_async_4(raw + i, p.dt + (static_cast<size_t>(b) * p.L + t) * p.H + h);
+        }
+      }
+      if (MODE == kBwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
+      for (int i = lane; i < p.P; i += 32)
+        cp_async_4(sst + i, p.states + b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h +
+                                i * p.st_p);
+      cp_async_mbar_arrive_noinc(&full[s]);
+    }
+    cp_async_wait_all();
     return;
   }
-  const uint32_t epoch = s_epoch;
-  const int BH = p.B * p.H;
-  const int c = p.nc - 1 - static_cast<int>(s_tile) / BH;
-  const int bh = static_cast<int>(s_tile) % BH;
-  const int b = bh / p.H, h = bh % p.H;
-  const int t0 = c * Q;
-  const size_t slot = static_cast<size_t>(c) * BH + bh;
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar, 2 * S::kXBytes);
-    tma_load_4d(s_x, &tm_x, bar, 0, h, t0, b);
-    tma_load_4d(s_dy, &tm_dy, bar, 0, h, t0, b);
-  }
 
-  // ---- per-token decay / weight; chunk start state ---------------------------
-  float Ah = 0.f;
-  if (MODE == kBwdDt) Ah = p.A[h];
-  if (tid < Q) {
-    const int t = t0 + tid;
-    float a = 1.f, w = 0.f;
-    if (t < p.L) {
-      if (MODE == kBwdCumsum) {
-        const float* cs = p.da_cs + (static_cast<size_t>(b) * p.H + h) * p.L;
-        const float prev = (tid == 0) ? 0.f : cs[t - 1];
-        a = exp2f(cs[t] - prev);
-        w = 1.f;
-      } else {
-        const float d = p.dt[(static_cast<size_t>(b) * p.L + t) * p.H + h];
-        a = exp2f(d * Ah * kLog2e);
-        w = d;
-      }
-    }
-    s_a[tid] = a;
-    s_w[tid] = w;
-  }
-  if (tid < BP) {
-    s_Sin[tid] = (tid < p.P) ? p.states[b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h +
-                                        tid * p.st_p]
-                             : 0.f;
-  }
-  __syncthreads();
-  mbar_wait_bounded(bar, 0, &ws.hdr[kHdrStatus]);
-
+  // ------------------------------ consumers -------------------------------
   const int s0 = warp * SEG;
   const int ch = lane * CPT;
-  // ---- pass 1: forward end state (zero input) and reverse aggregate ---------
-  {
-    float z[CPT], g[CPT];
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) z[k] = g[k] = 0.f;
-    float D = 1.f;
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-      const float a = s_a[s0 + i], w = s_w[s0 + i];
-      float xv[CPT];
-      load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) z[k] = fmaf(a, z[k], w * xv[k]);
-      D *= a;
-      const int r = SEG - 1 - i;
-      const float ar = s_a[s0 + r];
-      float dv[CPT];
-      load_pack<T, CPT>(s_dy + (s0 + r) * BP + ch, dv);
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) g[k] = ar * (dv[k] + g[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) {
-      s_E[warp * BP + ch + k] = z[k];
-      s_R[warp * BP + ch + k] = g[k];
-    }
-    if (lane == 0) s_D[warp] = D;
-  }
-  __syncthreads();
+  for (int k = 0;; ++k) {
+    const int s = k % S;
+    if (!mbar_wait_bounded(&full[s], (k / S) & 1, status)) break;
+    const int tile = s_tile[s];
+    if (tile < 0) break;
+    const int c = tile / BH, bh = tile % BH;
+    const int b = bh / p.H, h = bh % p.H, t0 = c * Q;
+    const size_t slot = static_cast<size_t>(tile);
+    unsigned char* st = smem + s * C::kStage;
+    const T* s_x = reinterpret_cast<const T*>(st);
+    T* s_dy = reinterpret_cast<T*>(st + C::kX);
+    const float* raw = reinterpret_cast<const float*>(st + C::oRaw);
+    const float* s_Sin = reinterpret_cast<const float*>(st + C::oSt);
+    const float Ah = (MODE == kBwdDt) ? raw[Q] : 0.f;
 
-  // ---- chain segments: Zin (forward) and Rloc (reverse) ---------------------
-  if (tid < BP) {
-    float Sv = s_Sin[tid];
-#pragma unroll
-    for (int s = 0; s < NW; ++s) {
-      const float e = s_E[s * BP + tid];
-      s_E[s * BP + tid] = Sv;  // true state before segment s
-      Sv = fmaf(s_D[s], Sv, e);
+    // ---- per-token decay / weight ------------------------------------------
+    if (tid < Q) {
+      const int t = t0 + tid;
+      float a = 1.f, w = 0.f;
+      if (t < p.L) {
+        if (MODE == kBwdCumsum) {
+          const float prev = (tid == 0) ? 0.f : raw[tid - 1];
+          a = exp2f(raw[tid] - prev);
+          w = 1.f;
+        } else {
+          const float d = raw[tid];
+          a = exp2f(d * Ah * kLog2e);
+          w = d;
+        }
+      }
+      s_a[tid] = a;
+      s_w[tid] = w;
     }
-    float r = 0.f, Hd = 1.f;
-#pragma unroll
-    for (int s = NW - 1; s >= 0; --s) {
-      const float rr = s_R[s * BP + tid];
-      s_R[s * BP + tid] = r;  // gradient w.r.t. z at segment end, from later segments of this tile
-      if (tid == 0) s_Hs[s] = Hd;
-      r = fmaf(s_D[s], r, rr);
-      Hd *= s_D[s];
-    }
-    s_Rt[tid] = r;  // gradient w.r.t. the state entering the tile, from this tile's dy
-    if (tid == 0) s_misc[0] = Hd;
-  }
-  __syncthreads();
-  const float Dtile = s_misc[0];
-  const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
-  if (c + 1 < p.nc && has_succ) publish_cta<BP>(ws, slot, 0, s_Rt, Dtile, (epoch << 2) | kFlagAgg, tid);
+    named_sync(1, NC);
 
-  // ---- look-back: gradient arriving at the tile end from later chunks -------
-  if (warp == 0) {
-    float run[CPT], rdec = 1.f;
-    bool at_end = true;
-    if (c + 1 < p.nc) {
-      at_end = lookback_warp<BP>(ws, epoch, bh, BH, c, +1, p.nc, lane, run, rdec);
-    } else {
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) run[k] = 0.f;
-    }
-    if (at_end && p.d_final != nullptr) {
-      const float* dv = p.d_final + (static_cast<size_t>(b) * p.H + h) * p.P;
-#pragma unroll
-      for (int k = 0; k < CPT; ++k)
-        if (ch + k < p.P) run[k] = fmaf(rdec, dv[ch + k], run[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) {
-      s_Gn[ch + k] = run[k];
-      run[k] = fmaf(Dtile, run[k], s_Rt[ch + k]);  // gradient w.r.t. the state before the tile
-    }
-    if (has_succ) {
-#pragma unroll
-      for (int k = 0; k < CPT; ++k) ws.vals[slot * (2 * BP) + BP + ch + k] = run[k];
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) st_release_gpu(&ws.flags[slot], (epoch << 2) | kFlagIncl);
-    } else if (p.d_init != nullptr) {
-      float* di = p.d_init + (static_cast<size_t>(b) * p.H + h) * p.P;
-#pragma unroll
-      for (int k = 0; k < CPT; ++k)
-        if (ch + k < p.P) di[ch + k] = run[k];
-    }
-  }
-  __syncthreads();
-
-  // ---- pass 2: exact gradients -----------------------------------------------
-  float dap = 0.f;  // dt-form: sum_t dt_t * dl_t over this lane's tokens
-  {
-    float g[CPT];
-    const float hs = s_Hs[warp];
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) g[k] = fmaf(hs, s_Gn[ch + k], s_R[warp * BP + ch + k]);
-    // forward recompute of the segment; the state entering every RB-token
-    // block is kept (per thread) in shared memory for the reverse sweep
-    float* ck = s_ck + warp * NB * BP + ch;
+    // ---- pass 1: forward end state (zero input) and reverse aggregate -------
     {
-      float z[CPT];
+      float z[CPT], g[CPT];
 #pragma unroll
-      for (int k = 0; k < CPT; ++k) z[k] = s_E[warp * BP + ch + k];
+      for (int q = 0; q < CPT; ++q) z[q] = g[q] = 0.f;
+      float D = 1.f;
 #pragma unroll
       for (int i = 0; i < SEG; ++i) {
-        if (i % RB == 0) {
-#pragma unroll
-          for (int k = 0; k < CPT; ++k) ck[(i / RB) * BP + k] = z[k];
-        }
         const float a = s_a[s0 + i], w = s_w[s0 + i];
         float xv[CPT];
         load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) z[k] = fmaf(a, z[k], w * xv[k]);
+        for (int q = 0; q < CPT; ++q) z[q] = fmaf(a, z[q], w * xv[q]);
+        D *= a;
+        const int r = SEG - 1 - i;
+        const float ar = s_a[s0 + r];
+        float dv[CPT];
+        load_pack<T, CPT>(s_dy + (s0 + r) * BP + ch, dv);
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) g[q] = ar * (dv[q] + g[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        s_E[warp * BP + ch + q] = z[q];
+        s_R[warp * BP + ch + q] = g[q];
+      }
+      if (lane == 0) s_D[warp] = D;
+    }
+    named_sync(1, NC);
+
+    // ---- chain segments: Zin (forward) and Rloc (reverse); publish ----------
+    const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
+    if (tid < BP) {
+      float Sv = (tid < p.P) ? s_Sin[tid] : 0.f;
+#pragma unroll
+      for (int q = 0; q < NW; ++q) {
+        const float e = s_E[q * BP + tid];
+        s_E[q * BP + tid] = Sv;  // true state before segment q
+        Sv = fmaf(s_D[q], Sv, e);
+      }
+      float r = 0.f, Hd = 1.f;
+#pragma unroll
+      for (int q = NW - 1; q >= 0; --q) {
+        const float rr = s_R[q * BP + tid];
+        s_R[q * BP + tid] = r;  // gradient w.r.t. z at the segment end, from later segments
+        if (tid == 0) s_Hs[q] = Hd;
+        r = fmaf(s_D[q], r, rr);
+        Hd *= s_D[q];
+      }
+      s_Rt[tid] = r;  // gradient w.r.t. the state entering the tile, from this tile's dy
+      if (tid == 0) s_misc[0] = Hd;
+      if (c + 1 < p.nc && has_succ) {
+        uint64_t* agg = ws.agg + slot * (BP + 1);
+        st_relaxed_u64(agg + tid, tag_word(r, tag));
+        if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Hd, tag));
       }
     }
-    const bool last_tile = (t0 + Q >= p.L);
-    const float* dlast = (p.d_last != nullptr && last_tile)
-                             ? p.d_last + (static_cast<size_t>(b) * p.H + h) * p.P
-                             : nullptr;
-#pragma unroll 1
-    for (int blk = NB - 1; blk >= 0; --blk) {
-      float zz[RB][CPT];
+    named_sync(1, NC);
+    const float Dtile = s_misc[0];
+
+    // ---- look-back: gradient arriving at the tile end from later chunks ------
+    if (warp == 0) {
+      float run[CPT], rdec = 1.f;
+      bool at_end = true;
+      if (c + 1 < p.nc) {
+        at_end = lookback_warp<BP>(ws, tag, bh, BH, c, +1, p.nc, lane, run, rdec);
+      } else {
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) run[q] = 0.f;
+      }
+      if (at_end && p.d_final != nullptr) {
+        const float* dv = p.d_final + (static_cast<size_t>(b) * p.H + h) * p.P;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
+          if (ch + q < p.P) run[q] = fmaf(rdec, dv[ch + q], run[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        s_Gn[ch + q] = run[q];
+        run[q] = fmaf(Dtile, run[q], s_Rt[ch + q]);  // gradient w.r.t. the state before the tile
+      }
+      if (has_succ) {
+        uint64_t* inc = ws.incl + slot * BP + ch;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) st_relaxed_u64(inc + q, tag_word(run[q], tag));
+      } else if (p.d_init != nullptr) {
+        float* di = p.d_init + (static_cast<size_t>(b) * p.H + h) * p.P;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
+          if (ch + q < p.P) di[ch + q] = run[q];
+      }
+    }
+    named_sync(1, NC);
+
+    // ---- pass 2: exact gradients ---------------------------------------------
+    float dap = 0.f;  // dt form: sum over this lane's tokens of dt * dl
+    {
+      float g[CPT];
+      const float hs = s_Hs[warp];
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) g[q] = fmaf(hs, s_Gn[ch + q], s_R[warp * BP + ch + q]);
+      // forward recompute of the segment; the state entering every RB-token
+      // block is kept (per thread) in shared memory for the reverse sweep
+      float* ck = s_ck + warp * NB * BP + ch;
       {
         float z[CPT];
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) z[k] = ck[blk * BP + k];
+        for (int q = 0; q < CPT; ++q) z[q] = s_E[warp * BP + ch + q];
 #pragma unroll
-        for (int j = 0; j < RB; ++j) {
+        for (int i = 0; i < SEG; ++i) {
+          if (i % RB == 0) {
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) ck[(i / RB) * BP + q] = z[q];
+          }
+          const float a = s_a[s0 + i], w = s_w[s0 + i];
+          float xv[CPT];
+          load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
+#pragma unroll
+          for (int q = 0; q < CPT; ++q) z[q] = fmaf(a, z[q], w * xv[q]);
+        }
+      }
+      const float* dlast = (p.d_last != nullptr && t0 + Q >= p.L)
+                               ? p.d_last + (static_cast<size_t>(b) * p.H + h) * p.P
+                               : nullptr;
+#pragma unroll 1
+      for (int blk = NB - 1; blk >= 0; --blk) {
+        float zz[RB][CPT];
+        {
+          float z[CPT];
+#pragma unroll
+          for (int q = 0; q < CPT; ++q) z[q] = ck[blk * BP + q];
+#pragma unroll
+          for (int j = 0; j < RB; ++j) {
+            const int t = s0 + blk * RB + j;
+            const float a = s_a[t], w = s_w[t];
+            float xv[CPT];
+            load_pack<T, CPT>(s_x + t * BP + ch, xv);
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) {
+              zz[j][q] = z[q];
+              z[q] = fmaf(a, z[q], w * xv[q]);
+            }
+          }
+        }
+        float p1[RB], p2[RB];
+#pragma unroll
+        for (int j = RB - 1; j >= 0; --j) {
           const int t = s0 + blk * RB + j;
           const float a = s_a[t], w = s_w[t];
-          float xv[CPT];
-          load_pack<T, CPT>(s_x + t * BP + ch, xv);
+          float dv[CPT];
+          T* pd = s_dy + t * BP + ch;
+          load_pack<T, CPT>(pd, dv);
+          float Gv[CPT], dxv[CPT];
 #pragma unroll
-          for (int k = 0; k < CPT; ++k) {
-            zz[j][k] = z[k];
-            z[k] = fmaf(a, z[k], w * xv[k]);
+          for (int q = 0; q < CPT; ++q) {
+            Gv[q] = dv[q] + g[q];
+            dxv[q] = w * Gv[q];
           }
-        }
-      }
-      float p1[RB], p2[RB];
+          if (dlast != nullptr && t0 + t == p.L - 1) {
 #pragma unroll
-      for (int j = RB - 1; j >= 0; --j) {
-        const int t = s0 + blk * RB + j;
-        const float a = s_a[t], w = s_w[t];
-        float dv[CPT];
-        T* pd = s_dy + t * BP + ch;
-        load_pack<T, CPT>(pd, dv);
-        float Gv[CPT], dxv[CPT];
+            for (int q = 0; q < CPT; ++q)
+              if (ch + q < p.P) dxv[q] += dlast[ch + q];
+          }
+          store_pack<T, CPT>(pd, dxv);
+          float q1 = 0.f, q2 = 0.f;
+          if (MODE == kBwdDt) {
+            float xv[CPT];
+            load_pack<T, CPT>(s_x + t * BP + ch, xv);
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) {
-          Gv[k] = dv[k] + g[k];
-          dxv[k] = w * Gv[k];
-        }
-        if (dlast != nullptr && t0 + t == p.L - 1) {
+            for (int q = 0; q < CPT; ++q) q2 = fmaf(Gv[q], xv[q], q2);
+          }
 #pragma unroll
-          for (int k = 0; k < CPT; ++k)
-            if (ch + k < p.P) dxv[k] += dlast[ch + k];
+          for (int q = 0; q < CPT; ++q) {
+            q1 = fmaf(Gv[q], zz[j][q], q1);
+            g[q] = a * Gv[q];
+          }
+          p1[j] = a * q1;
+          p2[j] = q2;
         }
-        store_pack<T, CPT>(pd, dxv);
-        float q1 = 0.f, q2 = 0.f;
-        if (MODE == kBwdDt) {
-          float xv[CPT];
-          load_pack<T, CPT>(s_x + t * BP + ch, xv);
-#pragma unroll
-          for (int k = 0; k < CPT; ++k) q2 = fmaf(Gv[k], xv[k], q2);
-        }
-#pragma unroll
-        for (int k = 0; k < CPT; ++k) {
-          q1 = fmaf(Gv[k], zz[j][k], q1);
-          g[k] = a * Gv[k];
-        }
-        p1[j] = a * q1;
-        p2[j] = q2;
-      }
-      const float P1 = transpose_reduce8(p1, lane);
-      float P2 = 0.f;
-      if (MODE == kBwdDt) P2 = transpose_reduce8(p2, lane);
-      if ((lane & 3) == 0) {
-        const int t = s0 + blk * RB + (lane >> 2);
-        const int gt = t0 + t;
-        if (gt < p.L) {
-          if (MODE == kBwdCumsum) {
-            p.dl[(static_cast<size_t>(b) * p.H + h) * p.L + gt] = P1;
-          } else {
-            p.ddt[(static_cast<size_t>(b) * p.L + gt) * p.H + h] = fmaf(Ah, P1, P2);
-            dap = fmaf(s_w[t], P1, dap);
+        const float P1 = transpose_reduce8(p1, lane);
+        float P2 = 0.f;
+        if (MODE == kBwdDt) P2 = transpose_reduce8(p2, lane);
+        if ((lane & 3) == 0) {
+          const int t = s0 + blk * RB + (lane >> 2);
+          const int gt = t0 + t;
+          if (gt < p.L) {
+            if (MODE == kBwdCumsum) {
+              p.dl[(static_cast<size_t>(b) * p.H + h) * p.L + gt] = P1;
+            } else {
+              p.ddt[(static_cast<size_t>(b) * p.L + gt) * p.H + h] = fmaf(Ah, P1, P2);
+              dap = fmaf(s_w[t], P1, dap);
+            }
           }
         }
       }
     }
-  }
 
-  // ---- dt-form: per-tile partial of dA (deterministic order) ----------------
-  if (MODE == kBwdDt) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(0xffffffffu, dap, o);
-    if (lane == 0) s_misc[1 + warp] = dap;
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    tma_store_4d(&tm_dx, s_dy, 0, h, t0, b);
-    bulk_commit();
+    // ---- dt form: per-tile partial of dA (fixed order) -------------------------
     if (MODE == kBwdDt) {
-      float tot = 0.f;
-      for (int w = 0; w < NW; ++w) tot += s_misc[1 + w];
-      ws.partial[slot] = tot;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(0xffffffffu, dap, o);
+      if (lane == 0) s_misc[1 + warp] = dap;
     }
-    bulk_wait_read_all();
+    fence_proxy_async_smem();
+    named_sync(1, NC);
+    if (tid == 0) {
+      tma_store_4d(&tm_dx, s_dy, 0, h, t0, b);
+      bulk_commit();
+      if (MODE == kBwdDt) {
+        float tot = 0.f;
+        for (int w = 0; w < NW; ++w) tot += s_misc[1 + w];
+        ws.partial[slot] = tot;
+      }
+      release_stage<S, C::R::DEFERRED>(empty, k);
+    }
   }
-  if (finish_cta(ws, epoch, tid, &s_last)) {
+  if (tid == 0) {
+    bulk_wait_all();
+    s_last = count_cta_done(ws) ? 1u : 0u;
+  }
+  named_sync(1, NC);
+  if (s_last) {
     if (MODE == kBwdDt) {
       __threadfence();
-      for (int hh = tid; hh < p.H; hh += G::NT) {
+      for (int hh = tid; hh < p.H; hh += NC) {
         float acc = 0.f;
         for (int cc = 0; cc < p.nc; ++cc)
           for (int bb = 0; bb < p.B; ++bb)
             acc += ld_relaxed_gpu(&ws.partial[static_cast<size_t>(cc) * BH + bb * p.H + hh]);
         p.dA_out[hh] = acc;
       }
-      __syncthreads();
+      named_sync(1, NC);
     }
-    if (tid == 0) reset_counters(ws, epoch);
+    if (tid == 0) reset_counters(ws, epoch, total);
   }
 }
 
