@@ -59,23 +59,30 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+// Test a phase; a thread whose phase is not complete is suspended in hardware
+// (issuing nothing) until it completes or about `hint_ns` pass.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase, uint32_t hint_ns = 1000000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 // Bounded wait on an mbarrier phase; returns false (and sets the status bit)
-// when the limit passes.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, uint32_t* status) {
+// when the limit passes.  Between polls the thread sleeps with exponential
+// backoff up to `max_sleep_ns`, so a waiting warp issues almost nothing.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, uint32_t* status,
+                                                  uint32_t max_sleep_ns = 256) {
   if (mbar_try_wait(bar, phase)) return true;
   const unsigned long long t0 = global_timer_ns();
+  uint32_t sleep = 16;
   while (!mbar_try_wait(bar, phase)) {
+    __nanosleep(sleep);
+    sleep = sleep < max_sleep_ns ? sleep * 2 : max_sleep_ns;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       atomicOr(status, kStatusTmaTimeout);
       return false;
@@ -116,6 +123,15 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One bulk (non-tensor) copy global -> shared, completing on `bar` by bytes.
+// Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst_smem)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---- cp.async (4-byte element gathers into shared memory) ----------------
@@ -212,6 +228,23 @@ __device__ __forceinline__ void load_pack(const T* p, float (&f)[N]) {
 #pragma unroll
   for (int k = 0; k < N; ++k) f[k] = to_f32(e[k]);
 }
+// Store N elements to global memory with the evict-first ("streaming") policy:
+// outputs are written once and not re-read by this path.  The __stcs
+// intrinsics (not inline asm) leave address arithmetic to the compiler.
+__device__ __forceinline__ void st_cs(uint16_t* p, uint16_t v) { __stcs(reinterpret_cast<unsigned short*>(p), v); }
+__device__ __forceinline__ void st_cs(uint32_t* p, uint32_t v) { __stcs(reinterpret_cast<unsigned int*>(p), v); }
+__device__ __forceinline__ void st_cs(uint2* p, uint2 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_cs(uint4* p, uint4 v) { __stcs(p, v); }
+template <typename T, int N>
+__device__ __forceinline__ void store_pack_global_cs(T* p, const float (&f)[N]) {
+  using R = typename RawVec<sizeof(T) * N>::type;
+  R r;
+  T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+  for (int k = 0; k < N; ++k) e[k] = from_f32<T>(f[k]);
+  st_cs(reinterpret_cast<R*>(p), r);
+}
+
 template <typename T, int N>
 __device__ __forceinline__ void store_pack(T* p, const float (&f)[N]) {
   using R = typename RawVec<sizeof(T) * N>::type;

@@ -13,7 +13,6 @@ namespace emab {
 
 struct FwdLaunch {
   const CUtensorMap* map_x;
-  const CUtensorMap* map_y;
   FwdParams params;
   int block_p, chunk, mode;
   bool seq;
@@ -25,7 +24,6 @@ struct FwdLaunch {
 struct BwdLaunch {
   const CUtensorMap* map_x;
   const CUtensorMap* map_dy;
-  const CUtensorMap* map_dx;
   BwdParams params;
   int block_p, chunk, mode;
   long long tiles;

@@ -49,6 +49,21 @@ CUtensorMapDataType map_dtype(int dtype) {
   }
 }
 
+// A (B, L, H, P) tensor written with vector stores: 16-byte aligned base and
+// strides that are multiples of 16 bytes (channel stride 1).
+int check_tile_tensor(const void* ptr, int dtype, const int64_t st[3], const char* name) {
+  const int es = elem_size(dtype);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "%s: base address must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i) {
+    if (st[i] <= 0 || (st[i] * es) % 16 != 0)
+      return fail(EMA_ERR_INVALID_ARGUMENT,
+                  "%s: stride %d (%lld elements) must be positive and a multiple of 16 bytes", name, i,
+                  static_cast<long long>(st[i]));
+  }
+  return EMA_OK;
+}
+
 // 4-D map over a (B, L, H, P) tensor with unit channel stride; box = one
 // (chunk, batch, head) tile of BP channels x Q tokens.
 int make_tile_map(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t L, int64_t H,
@@ -85,14 +100,16 @@ int block_p_for(int64_t P) {
 }
 
 // Workspace: 256-byte header | dA partials [tiles] f32 | aggregate records
-// [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64.
+// [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64 | two (B,H,L) f32
+// row buffers (dt-form: dt transposed to per-(batch, head) rows, and the ddt
+// rows the backward writes before they are transposed back).
 struct WsLayout {
-  size_t partial, agg, incl, total;
+  size_t partial, agg, incl, rows, rows2, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-WsLayout ws_layout(int64_t tiles, int BP) {
+WsLayout ws_layout(int64_t tiles, int BP, int64_t row_floats) {
   WsLayout l;
   size_t off = static_cast<size_t>(kHdrWords) * 4;
   l.partial = off;
@@ -101,15 +118,25 @@ WsLayout ws_layout(int64_t tiles, int BP) {
   off = align256(off + static_cast<size_t>(tiles) * (BP + 1) * 8);
   l.incl = off;
   off = align256(off + static_cast<size_t>(tiles) * BP * 8);
+  l.rows = off;
+  off = align256(off + static_cast<size_t>(row_floats) * 4);
+  l.rows2 = off;
+  off = align256(off + static_cast<size_t>(row_floats) * 4);
   l.total = off;
   return l;
 }
 
-int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace* out) {
+struct RowBuffers {
+  float* rows;
+  float* rows2;
+};
+
+int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, int64_t row_floats, ScanWorkspace* out,
+                    RowBuffers* rb) {
   if (ws == nullptr) return fail(EMA_ERR_WORKSPACE, "workspace is NULL");
   if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
     return fail(EMA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  const WsLayout l = ws_layout(tiles, BP);
+  const WsLayout l = ws_layout(tiles, BP, row_floats);
   if (bytes < l.total)
     return fail(EMA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", bytes, l.total);
   char* base = static_cast<char*>(ws);
@@ -117,6 +144,18 @@ int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace
   out->partial = reinterpret_cast<float*>(base + l.partial);
   out->agg = reinterpret_cast<uint64_t*>(base + l.agg);
   out->incl = reinterpret_cast<uint64_t*>(base + l.incl);
+  rb->rows = reinterpret_cast<float*>(base + l.rows);
+  rb->rows2 = reinterpret_cast<float*>(base + l.rows2);
+  return EMA_OK;
+}
+
+// (B, X, Y) -> (B, Y, X) float32, asynchronously on `s`.
+int launch_transpose(const float* src, float* dst, int64_t B, int64_t X, int64_t Y, cudaStream_t s) {
+  if (B > 65535) return fail(EMA_ERR_UNSUPPORTED, "transpose: batch too large");
+  dim3 grid(static_cast<unsigned>((X + 31) / 32), static_cast<unsigned>((Y + 31) / 32), static_cast<unsigned>(B));
+  transpose_f32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, dst, static_cast<int>(X), static_cast<int>(Y));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "transpose launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
 }
 
@@ -189,7 +228,7 @@ size_t ema_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, in
   if (batch <= 0 || seqlen <= 0 || nheads <= 0 || headdim <= 0 || chunk_size <= 0) return 256;
   const int BP = block_p_for(headdim) ? block_p_for(headdim) : 128;
   const int64_t nc = (seqlen + chunk_size - 1) / chunk_size;
-  return ws_layout(batch * nheads * nc, BP).total;
+  return ws_layout(batch * nheads * nc, BP, batch * nheads * seqlen).total;
 }
 
 int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
@@ -216,21 +255,22 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
 
   FwdLaunch l{};
   FwdParams& p = l.params;
-  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
+  RowBuffers rb;
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, a->batch * a->nheads * a->seqlen, &p.ws, &rb);
   if (r) return r;
-  CUtensorMap mx, my;
+  CUtensorMap mx;
   r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
   if (r) return r;
-  r = make_tile_map(&my, a->out, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->out_stride, BP,
-                    Q, "out");
+  r = check_tile_tensor(a->out, a->dtype, a->out_stride, "out");
   if (r) return r;
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);
   p.H = static_cast<int>(a->nheads);
   p.P = static_cast<int>(a->headdim);
   p.nc = static_cast<int>(nc);
-  p.dA = a->dA;
-  p.dt = a->dt;
+  p.div_bh = make_fast_div(static_cast<uint32_t>(a->batch * a->nheads));
+  p.div_h = make_fast_div(static_cast<uint32_t>(a->nheads));
+  p.rows = ref_form ? a->dA : rb.rows;
   p.A = a->A;
   p.seq_idx = a->seq_idx;
   p.seq_idx_type = a->seq_idx_type;
@@ -243,8 +283,11 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   p.da_cs = a->da_cs;
   p.da_cs_sum = a->da_cs_sum;
   p.final_state = a->final_state;
+  p.y = a->out;
+  p.sy_b = a->out_stride[0];
+  p.sy_l = a->out_stride[1];
+  p.sy_h = a->out_stride[2];
   l.map_x = &mx;
-  l.map_y = &my;
   l.block_p = BP;
   l.chunk = Q;
   l.mode = ref_form ? kFwdLog2 : kFwdDt;
@@ -253,6 +296,10 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
+  if (dt_form) {  // per-(batch, head) contiguous rows of dt for the tile loads
+    r = launch_transpose(a->dt, rb.rows, a->batch, a->seqlen, a->nheads, l.stream);
+    if (r) return r;
+  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = fwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = fwd_dispatch_f16(l); break;
@@ -283,25 +330,25 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
 
   BwdLaunch l{};
   BwdParams& p = l.params;
-  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
+  RowBuffers rb;
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, a->batch * a->nheads * a->seqlen, &p.ws, &rb);
   if (r) return r;
-  CUtensorMap mx, mdy, mdx;
+  CUtensorMap mx, mdy;
   r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
   if (r) return r;
   r = make_tile_map(&mdy, a->dout, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dout_stride, BP,
                     Q, "dout");
   if (r) return r;
-  r = make_tile_map(&mdx, a->dx, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dx_stride, BP, Q,
-                    "dx");
+  r = check_tile_tensor(a->dx, a->dtype, a->dx_stride, "dx");
   if (r) return r;
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);
   p.H = static_cast<int>(a->nheads);
   p.P = static_cast<int>(a->headdim);
   p.nc = static_cast<int>(nc);
-  p.da_cs = a->da_cs;
-  p.da_cs_sum = a->da_cs_sum;
-  p.dt = a->dt;
+  p.div_bh = make_fast_div(static_cast<uint32_t>(a->batch * a->nheads));
+  p.div_h = make_fast_div(static_cast<uint32_t>(a->nheads));
+  p.rows = ref_form ? a->da_cs : rb.rows;
   p.A = a->A;
   p.states = a->states;
   p.st_b = a->states_stride[0];
@@ -311,12 +358,15 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   p.d_final = a->d_final_state;
   p.d_last = a->d_last_token;
   p.dl = a->dl;
-  p.ddt = a->ddt;
+  p.ddt_rows = rb.rows2;
   p.dA_out = a->dA_out;
   p.d_init = a->d_initial_state;
+  p.dx = a->dx;
+  p.sdx_b = a->dx_stride[0];
+  p.sdx_l = a->dx_stride[1];
+  p.sdx_h = a->dx_stride[2];
   l.map_x = &mx;
   l.map_dy = &mdy;
-  l.map_dx = &mdx;
   l.block_p = BP;
   l.chunk = Q;
   l.mode = ref_form ? kBwdCumsum : kBwdDt;
@@ -324,12 +374,19 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
+  if (dt_form) {
+    r = launch_transpose(a->dt, rb.rows, a->batch, a->seqlen, a->nheads, l.stream);
+    if (r) return r;
+  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = bwd_dispatch_f16(l); break;
     default: r = bwd_dispatch_f32(l); break;
   }
-  return map_dispatch_result(r, "ema_bwd");
+  r = map_dispatch_result(r, "ema_bwd");
+  if (r == EMA_OK && dt_form)  // ddt rows (B,H,L) -> ddt (B,L,H)
+    r = launch_transpose(rb.rows2, a->ddt, a->batch, a->nheads, a->seqlen, l.stream);
+  return r;
 }
 
 int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], float* dA_cs, const int64_t cs_stride[3],
