@@ -13,6 +13,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace emab {
 
@@ -243,6 +244,93 @@ __device__ __forceinline__ void store_pack_global_cs(T* p, const float (&f)[N]) 
 #pragma unroll
   for (int k = 0; k < N; ++k) e[k] = from_f32<T>(f[k]);
   st_cs(reinterpret_cast<R*>(p), r);
+}
+
+// ---- packed fp32x2 (sm_100 FFMA2 / FMUL2 / FADD2) -------------------------
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2_bcast(float a) { return make_float2(a, a); }
+
+// 2*NP consecutive elements as NP float pairs.
+template <typename T, int NP>
+__device__ __forceinline__ void load_pairs(const T* p, float2 (&v)[NP]) {
+  float f[2 * NP];
+  load_pack<T, 2 * NP>(p, f);
+#pragma unroll
+  for (int k = 0; k < NP; ++k) v[k] = make_float2(f[2 * k], f[2 * k + 1]);
+}
+template <typename T, int NP>
+__device__ __forceinline__ void store_pairs_global_cs(T* p, const float2 (&v)[NP]) {
+  float f[2 * NP];
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+    f[2 * k] = v[k].x;
+    f[2 * k + 1] = v[k].y;
+  }
+  store_pack_global_cs<T, 2 * NP>(p, f);
+}
+
+// ---- groups of 8 channels as 4 float pairs ----------------------------------
+// One lane's channel group: 16 bytes of bf16 / f16, 32 bytes of f32.
+struct U32x8 {
+  uint4 a, b;
+};
+template <typename T>
+__device__ __forceinline__ float2 cvt_pair(uint32_t w);
+template <>
+__device__ __forceinline__ float2 cvt_pair<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 cvt_pair<__half>(uint32_t w) {
+  __half2 h;
+  memcpy(&h, &w, 4);
+  return __half22float2(h);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float2 v);
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float2 v) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  uint32_t w;
+  memcpy(&w, &h, 4);
+  return w;
+}
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__half>(float2 v) {
+  const __half2 h = __floats2half2_rn(v.x, v.y);
+  uint32_t w;
+  memcpy(&w, &h, 4);
+  return w;
+}
+// 8 consecutive elements (16-byte aligned for 2-byte types, 32-byte for f32).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float2 (&v)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(b.x, b.y);
+    v[3] = make_float2(b.z, b.w);
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    v[0] = cvt_pair<T>(u.x);
+    v[1] = cvt_pair<T>(u.y);
+    v[2] = cvt_pair<T>(u.z);
+    v[3] = cvt_pair<T>(u.w);
+  }
+}
+// Streaming store of the first `n` (8, or 4 for f32) of 8 elements.
+template <typename T>
+__device__ __forceinline__ void store8_cs(T* p, const float2 (&v)[4], int n) {
+  if constexpr (sizeof(T) == 4) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+    if (n > 4) __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[2].x, v[2].y, v[3].x, v[3].y));
+  } else {
+    __stcs(reinterpret_cast<uint4*>(p),
+           make_uint4(pack_pair<T>(v[0]), pack_pair<T>(v[1]), pack_pair<T>(v[2]), pack_pair<T>(v[3])));
+  }
 }
 
 template <typename T, int N>

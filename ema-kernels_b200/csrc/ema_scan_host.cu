@@ -93,13 +93,12 @@ int make_tile_map(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t
 }
 
 int block_p_for(int64_t P) {
-  if (P <= 32) return 32;
   if (P <= 64) return 64;
   if (P <= 128) return 128;
   return 0;
 }
 
-// Workspace: 256-byte header | dA partials [tiles] f32 | aggregate records
+// Workspace: 256-byte header | dA partials [tiles][32] f32 | aggregate records
 // [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64 | two (B,H,L) f32
 // row buffers (dt-form: dt transposed to per-(batch, head) rows, and the ddt
 // rows the backward writes before they are transposed back).
@@ -113,7 +112,7 @@ WsLayout ws_layout(int64_t tiles, int BP, int64_t row_floats) {
   WsLayout l;
   size_t off = static_cast<size_t>(kHdrWords) * 4;
   l.partial = off;
-  off = align256(off + tiles * 4);
+  off = align256(off + static_cast<size_t>(tiles) * 32 * 4);
   l.agg = off;
   off = align256(off + static_cast<size_t>(tiles) * (BP + 1) * 8);
   l.incl = off;

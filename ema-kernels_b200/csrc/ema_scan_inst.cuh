@@ -58,7 +58,6 @@ int fwd_q(const FwdLaunch& l) {
 template <typename T, int MODE, bool SEQ>
 int fwd_bp(const FwdLaunch& l) {
   switch (l.block_p) {
-    case 32: return fwd_q<T, 32, MODE, SEQ>(l);
     case 64: return fwd_q<T, 64, MODE, SEQ>(l);
     case 128: return fwd_q<T, 128, MODE, SEQ>(l);
     default: return -1;
@@ -85,7 +84,6 @@ int bwd_q(const BwdLaunch& l) {
 template <typename T, int MODE>
 int bwd_bp(const BwdLaunch& l) {
   switch (l.block_p) {
-    case 32: return bwd_q<T, 32, MODE>(l);
     case 64: return bwd_q<T, 64, MODE>(l);
     case 128: return bwd_q<T, 128, MODE>(l);
     default: return -1;

@@ -15,12 +15,15 @@
 //                   (forward) or arriving gradient (backward) from the tiles
 //                   before it while the compute warps run the tile's first pass;
 //   compute warps   scan the tile in the stage: warp w owns a token segment,
-//                   lane l owns BP/32 channels; the recurrence runs
-//                   sequentially per thread (one FMA per element), segments
-//                   are chained in shared memory, tiles through global memory;
-//                   outputs go straight from registers to global memory
-//                   (coalesced 128-byte rows), so a stage is free as soon as
-//                   the tile's second pass has read it.
+//                   lane l owns BP/32 channels as packed fp32x2 pairs; the
+//                   segment's decay products come from warp shuffles, its
+//                   local scan (and, backward, its local gradient) runs
+//                   sequentially per thread and stays in registers; segments
+//                   are chained in shared memory (two block barriers per
+//                   tile), tiles through global memory; outputs go straight
+//                   from registers to global memory (coalesced rows, streaming
+//                   stores).  Each warp releases the stage with its own
+//                   mbarrier arrival as soon as it no longer reads it.
 //
 // The tile's incoming state (forward) or outgoing gradient (backward) comes
 // from a decoupled look-back over earlier tiles of the same (batch, head)
@@ -86,7 +89,7 @@ inline FastDiv make_fast_div(uint32_t d) {
 
 struct ScanWorkspace {
   uint32_t* hdr;   // kHdrWords header words
-  float* partial;  // [tiles] per-tile dA partial sums (dt-form backward)
+  float* partial;  // [tiles][32] per-(tile, warp) dA partial sums (dt-form backward)
   uint64_t* agg;   // [tiles][BP + 1] aggregate words (index BP: decay)
   uint64_t* incl;  // [tiles][BP] inclusive words
 };
@@ -294,16 +297,22 @@ __device__ __forceinline__ void load_row(float* dst, const float* src, int n, ui
 
 // Producer warp: tickets -> tiles -> loads into the ring.  `issue(s, ticket)`
 // sets s_tile[s] and issues the stage's TMA (lane 0) and cp.async (all lanes).
+// The next ticket is drawn as soon as the current one is taken, so the
+// counter's round trip (a microsecond or more under contention) overlaps the
+// wait for a free stage instead of adding to every refill.  Tickets are
+// still taken in increasing order per CTA, and each producer still draws
+// exactly one ticket past the last tile.
 template <int S, class Issue>
 __device__ __forceinline__ void producer_loop(uint64_t* full, uint64_t* empty, uint64_t* tid_full, int* s_tile,
                                               uint32_t* hdr, int total, int lane, Issue&& issue) {
   uint32_t* status = &hdr[kHdrStatus];
+  uint32_t next = 0;
+  if (lane == 0) next = atomicAdd(&hdr[kHdrTicket], 1u);
   for (int k = 0;; ++k) {
     const int s = k % S;
-    if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status, 512)) break;
-    uint32_t ticket = 0;
-    if (lane == 0) ticket = atomicAdd(&hdr[kHdrTicket], 1u);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status, 128)) break;
+    const uint32_t ticket = __shfl_sync(0xffffffffu, next, 0);
+    if (ticket < static_cast<uint32_t>(total) && lane == 0) next = atomicAdd(&hdr[kHdrTicket], 1u);
     if (ticket >= static_cast<uint32_t>(total)) {
       post_sentinel(&full[s], &tid_full[s], &s_tile[s], lane);
       break;
@@ -320,16 +329,20 @@ __device__ __forceinline__ void producer_loop(uint64_t* full, uint64_t* empty, u
 // incoming vector (forward: state entering the tile; backward: gradient
 // arriving at its end) in vec[k % 2][BP] for the compute warps, while they
 // run the tile's first pass.  `body(tile, run)` fills this lane's channels.
+// Having read the tile id it arrives on the stage's empty barrier (which
+// counts the compute warps and this warp).
 template <int S, int BP, class Body>
-__device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_tile, uint64_t* vec_full,
-                                              uint64_t* vec_empty, float* vec, uint32_t* status, int lane,
-                                              Body&& body) {
+__device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_tile, uint64_t* empty,
+                                              uint64_t* vec_full, uint64_t* vec_empty, float* vec,
+                                              uint32_t* status, int lane, Body&& body) {
   constexpr int CPT = BP / 32;
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!mbar_wait_bounded(&tid_full[s], (k / S) & 1, status, 512)) break;
     const int tile = s_tile[s];
     if (tile < 0) break;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
     if (k >= 2 && !mbar_wait_bounded(&vec_empty[k & 1], ((k >> 1) - 1) & 1, status, 512)) break;
     float run[CPT];
     body(tile, run);
@@ -341,29 +354,168 @@ __device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_t
 }
 
 // ---------------------------------------------------------------------------
+// Compute-warp lane layout shared by both kernels
+// ---------------------------------------------------------------------------
+// A compute warp owns a segment of SEG consecutive tokens of the tile.  Lane
+// (ts, cg) = (lane / CG, lane % CG) owns channels [8 cg, 8 cg + 8) of the
+// 8-token run ts of that segment: the recurrence runs sequentially over the
+// run's tokens on four independent fp32x2 pairs, every shared-memory access
+// is a 16-byte vector, and per-token sums over channels reduce across only
+// the CG lanes of a run.  Runs are chained inside the warp with shuffles,
+// segments inside the CTA through shared memory, tiles through the look-back.
+template <int BP>
+struct Lanes {
+  static constexpr int CG = BP / 8;     // lanes per token (8-channel groups)
+  static constexpr int TS = 32 / CG;    // runs per warp
+  static constexpr int RUN = 8;         // tokens per run
+  static constexpr int SEG = TS * RUN;  // tokens per warp
+};
+
+// Padded index of per-token shared arrays: the runs of a warp (8 tokens
+// apart) then fall in different banks.
+__device__ __forceinline__ constexpr int tix(int t) { return t + (t >> 3); }
+constexpr int tix_size(int q) { return q + q / 8; }
+
+// Scan of the affine maps z -> D z + E over the TS runs of a warp, in token
+// order (inclusive and exclusive).  E holds this lane's 8 channels; lanes of
+// one channel group are CG apart.
+template <int CG, int TS>
+__device__ __forceinline__ void runs_scan_fwd(float D, const float2 (&E)[4], int ts, float& Dinc, float2 (&Einc)[4],
+                                              float& Dexc, float2 (&Eexc)[4]) {
+  const unsigned FULL = 0xffffffffu;
+  Dinc = D;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) Einc[q] = E[q];
+#pragma unroll
+  for (int o = 1; o < TS; o <<= 1) {
+    const float Dp = __shfl_up_sync(FULL, Dinc, o * CG);
+    float2 Ep[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      Ep[q].x = __shfl_up_sync(FULL, Einc[q].x, o * CG);
+      Ep[q].y = __shfl_up_sync(FULL, Einc[q].y, o * CG);
+    }
+    if (ts >= o) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) Einc[q] = f2_fma(f2_bcast(Dinc), Ep[q], Einc[q]);
+      Dinc *= Dp;
+    }
+  }
+  Dexc = __shfl_up_sync(FULL, Dinc, CG);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    Eexc[q].x = __shfl_up_sync(FULL, Einc[q].x, CG);
+    Eexc[q].y = __shfl_up_sync(FULL, Einc[q].y, CG);
+  }
+  if (ts == 0) {
+    Dexc = 1.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Eexc[q] = make_float2(0.f, 0.f);
+  }
+}
+// The same in reverse token order: g -> D g + R, composed from the last run.
+template <int CG, int TS>
+__device__ __forceinline__ void runs_scan_rev(float D, const float2 (&R)[4], int ts, float& Dinc, float2 (&Rinc)[4],
+                                              float& Dexc, float2 (&Rexc)[4]) {
+  const unsigned FULL = 0xffffffffu;
+  Dinc = D;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) Rinc[q] = R[q];
+#pragma unroll
+  for (int o = 1; o < TS; o <<= 1) {
+    const float Dn = __shfl_down_sync(FULL, Dinc, o * CG);
+    float2 Rn[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      Rn[q].x = __shfl_down_sync(FULL, Rinc[q].x, o * CG);
+      Rn[q].y = __shfl_down_sync(FULL, Rinc[q].y, o * CG);
+    }
+    if (ts + o < TS) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) Rinc[q] = f2_fma(f2_bcast(Dinc), Rn[q], Rinc[q]);
+      Dinc *= Dn;
+    }
+  }
+  Dexc = __shfl_down_sync(FULL, Dinc, CG);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    Rexc[q].x = __shfl_down_sync(FULL, Rinc[q].x, CG);
+    Rexc[q].y = __shfl_down_sync(FULL, Rinc[q].y, CG);
+  }
+  if (ts == TS - 1) {
+    Dexc = 1.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Rexc[q] = make_float2(0.f, 0.f);
+  }
+}
+
+// Sum of v[j] over the CG lanes of a channel-group run, transposed: lane cg
+// returns the total of v[cg & 7].
+template <int CG>
+__device__ __forceinline__ float group_reduce8(float (&v)[8], int cg) {
+  const unsigned FULL = 0xffffffffu;
+  {
+    const bool up = cg & 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float send = up ? v[k] : v[k + 4];
+      const float keep = up ? v[k + 4] : v[k];
+      v[k] = keep + __shfl_xor_sync(FULL, send, 4);
+    }
+  }
+  {
+    const bool up = cg & 2;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float send = up ? v[k] : v[k + 2];
+      const float keep = up ? v[k + 2] : v[k];
+      v[k] = keep + __shfl_xor_sync(FULL, send, 2);
+    }
+  }
+  const bool up = cg & 1;
+  const float send = up ? v[0] : v[1];
+  float r = (up ? v[1] : v[0]) + __shfl_xor_sync(FULL, send, 1);
+  if (CG == 16) r += __shfl_xor_sync(FULL, r, 8);
+  return r;
+}
+
+__device__ __forceinline__ void st_row8(float* dst, const float2 (&v)[4]) {
+  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
+}
+__device__ __forceinline__ void ld_row8(const float* src, float2 (&v)[4]) {
+  const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+  v[0] = make_float2(a.x, a.y);
+  v[1] = make_float2(a.z, a.w);
+  v[2] = make_float2(b.x, b.y);
+  v[3] = make_float2(b.z, b.w);
+}
+
+// ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct FwdCfg {
-  static constexpr int CPT = BP / 32;
-  static constexpr int SEG = (BP <= 64) ? 32 : 16;
-  static constexpr int NW = Q / SEG;  // compute warps
-  static constexpr int NC = NW * 32;  // compute threads
-  static constexpr int NT = NC + 64;  // + producer warp + look-back warp
-  static_assert(BP % 32 == 0 && BP <= 128 && Q % SEG == 0 && NC >= Q && NC >= BP, "geometry");
+  using Ln = Lanes<BP>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG;
+  static constexpr int CPT = BP / 32;  // channels per lane of the look-back warp
+  static constexpr int NW = Q / SEG;   // compute warps
+  static constexpr int NC = NW * 32;   // compute threads
+  static constexpr int NT = NC + 64;   // + producer warp + look-back warp
+  static_assert((BP == 64 || BP == 128) && Q % SEG == 0 && NC >= BP && NC >= Q && NW <= 32, "geometry");
   static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
   static constexpr int kStage = align_up(kX + (Q + 4) * 4, 128);  // x tile | decay row | A_h
   // per-CTA state after the ring
-  static constexpr int oAW = 0;                  // float2[Q] (token decay, token weight)
-  static constexpr int oG = oAW + Q * 8;         // float[Q]  decay from the segment start through t
-  static constexpr int oL2 = oG + Q * 4;         // float[Q]  log2 decay
-  static constexpr int oE = oL2 + Q * 4;         // float[NW][BP]
-  static constexpr int oD = oE + NW * BP * 4;    // float[NW]
-  static constexpr int oG0 = oD + NW * 4;        // float[NW]
-  static constexpr int oSin = oG0 + NW * 4;      // float[2][BP]  from the look-back warp
-  static constexpr int oEt = oSin + 2 * BP * 4;  // float[BP]
-  static constexpr int oMisc = oEt + BP * 4;     // float[32]
-  static constexpr int oTile = oMisc + 32 * 4;   // int[kMaxStages]
+  static constexpr int oTok = 0;                              // float4[tix]  (a, a, w, w)
+  static constexpr int oG = oTok + tix_size(Q) * 16;          // float2[tix]  decay from the run start through t
+  static constexpr int oL2 = oG + tix_size(Q) * 8;            // float[Q]     log2 decay
+  static constexpr int oE = align_up(oL2 + Q * 4, 16);        // float[NW][BP]
+  static constexpr int oD = oE + NW * BP * 4;                 // float[NW]
+  static constexpr int oG0 = oD + NW * 4;                     // float[NW]
+  static constexpr int oSin = align_up(oG0 + NW * 4, 16);     // float[2][BP]  from the look-back warp
+  static constexpr int oEt = oSin + 2 * BP * 4;               // float[BP]
+  static constexpr int oMisc = oEt + BP * 4;                  // float[32]
+  static constexpr int oTile = oMisc + 32 * 4;                // int[kMaxStages]
   static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);  // full, empty, tid_full, vec_full/empty
   static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
   using R = Ring<kStage, kPriv>;
@@ -377,11 +529,11 @@ template <typename T, int BP, int Q, int MODE, bool SEQ>
 __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     ema_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const FwdParams p) {
   using C = FwdCfg<T, BP, Q>;
-  constexpr int CPT = C::CPT, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
+  constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
-  float2* s_aw = reinterpret_cast<float2*>(priv + C::oAW);
-  float* s_g = reinterpret_cast<float*>(priv + C::oG);
+  float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
+  float2* s_g = reinterpret_cast<float2*>(priv + C::oG);
   float* s_l2 = reinterpret_cast<float*>(priv + C::oL2);
   float* s_E = reinterpret_cast<float*>(priv + C::oE);
   float* s_D = reinterpret_cast<float*>(priv + C::oD);
@@ -404,13 +556,13 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     s_fail = 0u;
     s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 33);     // producer lane 0 (expect_tx) + 32 cp.async arrivals
-      mbar_init(&empty[s], 1);     // compute thread 0
-      mbar_init(&tid_full[s], 1);  // producer lane 0, once the tile id is written
+      mbar_init(&full[s], 33);       // producer lane 0 (expect_tx) + 32 cp.async arrivals
+      mbar_init(&empty[s], NW + 1);  // every compute warp + the look-back warp
+      mbar_init(&tid_full[s], 1);    // producer lane 0, once the tile id is written
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&vec_full[i], 1);   // look-back lane 0
-      mbar_init(&vec_empty[i], 1);  // compute thread 0
+      mbar_init(&vec_full[i], 1);    // look-back lane 0
+      mbar_init(&vec_empty[i], NW);  // every compute warp
     }
     fence_mbar_init();
   }
@@ -443,7 +595,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   }
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
-    lookback_loop<S, BP>(tid_full, s_tile, vec_full, vec_empty, s_Sin2, status, lane,
+    lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Sin2, status, lane,
                          [&](int tile, float(&run)[CPT]) {
                            const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
                            float rdec = 1.f;
@@ -465,9 +617,11 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   }
 
   // ------------------------------ compute warps ---------------------------
-  const int s0 = warp * SEG;
-  const int ch = lane * CPT;
-  const bool ch_ok = ch < p.P;  // P is a multiple of CPT: a pack is wholly in or out
+  const int ts = lane / CG, cg = lane % CG;
+  const int s0 = warp * SEG;      // this warp's first token in the tile
+  const int r0 = s0 + ts * 8;     // this lane's run
+  const int ch = cg * 8;          // this lane's channel group
+  const int nch = min(8, p.P - ch);  // valid channels of the group (P is a multiple of 4)
   const unsigned FULL = 0xffffffffu;
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -480,39 +634,42 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     const T* s_x = reinterpret_cast<const T*>(smem + s * C::kStage);
     const float* raw = reinterpret_cast<const float*>(smem + s * C::kStage + C::kX);
 
-    // ---- per-token decay and weight; decay products within each segment -----
-    if (tid < Q) {
-      const int t = t0 + tid;
+    // ---- this warp's tokens: decay, weight, decay products within each run ----
+    {
+      const int i = lane & (SEG - 1);
+      const int t = t0 + s0 + i;
       float a = 1.f, w = 0.f, l2 = 0.f;
       if (t < p.L) {
         if (MODE == kFwdLog2) {
-          l2 = raw[tid];
+          l2 = raw[s0 + i];
           w = 1.f;
         } else {
-          const float d = raw[tid];
+          const float d = raw[s0 + i];
           l2 = d * raw[Q] * kLog2e;
           w = d;
         }
         a = exp2f(l2);
         if (SEQ && t > 0) {
-          const size_t i = static_cast<size_t>(b) * p.L + t;
-          if (load_seq_id(p.seq_idx, p.seq_idx_type, i) != load_seq_id(p.seq_idx, p.seq_idx_type, i - 1))
+          const size_t gi = static_cast<size_t>(b) * p.L + t;
+          if (load_seq_id(p.seq_idx, p.seq_idx_type, gi) != load_seq_id(p.seq_idx, p.seq_idx_type, gi - 1))
             a = 0.f;
         }
       }
-      float g = a;  // product of the decays from the segment start through t
+      float g = a;  // product of the decays from the run start through t
 #pragma unroll
-      for (int o = 1; o < SEG; o <<= 1) {
-        const float n = __shfl_up_sync(FULL, g, o, SEG);
-        if ((lane & (SEG - 1)) >= o) g *= n;
+      for (int o = 1; o < 8; o <<= 1) {
+        const float n = __shfl_up_sync(FULL, g, o, 8);
+        if ((i & 7) >= o) g *= n;
       }
-      s_aw[tid] = make_float2(a, w);
-      s_g[tid] = g;
-      if ((lane & (SEG - 1)) == SEG - 1) s_D[tid / SEG] = g;
-      s_l2[tid] = l2;
+      if (lane < SEG) {
+        s_tok[tix(s0 + i)] = make_float4(a, a, w, w);
+        s_g[tix(s0 + i)] = f2_bcast(g);
+        s_l2[s0 + i] = l2;
+      }
     }
     if (MODE == kFwdLog2 && (p.da_cs != nullptr || p.da_cs_sum != nullptr)) {
       // within-chunk cumsum of the log2 decay (reference outputs da_cs / da_cs_sum)
+      named_sync(1, NC);
       float v = (tid < Q) ? s_l2[tid] : 0.f;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -527,29 +684,39 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       if (tid < Q && t0 + tid < p.L && p.da_cs != nullptr) p.da_cs[static_cast<size_t>(bh) * p.L + t0 + tid] = v;
       if (tid == Q - 1 && p.da_cs_sum != nullptr) p.da_cs_sum[static_cast<size_t>(bh) * p.nc + c] = v;
     }
-    named_sync(1, NC);
+    __syncwarp();
 
-    // ---- pass 1: local scan of the segment from zero, kept in registers -------
-    float zl[SEG][CPT];
+    // ---- pass 1: local scan of the run from zero, kept in registers -----------
+    float2 zl[8][4];
+    float Dexc;
+    float2 Eexc[4];
     {
-      float z[CPT];
+      float2 z[4];
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) z[q] = 0.f;
+      for (int q = 0; q < 4; ++q) z[q] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < SEG; ++i) {
-        const float2 aw = s_aw[s0 + i];
-        float xv[CPT];
-        load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
+      for (int u = 0; u < 8; ++u) {
+        const float4 tk = s_tok[tix(r0 + u)];
+        const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
+        float2 xv[4];
+        load8<T>(s_x + (r0 + u) * BP + ch, xv);
 #pragma unroll
-        for (int q = 0; q < CPT; ++q) {
-          z[q] = (MODE == kFwdLog2) ? fmaf(aw.x, z[q], xv[q]) : fmaf(aw.x, z[q], aw.y * xv[q]);
-          zl[i][q] = z[q];
+        for (int q = 0; q < 4; ++q) {
+          z[q] = (MODE == kFwdLog2) ? f2_fma(aa, z[q], xv[q]) : f2_fma(aa, z[q], f2_mul(ww, xv[q]));
+          zl[u][q] = z[q];
         }
       }
-#pragma unroll
-      for (int q = 0; q < CPT; ++q) s_E[warp * BP + ch + q] = z[q];
+      float Dinc;
+      float2 Einc[4];
+      runs_scan_fwd<CG, TS>(s_g[tix(r0 + 7)].x, z, ts, Dinc, Einc, Dexc, Eexc);
+      if (ts == TS - 1) {
+        st_row8(s_E + warp * BP + ch, Einc);  // the segment's end state from zero
+        if (cg == 0) s_D[warp] = Dinc;
+      }
     }
-    named_sync(1, NC);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the x stage
+    named_sync(1, NC);                      // every segment's end state and decay
 
     // ---- chain the segments; publish the tile aggregate ---------------------
     const bool has_succ = (c + 1 < p.nc);
@@ -571,12 +738,9 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
         if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Gd, tag));
       }
     }
-    named_sync(1, NC);
-
-    // ---- state entering the tile (from the look-back warp) -------------------
-    if (!compute_wait(&vec_full[k & 1], (k >> 1) & 1, status, warp, NC, &s_fail)) break;
-    // the x stage is no longer read (and the look-back warp has taken the tile id)
-    if (tid == 0) mbar_arrive(&empty[s]);
+    if (warp == NW - 1 && !mbar_wait_bounded(&vec_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
+    named_sync(1, NC);  // chained segments + the state entering the tile
+    if (s_fail) break;
     const float* s_Sin = s_Sin2 + (k & 1) * BP;
     if (tid < BP) {
       const float incl = fmaf(s_misc[0], s_Sin[tid], s_Et[tid]);  // state at the tile end
@@ -589,28 +753,34 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
         p.states[b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h + tid * p.st_p] = s_Sin[tid];
     }
 
-    // ---- pass 2: y = local scan + (segment decay so far) x (incoming state) ---
+    // ---- pass 2: y = local scan + (run decay so far) x (state entering the run)
+    float2 tin[4];
     {
-      const float g0 = s_G0[warp];
-      float tin[CPT];
+      const float2 g0 = f2_bcast(s_G0[warp]);
+      float2 sin[4], sw[4];
+      ld_row8(s_Sin + ch, sin);
+      ld_row8(s_E + warp * BP + ch, sw);
+      const float2 dx = f2_bcast(Dexc);
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) tin[q] = fmaf(g0, s_Sin[ch + q], s_E[warp * BP + ch + q]);
+      for (int q = 0; q < 4; ++q) tin[q] = f2_fma(dx, f2_fma(g0, sin[q], sw[q]), Eexc[q]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the incoming state
+    {
       // running row pointer: one 64-bit add per token
-      T* yp = static_cast<T*>(p.y) + b * p.sy_b + static_cast<long long>(t0 + s0) * p.sy_l + h * p.sy_h + ch;
+      T* yp = static_cast<T*>(p.y) + b * p.sy_b + static_cast<long long>(t0 + r0) * p.sy_l + h * p.sy_h + ch;
       const long long ystep = p.sy_l;
-      const int nv = ch_ok ? p.L - (t0 + s0) : 0;
+      const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
 #pragma unroll
-      for (int i = 0; i < SEG; ++i) {
-        const float g = s_g[s0 + i];
-        float yv[CPT];
+      for (int u = 0; u < 8; ++u) {
+        const float2 g = s_g[tix(r0 + u)];
+        float2 yv[4];
 #pragma unroll
-        for (int q = 0; q < CPT; ++q) yv[q] = fmaf(g, tin[q], zl[i][q]);
-        if (i < nv) store_pack_global_cs<T, CPT>(yp, yv);
+        for (int q = 0; q < 4; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
+        if (u < nv) store8_cs<T>(yp, yv, nch);
         yp += ystep;
       }
     }
-    named_sync(1, NC);
-    if (tid == 0) mbar_arrive(&vec_empty[k & 1]);
   }
   if (tid == 0 && count_cta_done(ws)) reset_counters(ws, epoch, total);
 }
@@ -620,28 +790,29 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct BwdCfg {
+  using Ln = Lanes<BP>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG;
   static constexpr int CPT = BP / 32;
-  static constexpr int SEG = 16;  // tokens per warp segment
-  static constexpr int RB = 8;    // tokens per transposed reduction
   static constexpr int NW = Q / SEG;
   static constexpr int NC = NW * 32;
   static constexpr int NT = NC + 64;
-  static_assert(BP % 32 == 0 && BP <= 128 && Q % SEG == 0 && NC >= Q && NC >= BP && NT <= 1024, "geometry");
+  static_assert((BP == 64 || BP == 128) && Q % SEG == 0 && NC >= BP && NT <= 1024 && NW <= 32 && NW % 2 == 0,
+                "geometry");
   static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
   // stage: x tile | dy tile | decay row [Q] | A_h [4] | chunk start state [BP]
   static constexpr int oRaw = 2 * kX;
   static constexpr int oSt = oRaw + (Q + 4) * 4;
   static constexpr int kStage = align_up(oSt + BP * 4, 128);
-  static constexpr int oAW = 0;                  // float2[Q] (token decay, token weight)
-  static constexpr int oGf = oAW + Q * 8;        // float[Q]  decay from the segment start through t
-  static constexpr int oE = oGf + Q * 4;         // float[NW][BP]  forward prefix -> Zin
-  static constexpr int oR = oE + NW * BP * 4;    // float[NW][BP]  reverse aggregate -> Rloc
-  static constexpr int oD = oR + NW * BP * 4;    // float[NW]
-  static constexpr int oHs = oD + NW * 4;        // float[NW]
-  static constexpr int oGn = oHs + NW * 4;       // float[2][BP]  from the look-back warp
-  static constexpr int oRt = oGn + 2 * BP * 4;   // float[BP]
-  static constexpr int oMisc = oRt + BP * 4;     // float[48]
-  static constexpr int oTile = oMisc + 48 * 4;   // int[kMaxStages]
+  static constexpr int oTok = 0;                           // float4[tix]  (a, a, w, w)
+  static constexpr int oG = oTok + tix_size(Q) * 16;       // float2[tix]  decay after t through the run end
+  static constexpr int oE = align_up(oG + tix_size(Q) * 8, 16);  // float[NW][BP]  forward prefix -> Zin
+  static constexpr int oR = oE + NW * BP * 4;              // float[NW][BP]  reverse aggregate -> Rloc
+  static constexpr int oD = oR + NW * BP * 4;              // float[NW]
+  static constexpr int oHs = oD + NW * 4;                  // float[NW]
+  static constexpr int oGn = align_up(oHs + NW * 4, 16);   // float[2][BP]  from the look-back warp
+  static constexpr int oRt = oGn + 2 * BP * 4;             // float[BP]
+  static constexpr int oMisc = oRt + BP * 4;               // float[8]
+  static constexpr int oTile = oMisc + 8 * 4;              // int[kMaxStages]
   static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);  // full, empty, tid_full, vec_full/empty
   static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
   using R = Ring<kStage, kPriv>;
@@ -656,11 +827,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     ema_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_dy,
                    const BwdParams p) {
   using C = BwdCfg<T, BP, Q>;
-  constexpr int CPT = C::CPT, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S, RB = C::RB;
+  constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
-  float2* s_aw = reinterpret_cast<float2*>(priv + C::oAW);
-  float* s_gf = reinterpret_cast<float*>(priv + C::oGf);
+  float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
+  float2* s_g = reinterpret_cast<float2*>(priv + C::oG);
   float* s_E = reinterpret_cast<float*>(priv + C::oE);
   float* s_R = reinterpret_cast<float*>(priv + C::oR);
   float* s_D = reinterpret_cast<float*>(priv + C::oD);
@@ -684,12 +855,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 33);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], NW + 1);
       mbar_init(&tid_full[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&vec_full[i], 1);
-      mbar_init(&vec_empty[i], 1);
+      mbar_init(&vec_empty[i], NW);
     }
     fence_mbar_init();
   }
@@ -735,7 +906,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   }
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
-    lookback_loop<S, BP>(tid_full, s_tile, vec_full, vec_empty, s_Gn2, status, lane,
+    lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Gn2, status, lane,
                          [&](int tile, float(&run)[CPT]) {
                            const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
                            float rdec = 1.f;
@@ -757,9 +928,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   }
 
   // ------------------------------ compute warps ---------------------------
+  const int ts = lane / CG, cg = lane % CG;
   const int s0 = warp * SEG;
-  const int ch = lane * CPT;
-  const bool ch_ok = ch < p.P;
+  const int r0 = s0 + ts * 8;
+  const int ch = cg * 8;
+  const int nch = min(8, p.P - ch);
   const unsigned FULL = 0xffffffffu;
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -776,63 +949,85 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     const float* s_Sin = reinterpret_cast<const float*>(st + C::oSt);
     const float Ah = (MODE == kBwdDt) ? raw[Q] : 0.f;
 
-    // ---- per-token decay / weight; decay products within each segment ---------
-    if (tid < Q) {
-      const int t = t0 + tid;
+    // ---- this warp's tokens: decay, weight, decay after t within each run -----
+    {
+      const int i = lane & (SEG - 1);
+      const int t = t0 + s0 + i;
       float a = 1.f, w = 0.f;
       if (t < p.L) {
         if (MODE == kBwdCumsum) {
-          const float prev = (tid == 0) ? 0.f : raw[tid - 1];
-          a = exp2f(raw[tid] - prev);
+          const float prev = (s0 + i == 0) ? 0.f : raw[s0 + i - 1];
+          a = exp2f(raw[s0 + i] - prev);
           w = 1.f;
         } else {
-          const float d = raw[tid];
+          const float d = raw[s0 + i];
           a = exp2f(d * Ah * kLog2e);
           w = d;
         }
       }
-      float g = a;
+      float gb = a;  // product of the decays from t through the run end
 #pragma unroll
-      for (int o = 1; o < SEG; o <<= 1) {
-        const float n = __shfl_up_sync(FULL, g, o, SEG);
-        if ((lane & (SEG - 1)) >= o) g *= n;
+      for (int o = 1; o < 8; o <<= 1) {
+        const float m = __shfl_down_sync(FULL, gb, o, 8);
+        if ((i & 7) + o < 8) gb *= m;
       }
-      s_aw[tid] = make_float2(a, w);
-      s_gf[tid] = g;
-      if ((lane & (SEG - 1)) == SEG - 1) s_D[tid / SEG] = g;
+      float gr = __shfl_down_sync(FULL, gb, 1, 8);  // decay after t through the run end
+      if ((i & 7) == 7) gr = 1.f;
+      if (lane < SEG) {
+        s_tok[tix(s0 + i)] = make_float4(a, a, w, w);
+        s_g[tix(s0 + i)] = f2_bcast(gr);
+      }
     }
-    named_sync(1, NC);
+    __syncwarp();
 
-    // ---- pass 1: local forward scan (kept in registers) and reverse aggregate --
-    float zl[SEG][CPT];
+    // ---- pass 1: forward aggregate; local gradients kept in registers ---------
+    //   z  <- a_u z + w_u x_u                      (u ascending; only the end value)
+    //   gc <- a_{u+1} gc + dy_u,  gl[u] = gc       (u descending; gradient from
+    //                                               this run's dy only)
+    float2 gl[8][4];
+    float Dexc, Dsuf;
+    float2 Eexc[4], Gexc[4];
     {
-      float z[CPT], r[CPT];
+      float2 z[4], gc[4];
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) z[q] = r[q] = 0.f;
+      for (int q = 0; q < 4; ++q) z[q] = gc[q] = make_float2(0.f, 0.f);
+      float2 an = make_float2(0.f, 0.f);  // a_{u+1}; nothing beyond the run end
 #pragma unroll
-      for (int i = 0; i < SEG; ++i) {
-        const float2 aw = s_aw[s0 + i];
-        float xv[CPT];
-        load_pack<T, CPT>(s_x + (s0 + i) * BP + ch, xv);
+      for (int i = 0; i < 8; ++i) {
+        const float4 tk = s_tok[tix(r0 + i)];
+        float2 xv[4];
+        load8<T>(s_x + (r0 + i) * BP + ch, xv);
 #pragma unroll
-        for (int q = 0; q < CPT; ++q) {
-          z[q] = (MODE == kBwdCumsum) ? fmaf(aw.x, z[q], xv[q]) : fmaf(aw.x, z[q], aw.y * xv[q]);
-          zl[i][q] = z[q];
+        for (int q = 0; q < 4; ++q)
+          z[q] = (MODE == kBwdCumsum) ? f2_fma(make_float2(tk.x, tk.y), z[q], xv[q])
+                                      : f2_fma(make_float2(tk.x, tk.y), z[q], f2_mul(make_float2(tk.z, tk.w), xv[q]));
+        const int u = 7 - i;
+        float2 dv[4];
+        load8<T>(s_dy + (r0 + u) * BP + ch, dv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          gc[q] = f2_fma(an, gc[q], dv[q]);
+          gl[u][q] = gc[q];
         }
-        const int j = SEG - 1 - i;
-        const float aj = s_aw[s0 + j].x;
-        float dv[CPT];
-        load_pack<T, CPT>(s_dy + (s0 + j) * BP + ch, dv);
-#pragma unroll
-        for (int q = 0; q < CPT; ++q) r[q] = aj * (dv[q] + r[q]);
+        const float4 tu = s_tok[tix(r0 + u)];
+        an = make_float2(tu.x, tu.y);
       }
+      // an = a at the run start: the run's dy reaches the state before it as a_r0 gc
+      float2 Rr[4];
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) {
-        s_E[warp * BP + ch + q] = z[q];
-        s_R[warp * BP + ch + q] = r[q];
+      for (int q = 0; q < 4; ++q) Rr[q] = f2_mul(an, gc[q]);
+      const float Drun = an.x * s_g[tix(r0)].x;
+      float Dinc, Drinc;
+      float2 Einc[4], Rinc[4];
+      runs_scan_fwd<CG, TS>(Drun, z, ts, Dinc, Einc, Dexc, Eexc);
+      runs_scan_rev<CG, TS>(Drun, Rr, ts, Drinc, Rinc, Dsuf, Gexc);
+      if (ts == TS - 1) {
+        st_row8(s_E + warp * BP + ch, Einc);
+        if (cg == 0) s_D[warp] = Dinc;
       }
+      if (ts == 0) st_row8(s_R + warp * BP + ch, Rinc);
     }
-    named_sync(1, NC);
+    named_sync(1, NC);  // every segment's aggregates
 
     // ---- chain segments: Zin (forward) and Rloc (reverse); publish ----------
     const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
@@ -861,10 +1056,9 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Hd, tag));
       }
     }
-    named_sync(1, NC);
-
-    // ---- gradient arriving at the tile end (from the look-back warp) ----------
-    if (!compute_wait(&vec_full[k & 1], (k >> 1) & 1, status, warp, NC, &s_fail)) break;
+    if (warp == NW - 1 && !mbar_wait_bounded(&vec_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
+    named_sync(1, NC);  // chained segments + the gradient arriving at the tile end
+    if (s_fail) break;
     const float* s_Gn = s_Gn2 + (k & 1) * BP;
     if (tid < BP) {
       const float incl = fmaf(s_misc[0], s_Gn[tid], s_Rt[tid]);  // gradient w.r.t. the state before the tile
@@ -875,110 +1069,123 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       }
     }
 
-    // ---- pass 2: reverse sweep with exact gradients ------------------------------
-    float dap = 0.f;  // dt form: sum over this lane's tokens of dt * dl
+    // ---- pass 2: exact gradients, first token first ---------------------------
+    //   G_t = gl_t + (decay after t in the run) x (gradient at the run end)
+    //   z_{t-1} runs forward from the true state before the run
+    float2 zp[4], gend[4];
     {
-      float zin[CPT], g[CPT];
-      const float hs = s_Hs[warp];
+      float2 zw[4], gn[4], rw[4];
+      ld_row8(s_E + warp * BP + ch, zw);
+      ld_row8(s_Gn + ch, gn);
+      ld_row8(s_R + warp * BP + ch, rw);
+      const float2 hs = f2_bcast(s_Hs[warp]), de = f2_bcast(Dexc), ds = f2_bcast(Dsuf);
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) {
-        zin[q] = s_E[warp * BP + ch + q];
-        g[q] = fmaf(hs, s_Gn[ch + q], s_R[warp * BP + ch + q]);  // gradient w.r.t. z at the segment end
+      for (int q = 0; q < 4; ++q) {
+        zp[q] = f2_fma(de, zw[q], Eexc[q]);
+        gend[q] = f2_fma(ds, f2_fma(hs, gn[q], rw[q]), Gexc[q]);
       }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the arriving gradient
+    float2 dacc = make_float2(0.f, 0.f);  // dt form: sum over this lane's tokens of dt a G z_{t-1}
+    {
       const float* dlast = (p.d_last != nullptr && t0 + Q >= p.L) ? p.d_last + static_cast<size_t>(bh) * p.P
                                                                  : nullptr;
-      // running row pointer (reverse order): one 64-bit add per token
+      // running row pointer: one 64-bit add per token
       const long long dxstep = p.sdx_l;
-      T* dxp = static_cast<T*>(p.dx) + b * p.sdx_b + static_cast<long long>(t0 + s0 + SEG - 1) * dxstep +
-               h * p.sdx_h + ch;
-      const int nv = ch_ok ? p.L - (t0 + s0) : 0;
+      T* dxp = static_cast<T*>(p.dx) + b * p.sdx_b + static_cast<long long>(t0 + r0) * dxstep + h * p.sdx_h + ch;
+      const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
+      const float2 A2 = f2_bcast(Ah);
+      float pr[8];
 #pragma unroll
-      for (int blk = SEG / RB - 1; blk >= 0; --blk) {
-        float p1[RB], p2[RB];
+      for (int u = 0; u < 8; ++u) {
+        const int t = r0 + u;
+        const float4 tk = s_tok[tix(t)];
+        const float2 gr = s_g[tix(t)];
+        const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
+        float2 G[4], dxv[4], xv[4];
 #pragma unroll
-        for (int j = RB - 1; j >= 0; --j) {
-          const int i = blk * RB + j;
-          const int t = s0 + i;
-          const float2 aw = s_aw[t];
-          float dv[CPT];
-          load_pack<T, CPT>(s_dy + t * BP + ch, dv);
-          float Gv[CPT], dxv[CPT];
-#pragma unroll
-          for (int q = 0; q < CPT; ++q) {
-            Gv[q] = dv[q] + g[q];
-            dxv[q] = (MODE == kBwdCumsum) ? Gv[q] : aw.y * Gv[q];
-          }
-          if (dlast != nullptr && t0 + t == p.L - 1) {
-#pragma unroll
-            for (int q = 0; q < CPT; ++q)
-              if (ch + q < p.P) dxv[q] += dlast[ch + q];
-          }
-          if (i < nv) store_pack_global_cs<T, CPT>(dxp, dxv);
-          dxp -= dxstep;
-          // state before token t: local scan of the previous token + decay so far x Zin
-          const float gprev = (i > 0) ? s_gf[t - 1] : 1.f;
-          float q1 = 0.f, q2 = 0.f;
-#pragma unroll
-          for (int q = 0; q < CPT; ++q) {
-            const float zp = (i > 0) ? fmaf(gprev, zin[q], zl[i > 0 ? i - 1 : 0][q]) : zin[q];
-            q1 = fmaf(Gv[q], zp, q1);
-            g[q] = aw.x * Gv[q];
-          }
-          if (MODE == kBwdDt) {
-            float xv[CPT];
-            load_pack<T, CPT>(s_x + t * BP + ch, xv);
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) q2 = fmaf(Gv[q], xv[q], q2);
-          }
-          p1[j] = aw.x * q1;
-          p2[j] = q2;
+        for (int q = 0; q < 4; ++q) {
+          G[q] = f2_fma(gr, gend[q], gl[u][q]);
+          dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
         }
-        const float P1 = transpose_reduce8(p1, lane);
-        float P2 = 0.f;
-        if (MODE == kBwdDt) P2 = transpose_reduce8(p2, lane);
-        if ((lane & 3) == 0) {
-          const int t = s0 + blk * RB + (lane >> 2);
-          const int gt = t0 + t;
-          if (gt < p.L) {
-            if (MODE == kBwdCumsum) {
-              p.dl[static_cast<size_t>(bh) * p.L + gt] = P1;
-            } else {
-              p.ddt_rows[static_cast<size_t>(bh) * p.L + gt] = fmaf(Ah, P1, P2);
-              dap = fmaf(s_aw[t].y, P1, dap);
+        if (dlast != nullptr && t0 + t == p.L - 1) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (2 * q < nch) {
+              dxv[q].x += dlast[ch + 2 * q];
+              dxv[q].y += dlast[ch + 2 * q + 1];
             }
           }
         }
+        if (u < nv) store8_cs<T>(dxp, dxv, nch);
+        dxp += dxstep;
+        load8<T>(s_x + t * BP + ch, xv);
+        if (MODE == kBwdCumsum) {
+          // dl_t = a_t sum_p G_t z_{t-1}
+          float2 m = f2_mul(G[0], zp[0]);
+#pragma unroll
+          for (int q = 1; q < 4; ++q) m = f2_fma(G[q], zp[q], m);
+          pr[u] = tk.x * (m.x + m.y);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
+        } else {
+          // ddt_t = sum_p G_t (x_t + A a_t z_{t-1});  dA += dt_t a_t sum_p G_t z_{t-1}
+          const float2 Aa = f2_mul(A2, aa), wa = f2_mul(ww, aa);
+          float2 m = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            m = f2_fma(G[q], f2_fma(Aa, zp[q], xv[q]), m);
+            dacc = f2_fma(wa, f2_mul(G[q], zp[q]), dacc);
+            zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
+          }
+          pr[u] = m.x + m.y;
+        }
+      }
+      const float Pr = group_reduce8<CG>(pr, cg);
+      if (cg < 8) {
+        const int gt = t0 + r0 + cg;
+        if (gt < p.L) {
+          if (MODE == kBwdCumsum) p.dl[static_cast<size_t>(bh) * p.L + gt] = Pr;
+          else p.ddt_rows[static_cast<size_t>(bh) * p.L + gt] = Pr;
+        }
       }
     }
-
-    // ---- dt form: per-tile partial of dA (fixed order) -------------------------
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the stage
     if (MODE == kBwdDt) {
+      // per-(tile, warp) partial of dA, summed in a fixed order by the last CTA
+      float dap = dacc.x + dacc.y;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(FULL, dap, o);
-      if (lane == 0) s_misc[1 + warp] = dap;
-    }
-    named_sync(1, NC);
-    if (tid == 0) {
-      if (MODE == kBwdDt) {
-        float tot = 0.f;
-        for (int w = 0; w < NW; ++w) tot += s_misc[1 + w];
-        ws.partial[slot] = tot;
-      }
-      mbar_arrive(&empty[s]);
-      mbar_arrive(&vec_empty[k & 1]);
+      if (lane == 0) ws.partial[slot * 32 + warp] = dap;
     }
   }
+  named_sync(1, NC);
   if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
   named_sync(1, NC);
   if (s_last) {
     if (MODE == kBwdDt) {
+      // dA[h] = sum over (chunk, batch, warp) of the partials: warp-per-head,
+      // a fixed split over lanes and a fixed shuffle tree (deterministic);
+      // independent L2 loads, so the tail is one round trip per few rows
       __threadfence();
-      for (int hh = tid; hh < p.H; hh += NC) {
+      const int nbt = p.nc * p.B;
+      for (int hh = warp; hh < p.H; hh += NW) {
         float acc = 0.f;
-        for (int cc = 0; cc < p.nc; ++cc)
-          for (int bb = 0; bb < p.B; ++bb)
-            acc += ld_relaxed_gpu(&ws.partial[static_cast<size_t>(cc) * BH + bb * p.H + hh]);
-        p.dA_out[hh] = acc;
+        for (int j = lane; j < nbt; j += 32) {
+          const int cc = j / p.B, bb = j - cc * p.B;
+          const float2* part =
+              reinterpret_cast<const float2*>(ws.partial + (static_cast<size_t>(cc) * BH + bb * p.H + hh) * 32);
+#pragma unroll
+          for (int w = 0; w < NW / 2; ++w) {
+            const float2 v = __ldcg(part + w);
+            acc += v.x + v.y;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+        if (lane == 0) p.dA_out[hh] = acc;
       }
       named_sync(1, NC);
     }
