@@ -333,6 +333,34 @@ __device__ __forceinline__ void store8_cs(T* p, const float2 (&v)[4], int n) {
   }
 }
 
+// NPR float pairs of consecutive elements (NPR = 2 or 4).
+template <typename T, int NPR>
+__device__ __forceinline__ void load_grp(const T* p, float2 (&v)[NPR]) {
+  if constexpr (NPR == 4) {
+    load8<T>(p, v);
+  } else if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    v[0] = cvt_pair<T>(u.x);
+    v[1] = cvt_pair<T>(u.y);
+  }
+}
+// Streaming store of the first `n` of 2 * NPR elements (n is 2 * NPR, or 4
+// for an f32 group of 8 straddling the channel count).
+template <typename T, int NPR>
+__device__ __forceinline__ void store_grp_cs(T* p, const float2 (&v)[NPR], int n) {
+  if constexpr (NPR == 4) {
+    store8_cs<T>(p, v, n);
+  } else if constexpr (sizeof(T) == 4) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+  } else {
+    __stcs(reinterpret_cast<uint2*>(p), make_uint2(pack_pair<T>(v[0]), pack_pair<T>(v[1])));
+  }
+}
+
 template <typename T, int N>
 __device__ __forceinline__ void store_pack(T* p, const float (&f)[N]) {
   using R = typename RawVec<sizeof(T) * N>::type;

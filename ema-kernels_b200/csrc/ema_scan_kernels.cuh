@@ -89,7 +89,7 @@ inline FastDiv make_fast_div(uint32_t d) {
 
 struct ScanWorkspace {
   uint32_t* hdr;   // kHdrWords header words
-  float* partial;  // [tiles][32] per-(tile, warp) dA partial sums (dt-form backward)
+  float* partial;  // per-(tile, warp) dA partial sums, head-major (dt-form backward; room for 32 per tile)
   uint64_t* agg;   // [tiles][BP + 1] aggregate words (index BP: decay)
   uint64_t* incl;  // [tiles][BP] inclusive words
 };
@@ -357,15 +357,17 @@ __device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_t
 // Compute-warp lane layout shared by both kernels
 // ---------------------------------------------------------------------------
 // A compute warp owns a segment of SEG consecutive tokens of the tile.  Lane
-// (ts, cg) = (lane / CG, lane % CG) owns channels [8 cg, 8 cg + 8) of the
-// 8-token run ts of that segment: the recurrence runs sequentially over the
-// run's tokens on four independent fp32x2 pairs, every shared-memory access
-// is a 16-byte vector, and per-token sums over channels reduce across only
-// the CG lanes of a run.  Runs are chained inside the warp with shuffles,
+// (ts, cg) = (lane / CG, lane % CG) owns channels [CPL cg, CPL cg + CPL) of
+// the 8-token run ts of that segment: the recurrence runs sequentially over
+// the run's tokens on CPL / 2 independent fp32x2 pairs, every shared-memory
+// access is a vector, and per-token sums over channels reduce across only the
+// CG lanes of a run.  Runs are chained inside the warp with shuffles,
 // segments inside the CTA through shared memory, tiles through the look-back.
-template <int BP>
+template <int BP, int CPL>
 struct Lanes {
-  static constexpr int CG = BP / 8;     // lanes per token (8-channel groups)
+  static_assert(CPL == 4 || CPL == 8, "4 or 8 channels per lane");
+  static constexpr int NPR = CPL / 2;   // fp32x2 pairs per lane
+  static constexpr int CG = BP / CPL;   // lanes per token (channel groups)
   static constexpr int TS = 32 / CG;    // runs per warp
   static constexpr int RUN = 8;         // tokens per run
   static constexpr int SEG = TS * RUN;  // tokens per warp
@@ -379,73 +381,73 @@ constexpr int tix_size(int q) { return q + q / 8; }
 // Scan of the affine maps z -> D z + E over the TS runs of a warp, in token
 // order (inclusive and exclusive).  E holds this lane's 8 channels; lanes of
 // one channel group are CG apart.
-template <int CG, int TS>
-__device__ __forceinline__ void runs_scan_fwd(float D, const float2 (&E)[4], int ts, float& Dinc, float2 (&Einc)[4],
-                                              float& Dexc, float2 (&Eexc)[4]) {
+template <int CG, int TS, int NPR>
+__device__ __forceinline__ void runs_scan_fwd(float D, const float2 (&E)[NPR], int ts, float& Dinc,
+                                              float2 (&Einc)[NPR], float& Dexc, float2 (&Eexc)[NPR]) {
   const unsigned FULL = 0xffffffffu;
   Dinc = D;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) Einc[q] = E[q];
+  for (int q = 0; q < NPR; ++q) Einc[q] = E[q];
 #pragma unroll
   for (int o = 1; o < TS; o <<= 1) {
     const float Dp = __shfl_up_sync(FULL, Dinc, o * CG);
-    float2 Ep[4];
+    float2 Ep[NPR];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NPR; ++q) {
       Ep[q].x = __shfl_up_sync(FULL, Einc[q].x, o * CG);
       Ep[q].y = __shfl_up_sync(FULL, Einc[q].y, o * CG);
     }
     if (ts >= o) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) Einc[q] = f2_fma(f2_bcast(Dinc), Ep[q], Einc[q]);
+      for (int q = 0; q < NPR; ++q) Einc[q] = f2_fma(f2_bcast(Dinc), Ep[q], Einc[q]);
       Dinc *= Dp;
     }
   }
   Dexc = __shfl_up_sync(FULL, Dinc, CG);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < NPR; ++q) {
     Eexc[q].x = __shfl_up_sync(FULL, Einc[q].x, CG);
     Eexc[q].y = __shfl_up_sync(FULL, Einc[q].y, CG);
   }
   if (ts == 0) {
     Dexc = 1.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) Eexc[q] = make_float2(0.f, 0.f);
+    for (int q = 0; q < NPR; ++q) Eexc[q] = make_float2(0.f, 0.f);
   }
 }
 // The same in reverse token order: g -> D g + R, composed from the last run.
-template <int CG, int TS>
-__device__ __forceinline__ void runs_scan_rev(float D, const float2 (&R)[4], int ts, float& Dinc, float2 (&Rinc)[4],
-                                              float& Dexc, float2 (&Rexc)[4]) {
+template <int CG, int TS, int NPR>
+__device__ __forceinline__ void runs_scan_rev(float D, const float2 (&R)[NPR], int ts, float& Dinc,
+                                              float2 (&Rinc)[NPR], float& Dexc, float2 (&Rexc)[NPR]) {
   const unsigned FULL = 0xffffffffu;
   Dinc = D;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) Rinc[q] = R[q];
+  for (int q = 0; q < NPR; ++q) Rinc[q] = R[q];
 #pragma unroll
   for (int o = 1; o < TS; o <<= 1) {
     const float Dn = __shfl_down_sync(FULL, Dinc, o * CG);
-    float2 Rn[4];
+    float2 Rn[NPR];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NPR; ++q) {
       Rn[q].x = __shfl_down_sync(FULL, Rinc[q].x, o * CG);
       Rn[q].y = __shfl_down_sync(FULL, Rinc[q].y, o * CG);
     }
     if (ts + o < TS) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) Rinc[q] = f2_fma(f2_bcast(Dinc), Rn[q], Rinc[q]);
+      for (int q = 0; q < NPR; ++q) Rinc[q] = f2_fma(f2_bcast(Dinc), Rn[q], Rinc[q]);
       Dinc *= Dn;
     }
   }
   Dexc = __shfl_down_sync(FULL, Dinc, CG);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < NPR; ++q) {
     Rexc[q].x = __shfl_down_sync(FULL, Rinc[q].x, CG);
     Rexc[q].y = __shfl_down_sync(FULL, Rinc[q].y, CG);
   }
   if (ts == TS - 1) {
     Dexc = 1.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) Rexc[q] = make_float2(0.f, 0.f);
+    for (int q = 0; q < NPR; ++q) Rexc[q] = make_float2(0.f, 0.f);
   }
 }
 
@@ -475,20 +477,25 @@ __device__ __forceinline__ float group_reduce8(float (&v)[8], int cg) {
   const bool up = cg & 1;
   const float send = up ? v[0] : v[1];
   float r = (up ? v[1] : v[0]) + __shfl_xor_sync(FULL, send, 1);
-  if (CG == 16) r += __shfl_xor_sync(FULL, r, 8);
+  if (CG >= 16) r += __shfl_xor_sync(FULL, r, 8);
+  if (CG >= 32) r += __shfl_xor_sync(FULL, r, 16);
   return r;
 }
 
-__device__ __forceinline__ void st_row8(float* dst, const float2 (&v)[4]) {
-  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
-  reinterpret_cast<float4*>(dst)[1] = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
+template <int NPR>
+__device__ __forceinline__ void st_row(float* dst, const float2 (&v)[NPR]) {
+#pragma unroll
+  for (int q = 0; q < NPR; q += 2)
+    reinterpret_cast<float4*>(dst)[q / 2] = make_float4(v[q].x, v[q].y, v[q + 1].x, v[q + 1].y);
 }
-__device__ __forceinline__ void ld_row8(const float* src, float2 (&v)[4]) {
-  const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
-  v[0] = make_float2(a.x, a.y);
-  v[1] = make_float2(a.z, a.w);
-  v[2] = make_float2(b.x, b.y);
-  v[3] = make_float2(b.z, b.w);
+template <int NPR>
+__device__ __forceinline__ void ld_row(const float* src, float2 (&v)[NPR]) {
+#pragma unroll
+  for (int q = 0; q < NPR; q += 2) {
+    const float4 a = reinterpret_cast<const float4*>(src)[q / 2];
+    v[q] = make_float2(a.x, a.y);
+    v[q + 1] = make_float2(a.z, a.w);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -496,8 +503,9 @@ __device__ __forceinline__ void ld_row8(const float* src, float2 (&v)[4]) {
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct FwdCfg {
-  using Ln = Lanes<BP>;
-  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG;
+  static constexpr int CPL = 8;  // channels per compute lane
+  using Ln = Lanes<BP, CPL>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR;
   static constexpr int CPT = BP / 32;  // channels per lane of the look-back warp
   static constexpr int NW = Q / SEG;   // compute warps
   static constexpr int NC = NW * 32;   // compute threads
@@ -530,6 +538,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     ema_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const FwdParams p) {
   using C = FwdCfg<T, BP, Q>;
   constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
+  constexpr int CPL = C::CPL, NPR = C::NPR;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
   float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
@@ -620,8 +629,8 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   const int ts = lane / CG, cg = lane % CG;
   const int s0 = warp * SEG;      // this warp's first token in the tile
   const int r0 = s0 + ts * 8;     // this lane's run
-  const int ch = cg * 8;          // this lane's channel group
-  const int nch = min(8, p.P - ch);  // valid channels of the group (P is a multiple of 4)
+  const int ch = cg * CPL;        // this lane's channel group
+  const int nch = min(CPL, p.P - ch);  // valid channels of the group (P is a multiple of 4)
   const unsigned FULL = 0xffffffffu;
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -687,30 +696,30 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     __syncwarp();
 
     // ---- pass 1: local scan of the run from zero, kept in registers -----------
-    float2 zl[8][4];
+    float2 zl[8][NPR];
     float Dexc;
-    float2 Eexc[4];
+    float2 Eexc[NPR];
     {
-      float2 z[4];
+      float2 z[NPR];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) z[q] = make_float2(0.f, 0.f);
+      for (int q = 0; q < NPR; ++q) z[q] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float4 tk = s_tok[tix(r0 + u)];
         const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
-        float2 xv[4];
-        load8<T>(s_x + (r0 + u) * BP + ch, xv);
+        float2 xv[NPR];
+        load_grp<T, NPR>(s_x + (r0 + u) * BP + ch, xv);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NPR; ++q) {
           z[q] = (MODE == kFwdLog2) ? f2_fma(aa, z[q], xv[q]) : f2_fma(aa, z[q], f2_mul(ww, xv[q]));
           zl[u][q] = z[q];
         }
       }
       float Dinc;
-      float2 Einc[4];
-      runs_scan_fwd<CG, TS>(s_g[tix(r0 + 7)].x, z, ts, Dinc, Einc, Dexc, Eexc);
+      float2 Einc[NPR];
+      runs_scan_fwd<CG, TS, NPR>(s_g[tix(r0 + 7)].x, z, ts, Dinc, Einc, Dexc, Eexc);
       if (ts == TS - 1) {
-        st_row8(s_E + warp * BP + ch, Einc);  // the segment's end state from zero
+        st_row<NPR>(s_E + warp * BP + ch, Einc);  // the segment's end state from zero
         if (cg == 0) s_D[warp] = Dinc;
       }
     }
@@ -754,15 +763,15 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     }
 
     // ---- pass 2: y = local scan + (run decay so far) x (state entering the run)
-    float2 tin[4];
+    float2 tin[NPR];
     {
       const float2 g0 = f2_bcast(s_G0[warp]);
-      float2 sin[4], sw[4];
-      ld_row8(s_Sin + ch, sin);
-      ld_row8(s_E + warp * BP + ch, sw);
+      float2 sin[NPR], sw[NPR];
+      ld_row<NPR>(s_Sin + ch, sin);
+      ld_row<NPR>(s_E + warp * BP + ch, sw);
       const float2 dx = f2_bcast(Dexc);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tin[q] = f2_fma(dx, f2_fma(g0, sin[q], sw[q]), Eexc[q]);
+      for (int q = 0; q < NPR; ++q) tin[q] = f2_fma(dx, f2_fma(g0, sin[q], sw[q]), Eexc[q]);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the incoming state
@@ -774,10 +783,10 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const float2 g = s_g[tix(r0 + u)];
-        float2 yv[4];
+        float2 yv[NPR];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
-        if (u < nv) store8_cs<T>(yp, yv, nch);
+        for (int q = 0; q < NPR; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
+        if (u < nv) store_grp_cs<T, NPR>(yp, yv, nch);
         yp += ystep;
       }
     }
@@ -790,8 +799,11 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct BwdCfg {
-  using Ln = Lanes<BP>;
-  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG;
+  // channels per compute lane: 4 at BP = 64 gives 16-token segments, twice
+  // the compute warps per tile, at half the registers per lane
+  static constexpr int CPL = (BP == 64) ? 4 : 8;
+  using Ln = Lanes<BP, CPL>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR;
   static constexpr int CPT = BP / 32;
   static constexpr int NW = Q / SEG;
   static constexpr int NC = NW * 32;
@@ -828,6 +840,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
                    const BwdParams p) {
   using C = BwdCfg<T, BP, Q>;
   constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
+  constexpr int CPL = C::CPL, NPR = C::NPR;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
   float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
@@ -931,8 +944,8 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   const int ts = lane / CG, cg = lane % CG;
   const int s0 = warp * SEG;
   const int r0 = s0 + ts * 8;
-  const int ch = cg * 8;
-  const int nch = min(8, p.P - ch);
+  const int ch = cg * CPL;
+  const int nch = min(CPL, p.P - ch);
   const unsigned FULL = 0xffffffffu;
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -984,28 +997,28 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     //   z  <- a_u z + w_u x_u                      (u ascending; only the end value)
     //   gc <- a_{u+1} gc + dy_u,  gl[u] = gc       (u descending; gradient from
     //                                               this run's dy only)
-    float2 gl[8][4];
+    float2 gl[8][NPR];
     float Dexc, Dsuf;
-    float2 Eexc[4], Gexc[4];
+    float2 Eexc[NPR], Gexc[NPR];
     {
-      float2 z[4], gc[4];
+      float2 z[NPR], gc[NPR];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) z[q] = gc[q] = make_float2(0.f, 0.f);
+      for (int q = 0; q < NPR; ++q) z[q] = gc[q] = make_float2(0.f, 0.f);
       float2 an = make_float2(0.f, 0.f);  // a_{u+1}; nothing beyond the run end
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 tk = s_tok[tix(r0 + i)];
-        float2 xv[4];
-        load8<T>(s_x + (r0 + i) * BP + ch, xv);
+        float2 xv[NPR];
+        load_grp<T, NPR>(s_x + (r0 + i) * BP + ch, xv);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < NPR; ++q)
           z[q] = (MODE == kBwdCumsum) ? f2_fma(make_float2(tk.x, tk.y), z[q], xv[q])
                                       : f2_fma(make_float2(tk.x, tk.y), z[q], f2_mul(make_float2(tk.z, tk.w), xv[q]));
         const int u = 7 - i;
-        float2 dv[4];
-        load8<T>(s_dy + (r0 + u) * BP + ch, dv);
+        float2 dv[NPR];
+        load_grp<T, NPR>(s_dy + (r0 + u) * BP + ch, dv);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NPR; ++q) {
           gc[q] = f2_fma(an, gc[q], dv[q]);
           gl[u][q] = gc[q];
         }
@@ -1013,19 +1026,19 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         an = make_float2(tu.x, tu.y);
       }
       // an = a at the run start: the run's dy reaches the state before it as a_r0 gc
-      float2 Rr[4];
+      float2 Rr[NPR];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) Rr[q] = f2_mul(an, gc[q]);
+      for (int q = 0; q < NPR; ++q) Rr[q] = f2_mul(an, gc[q]);
       const float Drun = an.x * s_g[tix(r0)].x;
       float Dinc, Drinc;
-      float2 Einc[4], Rinc[4];
-      runs_scan_fwd<CG, TS>(Drun, z, ts, Dinc, Einc, Dexc, Eexc);
-      runs_scan_rev<CG, TS>(Drun, Rr, ts, Drinc, Rinc, Dsuf, Gexc);
+      float2 Einc[NPR], Rinc[NPR];
+      runs_scan_fwd<CG, TS, NPR>(Drun, z, ts, Dinc, Einc, Dexc, Eexc);
+      runs_scan_rev<CG, TS, NPR>(Drun, Rr, ts, Drinc, Rinc, Dsuf, Gexc);
       if (ts == TS - 1) {
-        st_row8(s_E + warp * BP + ch, Einc);
+        st_row<NPR>(s_E + warp * BP + ch, Einc);
         if (cg == 0) s_D[warp] = Dinc;
       }
-      if (ts == 0) st_row8(s_R + warp * BP + ch, Rinc);
+      if (ts == 0) st_row<NPR>(s_R + warp * BP + ch, Rinc);
     }
     named_sync(1, NC);  // every segment's aggregates
 
@@ -1072,15 +1085,15 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     // ---- pass 2: exact gradients, first token first ---------------------------
     //   G_t = gl_t + (decay after t in the run) x (gradient at the run end)
     //   z_{t-1} runs forward from the true state before the run
-    float2 zp[4], gend[4];
+    float2 zp[NPR], gend[NPR];
     {
-      float2 zw[4], gn[4], rw[4];
-      ld_row8(s_E + warp * BP + ch, zw);
-      ld_row8(s_Gn + ch, gn);
-      ld_row8(s_R + warp * BP + ch, rw);
+      float2 zw[NPR], gn[NPR], rw[NPR];
+      ld_row<NPR>(s_E + warp * BP + ch, zw);
+      ld_row<NPR>(s_Gn + ch, gn);
+      ld_row<NPR>(s_R + warp * BP + ch, rw);
       const float2 hs = f2_bcast(s_Hs[warp]), de = f2_bcast(Dexc), ds = f2_bcast(Dsuf);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NPR; ++q) {
         zp[q] = f2_fma(de, zw[q], Eexc[q]);
         gend[q] = f2_fma(ds, f2_fma(hs, gn[q], rw[q]), Gexc[q]);
       }
@@ -1103,38 +1116,38 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         const float4 tk = s_tok[tix(t)];
         const float2 gr = s_g[tix(t)];
         const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
-        float2 G[4], dxv[4], xv[4];
+        float2 G[NPR], dxv[NPR], xv[NPR];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NPR; ++q) {
           G[q] = f2_fma(gr, gend[q], gl[u][q]);
           dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
         }
         if (dlast != nullptr && t0 + t == p.L - 1) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < NPR; ++q) {
             if (2 * q < nch) {
               dxv[q].x += dlast[ch + 2 * q];
               dxv[q].y += dlast[ch + 2 * q + 1];
             }
           }
         }
-        if (u < nv) store8_cs<T>(dxp, dxv, nch);
+        if (u < nv) store_grp_cs<T, NPR>(dxp, dxv, nch);
         dxp += dxstep;
-        load8<T>(s_x + t * BP + ch, xv);
+        load_grp<T, NPR>(s_x + t * BP + ch, xv);
         if (MODE == kBwdCumsum) {
           // dl_t = a_t sum_p G_t z_{t-1}
           float2 m = f2_mul(G[0], zp[0]);
 #pragma unroll
-          for (int q = 1; q < 4; ++q) m = f2_fma(G[q], zp[q], m);
+          for (int q = 1; q < NPR; ++q) m = f2_fma(G[q], zp[q], m);
           pr[u] = tk.x * (m.x + m.y);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
+          for (int q = 0; q < NPR; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
         } else {
           // ddt_t = sum_p G_t (x_t + A a_t z_{t-1});  dA += dt_t a_t sum_p G_t z_{t-1}
           const float2 Aa = f2_mul(A2, aa), wa = f2_mul(ww, aa);
           float2 m = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < NPR; ++q) {
             m = f2_fma(G[q], f2_fma(Aa, zp[q], xv[q]), m);
             dacc = f2_fma(wa, f2_mul(G[q], zp[q]), dacc);
             zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
@@ -1154,11 +1167,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the stage
     if (MODE == kBwdDt) {
-      // per-(tile, warp) partial of dA, summed in a fixed order by the last CTA
+      // per-(tile, warp) partial of dA, head-major so that the last CTA sums
+      // each head's partials as one contiguous run, in a fixed order
       float dap = dacc.x + dacc.y;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(FULL, dap, o);
-      if (lane == 0) ws.partial[slot * 32 + warp] = dap;
+      if (lane == 0) ws.partial[((static_cast<size_t>(h) * p.nc + c) * p.B + b) * NW + warp] = dap;
     }
   }
   named_sync(1, NC);
@@ -1166,26 +1180,28 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   named_sync(1, NC);
   if (s_last) {
     if (MODE == kBwdDt) {
-      // dA[h] = sum over (chunk, batch, warp) of the partials: warp-per-head,
-      // a fixed split over lanes and a fixed shuffle tree (deterministic);
-      // independent L2 loads, so the tail is one round trip per few rows
+      // dA[h] = sum of head h's nc * B * NW partials (contiguous): warp per
+      // head, a fixed split over lanes and a fixed shuffle tree, so the sum is
+      // deterministic.  Loads are issued eight at a time before any is used:
+      // the tail costs a few L2 round trips, not one per partial.
       __threadfence();
-      const int nbt = p.nc * p.B;
+      const int n2 = p.nc * p.B * NW / 2;
       for (int hh = warp; hh < p.H; hh += NW) {
-        float acc = 0.f;
-        for (int j = lane; j < nbt; j += 32) {
-          const int cc = j / p.B, bb = j - cc * p.B;
-          const float2* part =
-              reinterpret_cast<const float2*>(ws.partial + (static_cast<size_t>(cc) * BH + bb * p.H + hh) * 32);
+        const float2* part = reinterpret_cast<const float2*>(ws.partial + static_cast<size_t>(hh) * p.nc * p.B * NW);
+        float2 acc = make_float2(0.f, 0.f);
+        int i = lane;
+        for (; i + 7 * 32 < n2; i += 8 * 32) {
+          float2 v[8];
 #pragma unroll
-          for (int w = 0; w < NW / 2; ++w) {
-            const float2 v = __ldcg(part + w);
-            acc += v.x + v.y;
-          }
+          for (int u = 0; u < 8; ++u) v[u] = __ldcg(part + i + u * 32);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) acc = f2_add(acc, v[u]);
         }
+        for (; i < n2; i += 32) acc = f2_add(acc, __ldcg(part + i));
+        float a = acc.x + acc.y;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
-        if (lane == 0) p.dA_out[hh] = acc;
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(FULL, a, o);
+        if (lane == 0) p.dA_out[hh] = a;
       }
       named_sync(1, NC);
     }
