@@ -99,16 +99,14 @@ int block_p_for(int64_t P) {
 }
 
 // Workspace: 256-byte header | dA partials [tiles][32] f32 | aggregate records
-// [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64 | two (B,H,L) f32
-// row buffers (dt-form: dt transposed to per-(batch, head) rows, and the ddt
-// rows the backward writes before they are transposed back).
+// [tiles][BP + 1] u64 | inclusive records [tiles][BP] u64.
 struct WsLayout {
-  size_t partial, agg, incl, rows, rows2, total;
+  size_t partial, agg, incl, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-WsLayout ws_layout(int64_t tiles, int BP, int64_t row_floats) {
+WsLayout ws_layout(int64_t tiles, int BP) {
   WsLayout l;
   size_t off = static_cast<size_t>(kHdrWords) * 4;
   l.partial = off;
@@ -117,25 +115,15 @@ WsLayout ws_layout(int64_t tiles, int BP, int64_t row_floats) {
   off = align256(off + static_cast<size_t>(tiles) * (BP + 1) * 8);
   l.incl = off;
   off = align256(off + static_cast<size_t>(tiles) * BP * 8);
-  l.rows = off;
-  off = align256(off + static_cast<size_t>(row_floats) * 4);
-  l.rows2 = off;
-  off = align256(off + static_cast<size_t>(row_floats) * 4);
   l.total = off;
   return l;
 }
 
-struct RowBuffers {
-  float* rows;
-  float* rows2;
-};
-
-int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, int64_t row_floats, ScanWorkspace* out,
-                    RowBuffers* rb) {
+int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace* out) {
   if (ws == nullptr) return fail(EMA_ERR_WORKSPACE, "workspace is NULL");
   if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
     return fail(EMA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-  const WsLayout l = ws_layout(tiles, BP, row_floats);
+  const WsLayout l = ws_layout(tiles, BP);
   if (bytes < l.total)
     return fail(EMA_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu needed", bytes, l.total);
   char* base = static_cast<char*>(ws);
@@ -143,18 +131,6 @@ int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, int64_t row_f
   out->partial = reinterpret_cast<float*>(base + l.partial);
   out->agg = reinterpret_cast<uint64_t*>(base + l.agg);
   out->incl = reinterpret_cast<uint64_t*>(base + l.incl);
-  rb->rows = reinterpret_cast<float*>(base + l.rows);
-  rb->rows2 = reinterpret_cast<float*>(base + l.rows2);
-  return EMA_OK;
-}
-
-// (B, X, Y) -> (B, Y, X) float32, asynchronously on `s`.
-int launch_transpose(const float* src, float* dst, int64_t B, int64_t X, int64_t Y, cudaStream_t s) {
-  if (B > 65535) return fail(EMA_ERR_UNSUPPORTED, "transpose: batch too large");
-  dim3 grid(static_cast<unsigned>((X + 31) / 32), static_cast<unsigned>((Y + 31) / 32), static_cast<unsigned>(B));
-  transpose_f32_kernel<<<grid, dim3(32, 8), 0, s>>>(src, dst, static_cast<int>(X), static_cast<int>(Y));
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "transpose launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
 }
 
@@ -227,7 +203,7 @@ size_t ema_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t nheads, in
   if (batch <= 0 || seqlen <= 0 || nheads <= 0 || headdim <= 0 || chunk_size <= 0) return 256;
   const int BP = block_p_for(headdim) ? block_p_for(headdim) : 128;
   const int64_t nc = (seqlen + chunk_size - 1) / chunk_size;
-  return ws_layout(batch * nheads * nc, BP, batch * nheads * seqlen).total;
+  return ws_layout(batch * nheads * nc, BP).total;
 }
 
 int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
@@ -254,8 +230,7 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
 
   FwdLaunch l{};
   FwdParams& p = l.params;
-  RowBuffers rb;
-  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, a->batch * a->nheads * a->seqlen, &p.ws, &rb);
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
   if (r) return r;
   CUtensorMap mx;
   r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
@@ -269,7 +244,8 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   p.nc = static_cast<int>(nc);
   p.div_bh = make_fast_div(static_cast<uint32_t>(a->batch * a->nheads));
   p.div_h = make_fast_div(static_cast<uint32_t>(a->nheads));
-  p.rows = ref_form ? a->dA : rb.rows;
+  p.rows = a->dA;
+  p.dt = a->dt;
   p.A = a->A;
   p.seq_idx = a->seq_idx;
   p.seq_idx_type = a->seq_idx_type;
@@ -295,10 +271,6 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
-  if (dt_form) {  // per-(batch, head) contiguous rows of dt for the tile loads
-    r = launch_transpose(a->dt, rb.rows, a->batch, a->seqlen, a->nheads, l.stream);
-    if (r) return r;
-  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = fwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = fwd_dispatch_f16(l); break;
@@ -329,8 +301,7 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
 
   BwdLaunch l{};
   BwdParams& p = l.params;
-  RowBuffers rb;
-  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, a->batch * a->nheads * a->seqlen, &p.ws, &rb);
+  r = carve_workspace(a->workspace, a->workspace_bytes, tiles, BP, &p.ws);
   if (r) return r;
   CUtensorMap mx, mdy;
   r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
@@ -347,7 +318,8 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   p.nc = static_cast<int>(nc);
   p.div_bh = make_fast_div(static_cast<uint32_t>(a->batch * a->nheads));
   p.div_h = make_fast_div(static_cast<uint32_t>(a->nheads));
-  p.rows = ref_form ? a->da_cs : rb.rows;
+  p.rows = a->da_cs;
+  p.dt = a->dt;
   p.A = a->A;
   p.states = a->states;
   p.st_b = a->states_stride[0];
@@ -357,7 +329,7 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   p.d_final = a->d_final_state;
   p.d_last = a->d_last_token;
   p.dl = a->dl;
-  p.ddt_rows = rb.rows2;
+  p.ddt = a->ddt;
   p.dA_out = a->dA_out;
   p.d_init = a->d_initial_state;
   p.dx = a->dx;
@@ -373,19 +345,12 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
-  if (dt_form) {
-    r = launch_transpose(a->dt, rb.rows, a->batch, a->seqlen, a->nheads, l.stream);
-    if (r) return r;
-  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = bwd_dispatch_f16(l); break;
     default: r = bwd_dispatch_f32(l); break;
   }
-  r = map_dispatch_result(r, "ema_bwd");
-  if (r == EMA_OK && dt_form)  // ddt rows (B,H,L) -> ddt (B,L,H)
-    r = launch_transpose(rb.rows2, a->ddt, a->batch, a->nheads, a->seqlen, l.stream);
-  return r;
+  return map_dispatch_result(r, "ema_bwd");
 }
 
 int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], float* dA_cs, const int64_t cs_stride[3],

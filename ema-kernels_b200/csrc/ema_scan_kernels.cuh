@@ -97,7 +97,8 @@ struct ScanWorkspace {
 struct FwdParams {
   int B, L, H, P, nc;
   FastDiv div_bh, div_h;  // division by B*H and by H
-  const float* rows;  // (B,H,L) per-token decay rows: log2 decay dA, or dt (transposed)
+  const float* rows;  // (B,H,L) log2 decay dA (reference form)
+  const float* dt;    // (B,L,H) dt (dt form)
   const float* A;     // (H,)
   const void* seq_idx;
   int seq_idx_type;
@@ -115,14 +116,15 @@ struct FwdParams {
 struct BwdParams {
   int B, L, H, P, nc;
   FastDiv div_bh, div_h;
-  const float* rows;  // (B,H,L) per-token rows: within-chunk log2 cumsum da_cs, or dt (transposed)
+  const float* rows;  // (B,H,L) within-chunk log2 cumsum da_cs (reference form)
+  const float* dt;    // (B,L,H) dt (dt form)
   const float* A;     // (H,)
   const float* states;
   long long st_b, st_c, st_h, st_p;
   const float* d_final;  // (B,H,P)
   const float* d_last;   // (B,H,P)
   float* dl;             // (B,H,L) reference form
-  float* ddt_rows;       // (B,H,L) dt form (transposed to (B,L,H) by the launcher)
+  float* ddt;            // (B,L,H) dt form
   float* dA_out;         // (H,)
   float* d_init;         // (B,H,P)
   void* dx;                     // (B,L,H,P) output
@@ -293,6 +295,13 @@ __device__ __forceinline__ void load_row(float* dst, const float* src, int n, ui
   } else {
     for (int i = lane; i < n; i += 32) cp_async_4(dst + i, src + i);
   }
+}
+
+// Producer warp, one tile: gather `n` floats spaced `stride` apart (a column
+// of a (B, L, H) tensor) with 4-byte cp.async; the neighbouring heads' tiles
+// read the same sectors at about the same time, so DRAM sees each once.
+__device__ __forceinline__ void gather_col(float* dst, const float* src, int stride, int n, int lane) {
+  for (int i = lane; i < n; i += 32) cp_async_4(dst + i, src + static_cast<size_t>(i) * stride);
 }
 
 // Producer warp: tickets -> tiles -> loads into the ring.  `issue(s, ticket)`
@@ -589,16 +598,21 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
       unsigned char* st = smem + s * C::kStage;
       float* raw = reinterpret_cast<float*>(st + C::kX);
-      const float* src = p.rows + static_cast<size_t>(bh) * p.L + t0;
       const int n = min(Q, p.L - t0);
-      const uint32_t bulk = row_bulk_bytes(src, n);
+      const float* src = (MODE == kFwdDt) ? p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h
+                                          : p.rows + static_cast<size_t>(bh) * p.L + t0;
+      const uint32_t bulk = (MODE == kFwdDt) ? 0u : row_bulk_bytes(src, n);
       if (lane == 0) {
         s_tile[s] = ticket;
         mbar_arrive_expect_tx(&full[s], C::kX + bulk);
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
       }
-      load_row(raw, src, n, bulk, &full[s], lane);
-      if (MODE == kFwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
+      if (MODE == kFwdDt) {
+        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
+        if (lane == 0) cp_async_4(raw + Q, p.A + h);
+      } else {
+        load_row(raw, src, n, bulk, &full[s], lane);
+      }
     });
     return;
   }
@@ -896,9 +910,10 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       unsigned char* st = smem + s * C::kStage;
       float* raw = reinterpret_cast<float*>(st + C::oRaw);
       float* sst = reinterpret_cast<float*>(st + C::oSt);
-      const float* src = p.rows + static_cast<size_t>(bh) * p.L + t0;
       const int n = min(Q, p.L - t0);
-      const uint32_t bulk = row_bulk_bytes(src, n);
+      const float* src = (MODE == kBwdDt) ? p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h
+                                          : p.rows + static_cast<size_t>(bh) * p.L + t0;
+      const uint32_t bulk = (MODE == kBwdDt) ? 0u : row_bulk_bytes(src, n);
       const float* srow = p.states + b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h;
       const uint32_t sbulk = (p.st_p == 1) ? row_bulk_bytes(srow, p.P) : 0u;
       if (lane == 0) {
@@ -907,8 +922,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
         tma_load_4d(st + C::kX, &tm_dy, &full[s], 0, h, t0, b);
       }
-      load_row(raw, src, n, bulk, &full[s], lane);
-      if (MODE == kBwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
+      if (MODE == kBwdDt) {
+        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
+        if (lane == 0) cp_async_4(raw + Q, p.A + h);
+      } else {
+        load_row(raw, src, n, bulk, &full[s], lane);
+      }
       if (sbulk) {
         if (lane == 0) bulk_g2s(sst, srow, sbulk, &full[s]);
       } else {
@@ -1160,7 +1179,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         const int gt = t0 + r0 + cg;
         if (gt < p.L) {
           if (MODE == kBwdCumsum) p.dl[static_cast<size_t>(bh) * p.L + gt] = Pr;
-          else p.ddt_rows[static_cast<size_t>(bh) * p.L + gt] = Pr;
+          else p.ddt[(static_cast<size_t>(b) * p.L + gt) * p.H + h] = Pr;
         }
       }
     }
@@ -1206,30 +1225,6 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       named_sync(1, NC);
     }
     if (tid == 0) reset_counters(ws, epoch, total);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// (B, X, Y) -> (B, Y, X) float32 transpose through 32x32 shared-memory tiles
-// (per-token rows for the scan kernels: dt (B,L,H) <-> rows (B,H,L)).
-// ---------------------------------------------------------------------------
-static __global__ void __launch_bounds__(256) transpose_f32_kernel(const float* __restrict__ src, float* __restrict__ dst,
-                                                            int X, int Y) {
-  __shared__ float tile[32][33];
-  const int b = blockIdx.z;
-  const int x0 = blockIdx.x * 32, y0 = blockIdx.y * 32;
-  const float* s = src + static_cast<size_t>(b) * X * Y;
-  float* d = dst + static_cast<size_t>(b) * X * Y;
-#pragma unroll
-  for (int r = threadIdx.y; r < 32; r += 8) {
-    const int x = x0 + r, y = y0 + threadIdx.x;
-    if (x < X && y < Y) tile[r][threadIdx.x] = s[static_cast<size_t>(x) * Y + y];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int r = threadIdx.y; r < 32; r += 8) {
-    const int y = y0 + r, x = x0 + threadIdx.x;
-    if (x < X && y < Y) d[static_cast<size_t>(y) * X + x] = tile[threadIdx.x][r];
   }
 }
 
