@@ -507,6 +507,86 @@ __device__ __forceinline__ void ld_row(const float* src, float2 (&v)[NPR]) {
   }
 }
 
+// Per-segment rows of channel values (s_E, s_R) are padded by 4 floats: the
+// chain below reads one channel of every segment at once, and unpadded rows
+// of BP floats would put all of them in one bank.
+constexpr int kRowPad = 4;
+
+// Chain the NW segments of a tile: thread c < BP runs channel c's chain over
+// the segments.  All of the chain's shared-memory operands are loaded before
+// the first FMA, so the chain costs NW dependent FMAs, not NW load latencies.
+//
+// Forward chain.  In: s_E[q][c] = end state of segment q from a zero start,
+// s_D[q] = its decay.  Out: s_E[q][c] = state before segment q from the tile
+// start state s0 (zero when s0 is null), s_G0[q] = decay from the tile start
+// to segment q, s_Et[c] / *Gd = the tile's end state from zero and its decay;
+// `agg` (if non-null) receives them as tagged words.
+template <int BP, int NW>
+__device__ __forceinline__ void chain_segments_fwd(float* s_E, const float* s_D, float* s_G0, float* s_Et,
+                                                   float* Gd, const float* s0, int P, uint64_t* agg, uint32_t tag,
+                                                   int tid) {
+  if (tid >= BP) return;
+  constexpr int RS = BP + kRowPad;
+  float e[NW], d[NW];
+#pragma unroll
+  for (int q = 0; q < NW; ++q) {
+    e[q] = s_E[q * RS + tid];
+    d[q] = s_D[q];
+  }
+  float Sv = (s0 != nullptr && tid < P) ? s0[tid] : 0.f, Z = 0.f, G = 1.f;
+#pragma unroll
+  for (int q = 0; q < NW; ++q) {
+    const float before = Sv;
+    if (tid == 0 && s_G0 != nullptr) s_G0[q] = G;
+    Sv = fmaf(d[q], Sv, e[q]);
+    Z = fmaf(d[q], Z, e[q]);
+    G *= d[q];
+    e[q] = before;
+  }
+#pragma unroll
+  for (int q = 0; q < NW; ++q) s_E[q * RS + tid] = e[q];
+  if (s_Et != nullptr) s_Et[tid] = Z;
+  if (tid == 0) *Gd = G;
+  if (agg != nullptr) {
+    st_relaxed_u64(agg + tid, tag_word(Z, tag));
+    if (tid == 0) st_relaxed_u64(agg + BP, tag_word(G, tag));
+  }
+}
+// Reverse chain.  In: s_R[q][c] = what segment q's own dy contributes to the
+// gradient of the state before it, s_D[q] its decay.  Out: s_R[q][c] = the
+// gradient w.r.t. z at the end of segment q from later segments of the tile,
+// s_Hs[q] = decay of the segments after q, s_Rt[c] / *Hd = the tile's total
+// and its decay; `agg` as above.
+template <int BP, int NW>
+__device__ __forceinline__ void chain_segments_rev(float* s_R, const float* s_D, float* s_Hs, float* s_Rt,
+                                                   float* Hd, uint64_t* agg, uint32_t tag, int tid) {
+  if (tid >= BP) return;
+  constexpr int RS = BP + kRowPad;
+  float r[NW], d[NW];
+#pragma unroll
+  for (int q = 0; q < NW; ++q) {
+    r[q] = s_R[q * RS + tid];
+    d[q] = s_D[q];
+  }
+  float g = 0.f, H = 1.f;
+#pragma unroll
+  for (int q = NW - 1; q >= 0; --q) {
+    const float after = g;
+    if (tid == 0) s_Hs[q] = H;
+    g = fmaf(d[q], g, r[q]);
+    H *= d[q];
+    r[q] = after;
+  }
+#pragma unroll
+  for (int q = 0; q < NW; ++q) s_R[q * RS + tid] = r[q];
+  s_Rt[tid] = g;
+  if (tid == 0) *Hd = H;
+  if (agg != nullptr) {
+    st_relaxed_u64(agg + tid, tag_word(g, tag));
+    if (tid == 0) st_relaxed_u64(agg + BP, tag_word(H, tag));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
@@ -526,8 +606,8 @@ struct FwdCfg {
   static constexpr int oTok = 0;                              // float4[tix]  (a, a, w, w)
   static constexpr int oG = oTok + tix_size(Q) * 16;          // float2[tix]  decay from the run start through t
   static constexpr int oL2 = oG + tix_size(Q) * 8;            // float[Q]     log2 decay
-  static constexpr int oE = align_up(oL2 + Q * 4, 16);        // float[NW][BP]
-  static constexpr int oD = oE + NW * BP * 4;                 // float[NW]
+  static constexpr int oE = align_up(oL2 + Q * 4, 16);        // float[NW][BP + pad]
+  static constexpr int oD = oE + NW * (BP + kRowPad) * 4;     // float[NW]
   static constexpr int oG0 = oD + NW * 4;                     // float[NW]
   static constexpr int oSin = align_up(oG0 + NW * 4, 16);     // float[2][BP]  from the look-back warp
   static constexpr int oEt = oSin + 2 * BP * 4;               // float[BP]
@@ -733,7 +813,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       float2 Einc[NPR];
       runs_scan_fwd<CG, TS, NPR>(s_g[tix(r0 + 7)].x, z, ts, Dinc, Einc, Dexc, Eexc);
       if (ts == TS - 1) {
-        st_row<NPR>(s_E + warp * BP + ch, Einc);  // the segment's end state from zero
+        st_row<NPR>(s_E + warp * (BP + kRowPad) + ch, Einc);  // the segment's end state from zero
         if (cg == 0) s_D[warp] = Dinc;
       }
     }
@@ -743,24 +823,8 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 
     // ---- chain the segments; publish the tile aggregate ---------------------
     const bool has_succ = (c + 1 < p.nc);
-    if (tid < BP) {
-      float Sv = 0.f, Gd = 1.f;
-#pragma unroll
-      for (int q = 0; q < NW; ++q) {
-        const float e = s_E[q * BP + tid];
-        s_E[q * BP + tid] = Sv;  // state before segment q (zero tile input)
-        if (tid == 0) s_G0[q] = Gd;
-        Sv = fmaf(s_D[q], Sv, e);
-        Gd *= s_D[q];
-      }
-      s_Et[tid] = Sv;
-      if (tid == 0) s_misc[0] = Gd;
-      if (c > 0 && has_succ) {
-        uint64_t* agg = ws.agg + slot * (BP + 1);
-        st_relaxed_u64(agg + tid, tag_word(Sv, tag));
-        if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Gd, tag));
-      }
-    }
+    chain_segments_fwd<BP, NW>(s_E, s_D, s_G0, s_Et, &s_misc[0], nullptr, p.P,
+                               (c > 0 && has_succ) ? ws.agg + slot * (BP + 1) : nullptr, tag, tid);
     if (warp == NW - 1 && !mbar_wait_bounded(&vec_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
     named_sync(1, NC);  // chained segments + the state entering the tile
     if (s_fail) break;
@@ -782,7 +846,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       const float2 g0 = f2_bcast(s_G0[warp]);
       float2 sin[NPR], sw[NPR];
       ld_row<NPR>(s_Sin + ch, sin);
-      ld_row<NPR>(s_E + warp * BP + ch, sw);
+      ld_row<NPR>(s_E + warp * (BP + kRowPad) + ch, sw);
       const float2 dx = f2_bcast(Dexc);
 #pragma unroll
       for (int q = 0; q < NPR; ++q) tin[q] = f2_fma(dx, f2_fma(g0, sin[q], sw[q]), Eexc[q]);
@@ -831,9 +895,9 @@ struct BwdCfg {
   static constexpr int kStage = align_up(oSt + BP * 4, 128);
   static constexpr int oTok = 0;                           // float4[tix]  (a, a, w, w)
   static constexpr int oG = oTok + tix_size(Q) * 16;       // float2[tix]  decay after t through the run end
-  static constexpr int oE = align_up(oG + tix_size(Q) * 8, 16);  // float[NW][BP]  forward prefix -> Zin
-  static constexpr int oR = oE + NW * BP * 4;              // float[NW][BP]  reverse aggregate -> Rloc
-  static constexpr int oD = oR + NW * BP * 4;              // float[NW]
+  static constexpr int oE = align_up(oG + tix_size(Q) * 8, 16);  // float[NW][BP + pad]  forward prefix -> Zin
+  static constexpr int oR = oE + NW * (BP + kRowPad) * 4;  // float[NW][BP + pad]  reverse aggregate -> Rloc
+  static constexpr int oD = oR + NW * (BP + kRowPad) * 4;  // float[NW]
   static constexpr int oHs = oD + NW * 4;                  // float[NW]
   static constexpr int oGn = align_up(oHs + NW * 4, 16);   // float[2][BP]  from the look-back warp
   static constexpr int oRt = oGn + 2 * BP * 4;             // float[BP]
@@ -1054,40 +1118,18 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       runs_scan_fwd<CG, TS, NPR>(Drun, z, ts, Dinc, Einc, Dexc, Eexc);
       runs_scan_rev<CG, TS, NPR>(Drun, Rr, ts, Drinc, Rinc, Dsuf, Gexc);
       if (ts == TS - 1) {
-        st_row<NPR>(s_E + warp * BP + ch, Einc);
+        st_row<NPR>(s_E + warp * (BP + kRowPad) + ch, Einc);
         if (cg == 0) s_D[warp] = Dinc;
       }
-      if (ts == 0) st_row<NPR>(s_R + warp * BP + ch, Rinc);
+      if (ts == 0) st_row<NPR>(s_R + warp * (BP + kRowPad) + ch, Rinc);
     }
     named_sync(1, NC);  // every segment's aggregates
 
-    // ---- chain segments: Zin (forward) and Rloc (reverse); publish ----------
+    // ---- chain segments: Zin (forward, true states) and Rloc (reverse); publish
     const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
-    if (tid < BP) {
-      float Sv = (tid < p.P) ? s_Sin[tid] : 0.f;
-#pragma unroll
-      for (int q = 0; q < NW; ++q) {
-        const float e = s_E[q * BP + tid];
-        s_E[q * BP + tid] = Sv;  // true state before segment q
-        Sv = fmaf(s_D[q], Sv, e);
-      }
-      float r = 0.f, Hd = 1.f;
-#pragma unroll
-      for (int q = NW - 1; q >= 0; --q) {
-        const float rr = s_R[q * BP + tid];
-        s_R[q * BP + tid] = r;  // gradient w.r.t. z at the segment end, from later segments
-        if (tid == 0) s_Hs[q] = Hd;
-        r = fmaf(s_D[q], r, rr);
-        Hd *= s_D[q];
-      }
-      s_Rt[tid] = r;  // gradient w.r.t. the state entering the tile, from this tile's dy
-      if (tid == 0) s_misc[0] = Hd;
-      if (c + 1 < p.nc && has_succ) {
-        uint64_t* agg = ws.agg + slot * (BP + 1);
-        st_relaxed_u64(agg + tid, tag_word(r, tag));
-        if (tid == 0) st_relaxed_u64(agg + BP, tag_word(Hd, tag));
-      }
-    }
+    chain_segments_fwd<BP, NW>(s_E, s_D, nullptr, nullptr, &s_misc[1], s_Sin, p.P, nullptr, 0u, tid);
+    chain_segments_rev<BP, NW>(s_R, s_D, s_Hs, s_Rt, &s_misc[0],
+                               (c + 1 < p.nc && has_succ) ? ws.agg + slot * (BP + 1) : nullptr, tag, tid);
     if (warp == NW - 1 && !mbar_wait_bounded(&vec_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
     named_sync(1, NC);  // chained segments + the gradient arriving at the tile end
     if (s_fail) break;
@@ -1107,9 +1149,9 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     float2 zp[NPR], gend[NPR];
     {
       float2 zw[NPR], gn[NPR], rw[NPR];
-      ld_row<NPR>(s_E + warp * BP + ch, zw);
+      ld_row<NPR>(s_E + warp * (BP + kRowPad) + ch, zw);
       ld_row<NPR>(s_Gn + ch, gn);
-      ld_row<NPR>(s_R + warp * BP + ch, rw);
+      ld_row<NPR>(s_R + warp * (BP + kRowPad) + ch, rw);
       const float2 hs = f2_bcast(s_Hs[warp]), de = f2_bcast(Dexc), ds = f2_bcast(Dsuf);
 #pragma unroll
       for (int q = 0; q < NPR; ++q) {
