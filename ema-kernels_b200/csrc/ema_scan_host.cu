@@ -211,7 +211,9 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   int r = check_shape(a->batch, a->seqlen, a->nheads, a->headdim, a->chunk_size, a->dtype);
   if (r) return r;
   if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
-  if (a->x == nullptr || a->out == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "x and out are required");
+  if (a->x == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "x is required");
+  if (a->out == nullptr && a->final_state == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "out is required (a state-only forward needs final_state)");
   const bool ref_form = a->dA != nullptr;
   const bool dt_form = a->dt != nullptr || a->A != nullptr;
   if (ref_form == dt_form || (dt_form && (a->dt == nullptr || a->A == nullptr)))
@@ -235,8 +237,10 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   CUtensorMap mx;
   r = make_tile_map(&mx, a->x, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->x_stride, BP, Q, "x");
   if (r) return r;
-  r = check_tile_tensor(a->out, a->dtype, a->out_stride, "out");
-  if (r) return r;
+  if (a->out != nullptr) {
+    r = check_tile_tensor(a->out, a->dtype, a->out_stride, "out");
+    if (r) return r;
+  }
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);
   p.H = static_cast<int>(a->nheads);
@@ -284,14 +288,18 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   int r = check_shape(a->batch, a->seqlen, a->nheads, a->headdim, a->chunk_size, a->dtype);
   if (r) return r;
   if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
-  if (a->x == nullptr || a->dout == nullptr || a->dx == nullptr || a->states == nullptr)
-    return fail(EMA_ERR_INVALID_ARGUMENT, "x, dout, dx and states are required");
+  if (a->x == nullptr || a->dout == nullptr || a->states == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "x, dout and states are required");
+  const bool state_only = a->dx == nullptr;
+  if (state_only && a->d_initial_state == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "dx is required (a state-only backward needs d_initial_state)");
   const bool ref_form = a->da_cs != nullptr;
   const bool dt_form = a->dt != nullptr || a->A != nullptr;
   if (ref_form == dt_form || (dt_form && (a->dt == nullptr || a->A == nullptr)))
     return fail(EMA_ERR_INVALID_ARGUMENT, "give either da_cs, or both dt and A");
-  if (ref_form && a->dl == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "dl output is required with da_cs");
-  if (dt_form && (a->ddt == nullptr || a->dA_out == nullptr))
+  if (!state_only && ref_form && a->dl == nullptr)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "dl output is required with da_cs");
+  if (!state_only && dt_form && (a->ddt == nullptr || a->dA_out == nullptr))
     return fail(EMA_ERR_INVALID_ARGUMENT, "ddt and dA_out outputs are required with dt/A");
 
   const int Q = static_cast<int>(a->chunk_size);
@@ -309,8 +317,10 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   r = make_tile_map(&mdy, a->dout, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dout_stride, BP,
                     Q, "dout");
   if (r) return r;
-  r = check_tile_tensor(a->dx, a->dtype, a->dx_stride, "dx");
-  if (r) return r;
+  if (!state_only) {
+    r = check_tile_tensor(a->dx, a->dtype, a->dx_stride, "dx");
+    if (r) return r;
+  }
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);
   p.H = static_cast<int>(a->nheads);

@@ -94,6 +94,13 @@ struct ScanWorkspace {
   uint64_t* incl;  // [tiles][BP] inclusive words
 };
 
+// A ring stage's tile, decoded once by the producer for the compute warps.
+struct __align__(16) TileInfo {
+  int c, b, h, t0;      // chunk, batch, head, first token
+  int bh, pad0;         // batch * H + head
+  long long out_off;    // element offset of (b, t0, h, 0) in the (B, L, H, P) output
+};
+
 struct FwdParams {
   int B, L, H, P, nc;
   FastDiv div_bh, div_h;  // division by B*H and by H
@@ -613,7 +620,8 @@ struct FwdCfg {
   static constexpr int oEt = oSin + 2 * BP * 4;               // float[BP]
   static constexpr int oMisc = oEt + BP * 4;                  // float[32]
   static constexpr int oTile = oMisc + 32 * 4;                // int[kMaxStages]
-  static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);  // full, empty, tid_full, vec_full/empty
+  static constexpr int oInfo = align_up(oTile + kMaxStages * 4, 16);  // TileInfo[kMaxStages]
+  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));  // full, empty, tid_full, vec_full/empty
   static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
   using R = Ring<kStage, kPriv>;
   static constexpr int S = R::S;
@@ -640,6 +648,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   float* s_Et = reinterpret_cast<float*>(priv + C::oEt);
   float* s_misc = reinterpret_cast<float*>(priv + C::oMisc);
   int* s_tile = reinterpret_cast<int*>(priv + C::oTile);
+  TileInfo* s_info = reinterpret_cast<TileInfo*>(priv + C::oInfo);
   uint64_t* full = reinterpret_cast<uint64_t*>(priv + C::oBar);
   uint64_t* empty = full + kMaxStages;
   uint64_t* tid_full = empty + kMaxStages;
@@ -684,6 +693,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       const uint32_t bulk = (MODE == kFwdDt) ? 0u : row_bulk_bytes(src, n);
       if (lane == 0) {
         s_tile[s] = ticket;
+        s_info[s] = TileInfo{c, b, h, t0, bh, 0, b * p.sy_b + static_cast<long long>(t0) * p.sy_l + h * p.sy_h};
         mbar_arrive_expect_tx(&full[s], C::kX + bulk);
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
       }
@@ -726,13 +736,17 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   const int ch = cg * CPL;        // this lane's channel group
   const int nch = min(CPL, p.P - ch);  // valid channels of the group (P is a multiple of 4)
   const unsigned FULL = 0xffffffffu;
+  // this run's per-token entries: r0 is a multiple of 8, so tix(r0 + u) = tix(r0) + u
+  const float4* tok_r = s_tok + tix(r0);
+  const float2* g_r = s_g + tix(r0);
+  const long long lane_off = static_cast<long long>(r0) * p.sy_l + ch;  // within a tile's output
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!compute_wait(&full[s], (k / S) & 1, status, warp, NC, &s_fail)) break;
     const int tile = s_tile[s];
     if (tile < 0) break;
-    const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
-    const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
+    const TileInfo ti = s_info[s];
+    const int c = ti.c, bh = ti.bh, b = ti.b, h = ti.h, t0 = ti.t0;
     const size_t slot = static_cast<size_t>(tile);
     const T* s_x = reinterpret_cast<const T*>(smem + s * C::kStage);
     const float* raw = reinterpret_cast<const float*>(smem + s * C::kStage + C::kX);
@@ -790,6 +804,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     __syncwarp();
 
     // ---- pass 1: local scan of the run from zero, kept in registers -----------
+    const T* x_r = s_x + r0 * BP + ch;
     float2 zl[8][NPR];
     float Dexc;
     float2 Eexc[NPR];
@@ -799,10 +814,10 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       for (int q = 0; q < NPR; ++q) z[q] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float4 tk = s_tok[tix(r0 + u)];
+        const float4 tk = tok_r[u];
         const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
         float2 xv[NPR];
-        load_grp<T, NPR>(s_x + (r0 + u) * BP + ch, xv);
+        load_grp<T, NPR>(x_r + u * BP, xv);
 #pragma unroll
         for (int q = 0; q < NPR; ++q) {
           z[q] = (MODE == kFwdLog2) ? f2_fma(aa, z[q], xv[q]) : f2_fma(aa, z[q], f2_mul(ww, xv[q]));
@@ -811,7 +826,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       }
       float Dinc;
       float2 Einc[NPR];
-      runs_scan_fwd<CG, TS, NPR>(s_g[tix(r0 + 7)].x, z, ts, Dinc, Einc, Dexc, Eexc);
+      runs_scan_fwd<CG, TS, NPR>(g_r[7].x, z, ts, Dinc, Einc, Dexc, Eexc);
       if (ts == TS - 1) {
         st_row<NPR>(s_E + warp * (BP + kRowPad) + ch, Einc);  // the segment's end state from zero
         if (cg == 0) s_D[warp] = Dinc;
@@ -853,14 +868,14 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the incoming state
-    {
+    if (p.y != nullptr) {  // (a state-only pass computes just the chunk and final states)
       // running row pointer: one 64-bit add per token
-      T* yp = static_cast<T*>(p.y) + b * p.sy_b + static_cast<long long>(t0 + r0) * p.sy_l + h * p.sy_h + ch;
+      T* yp = static_cast<T*>(p.y) + ti.out_off + lane_off;
       const long long ystep = p.sy_l;
       const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float2 g = s_g[tix(r0 + u)];
+        const float2 g = g_r[u];
         float2 yv[NPR];
 #pragma unroll
         for (int q = 0; q < NPR; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
@@ -903,7 +918,8 @@ struct BwdCfg {
   static constexpr int oRt = oGn + 2 * BP * 4;             // float[BP]
   static constexpr int oMisc = oRt + BP * 4;               // float[8]
   static constexpr int oTile = oMisc + 8 * 4;              // int[kMaxStages]
-  static constexpr int oBar = align_up(oTile + kMaxStages * 4, 16);  // full, empty, tid_full, vec_full/empty
+  static constexpr int oInfo = align_up(oTile + kMaxStages * 4, 16);  // TileInfo[kMaxStages]
+  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));  // full, empty, tid_full, vec_full/empty
   static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
   using R = Ring<kStage, kPriv>;
   static constexpr int S = R::S;
@@ -931,6 +947,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   float* s_Rt = reinterpret_cast<float*>(priv + C::oRt);
   float* s_misc = reinterpret_cast<float*>(priv + C::oMisc);
   int* s_tile = reinterpret_cast<int*>(priv + C::oTile);
+  TileInfo* s_info = reinterpret_cast<TileInfo*>(priv + C::oInfo);
   uint64_t* full = reinterpret_cast<uint64_t*>(priv + C::oBar);
   uint64_t* empty = full + kMaxStages;
   uint64_t* tid_full = empty + kMaxStages;
@@ -982,6 +999,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       const uint32_t sbulk = (p.st_p == 1) ? row_bulk_bytes(srow, p.P) : 0u;
       if (lane == 0) {
         s_tile[s] = c * BH + bh;
+        s_info[s] = TileInfo{c, b, h, t0, bh, 0, b * p.sdx_b + static_cast<long long>(t0) * p.sdx_l + h * p.sdx_h};
         mbar_arrive_expect_tx(&full[s], 2 * C::kX + bulk + sbulk);
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
         tma_load_4d(st + C::kX, &tm_dy, &full[s], 0, h, t0, b);
@@ -1030,13 +1048,17 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   const int ch = cg * CPL;
   const int nch = min(CPL, p.P - ch);
   const unsigned FULL = 0xffffffffu;
+  // this run's per-token entries: r0 is a multiple of 8, so tix(r0 + u) = tix(r0) + u
+  const float4* tok_r = s_tok + tix(r0);
+  const float2* g_r = s_g + tix(r0);
+  const long long lane_off = static_cast<long long>(r0) * p.sdx_l + ch;  // within a tile's dx
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!compute_wait(&full[s], (k / S) & 1, status, warp, NC, &s_fail)) break;
     const int tile = s_tile[s];
     if (tile < 0) break;
-    const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
-    const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
+    const TileInfo ti = s_info[s];
+    const int c = ti.c, bh = ti.bh, b = ti.b, h = ti.h, t0 = ti.t0;
     const size_t slot = static_cast<size_t>(tile);
     const unsigned char* st = smem + s * C::kStage;
     const T* s_x = reinterpret_cast<const T*>(st);
@@ -1080,6 +1102,8 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     //   z  <- a_u z + w_u x_u                      (u ascending; only the end value)
     //   gc <- a_{u+1} gc + dy_u,  gl[u] = gc       (u descending; gradient from
     //                                               this run's dy only)
+    const T* x_r = s_x + r0 * BP + ch;
+    const T* dy_r = s_dy + r0 * BP + ch;
     float2 gl[8][NPR];
     float Dexc, Dsuf;
     float2 Eexc[NPR], Gexc[NPR];
@@ -1090,29 +1114,29 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       float2 an = make_float2(0.f, 0.f);  // a_{u+1}; nothing beyond the run end
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 tk = s_tok[tix(r0 + i)];
+        const float4 tk = tok_r[i];
         float2 xv[NPR];
-        load_grp<T, NPR>(s_x + (r0 + i) * BP + ch, xv);
+        load_grp<T, NPR>(x_r + i * BP, xv);
 #pragma unroll
         for (int q = 0; q < NPR; ++q)
           z[q] = (MODE == kBwdCumsum) ? f2_fma(make_float2(tk.x, tk.y), z[q], xv[q])
                                       : f2_fma(make_float2(tk.x, tk.y), z[q], f2_mul(make_float2(tk.z, tk.w), xv[q]));
         const int u = 7 - i;
         float2 dv[NPR];
-        load_grp<T, NPR>(s_dy + (r0 + u) * BP + ch, dv);
+        load_grp<T, NPR>(dy_r + u * BP, dv);
 #pragma unroll
         for (int q = 0; q < NPR; ++q) {
           gc[q] = f2_fma(an, gc[q], dv[q]);
           gl[u][q] = gc[q];
         }
-        const float4 tu = s_tok[tix(r0 + u)];
+        const float4 tu = tok_r[u];
         an = make_float2(tu.x, tu.y);
       }
       // an = a at the run start: the run's dy reaches the state before it as a_r0 gc
       float2 Rr[NPR];
 #pragma unroll
       for (int q = 0; q < NPR; ++q) Rr[q] = f2_mul(an, gc[q]);
-      const float Drun = an.x * s_g[tix(r0)].x;
+      const float Drun = an.x * g_r[0].x;
       float Dinc, Drinc;
       float2 Einc[NPR], Rinc[NPR];
       runs_scan_fwd<CG, TS, NPR>(Drun, z, ts, Dinc, Einc, Dexc, Eexc);
@@ -1162,72 +1186,82 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     __syncwarp();
     if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the arriving gradient
     float2 dacc = make_float2(0.f, 0.f);  // dt form: sum over this lane's tokens of dt a G z_{t-1}
-    {
-      const float* dlast = (p.d_last != nullptr && t0 + Q >= p.L) ? p.d_last + static_cast<size_t>(bh) * p.P
-                                                                 : nullptr;
-      // running row pointer: one 64-bit add per token
-      const long long dxstep = p.sdx_l;
-      T* dxp = static_cast<T*>(p.dx) + b * p.sdx_b + static_cast<long long>(t0 + r0) * dxstep + h * p.sdx_h + ch;
-      const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
-      const float2 A2 = f2_bcast(Ah);
-      float pr[8];
+    if (p.dx != nullptr) {  // (a state-only pass computes just the gradient at the span start)
+      {
+        // running row pointer: one 64-bit add per token
+        const long long dxstep = p.sdx_l;
+        T* const dx_r = static_cast<T*>(p.dx) + ti.out_off + lane_off;
+        T* dxp = dx_r;
+        const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
+        const float2 A2 = f2_bcast(Ah);
+        float pr[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int t = r0 + u;
-        const float4 tk = s_tok[tix(t)];
-        const float2 gr = s_g[tix(t)];
-        const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
-        float2 G[NPR], dxv[NPR], xv[NPR];
-#pragma unroll
-        for (int q = 0; q < NPR; ++q) {
-          G[q] = f2_fma(gr, gend[q], gl[u][q]);
-          dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
-        }
-        if (dlast != nullptr && t0 + t == p.L - 1) {
+        for (int u = 0; u < 8; ++u) {
+          const float4 tk = tok_r[u];
+          const float2 gr = g_r[u];
+          const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
+          float2 G[NPR], dxv[NPR], xv[NPR];
 #pragma unroll
           for (int q = 0; q < NPR; ++q) {
-            if (2 * q < nch) {
-              dxv[q].x += dlast[ch + 2 * q];
-              dxv[q].y += dlast[ch + 2 * q + 1];
+            G[q] = f2_fma(gr, gend[q], gl[u][q]);
+            dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
+          }
+          if (u < nv) store_grp_cs<T, NPR>(dxp, dxv, nch);
+          dxp += dxstep;
+          load_grp<T, NPR>(x_r + u * BP, xv);
+          if (MODE == kBwdCumsum) {
+            // dl_t = a_t sum_p G_t z_{t-1}
+            float2 m = f2_mul(G[0], zp[0]);
+#pragma unroll
+            for (int q = 1; q < NPR; ++q) m = f2_fma(G[q], zp[q], m);
+            pr[u] = tk.x * (m.x + m.y);
+#pragma unroll
+            for (int q = 0; q < NPR; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
+          } else {
+            // ddt_t = sum_p G_t (x_t + A a_t z_{t-1});  dA += dt_t a_t sum_p G_t z_{t-1}
+            const float2 Aa = f2_mul(A2, aa), wa = f2_mul(ww, aa);
+            float2 m = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < NPR; ++q) {
+              m = f2_fma(G[q], f2_fma(Aa, zp[q], xv[q]), m);
+              dacc = f2_fma(wa, f2_mul(G[q], zp[q]), dacc);
+              zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
             }
+            pr[u] = m.x + m.y;
           }
         }
-        if (u < nv) store_grp_cs<T, NPR>(dxp, dxv, nch);
-        dxp += dxstep;
-        load_grp<T, NPR>(s_x + t * BP + ch, xv);
-        if (MODE == kBwdCumsum) {
-          // dl_t = a_t sum_p G_t z_{t-1}
-          float2 m = f2_mul(G[0], zp[0]);
+        // the last token's extra gradient is added to the stored dx, as the
+        // reference does after its kernel (dx[:, -1] += d_ox_state)
+        if (p.d_last != nullptr && nv > 0) {
+          const int ul = p.L - 1 - (t0 + r0);
+          if (ul < 8) {
+            T* q_dx = dx_r + ul * dxstep;
+            const float* dl = p.d_last + static_cast<size_t>(bh) * p.P + ch;
+            float2 v[NPR];
+            load_grp<T, NPR>(q_dx, v);
 #pragma unroll
-          for (int q = 1; q < NPR; ++q) m = f2_fma(G[q], zp[q], m);
-          pr[u] = tk.x * (m.x + m.y);
-#pragma unroll
-          for (int q = 0; q < NPR; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
-        } else {
-          // ddt_t = sum_p G_t (x_t + A a_t z_{t-1});  dA += dt_t a_t sum_p G_t z_{t-1}
-          const float2 Aa = f2_mul(A2, aa), wa = f2_mul(ww, aa);
-          float2 m = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int q = 0; q < NPR; ++q) {
-            m = f2_fma(G[q], f2_fma(Aa, zp[q], xv[q]), m);
-            dacc = f2_fma(wa, f2_mul(G[q], zp[q]), dacc);
-            zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
+            for (int q = 0; q < NPR; ++q) {
+              if (2 * q < nch) {
+                v[q].x += dl[2 * q];
+                v[q].y += dl[2 * q + 1];
+              }
+            }
+            store_grp_cs<T, NPR>(q_dx, v, nch);
           }
-          pr[u] = m.x + m.y;
         }
-      }
-      const float Pr = group_reduce8<CG>(pr, cg);
-      if (cg < 8) {
-        const int gt = t0 + r0 + cg;
-        if (gt < p.L) {
-          if (MODE == kBwdCumsum) p.dl[static_cast<size_t>(bh) * p.L + gt] = Pr;
-          else p.ddt[(static_cast<size_t>(b) * p.L + gt) * p.H + h] = Pr;
+        const float Pr = group_reduce8<CG>(pr, cg);
+        if (cg < 8) {
+          const int gt = t0 + r0 + cg;
+          if (gt < p.L) {
+            if (MODE == kBwdCumsum) p.dl[static_cast<size_t>(bh) * p.L + gt] = Pr;
+            else p.ddt[(static_cast<size_t>(b) * p.L + gt) * p.H + h] = Pr;
+          }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the stage
-    if (MODE == kBwdDt) {
+    if (MODE == kBwdDt && p.dx != nullptr) {
       // per-(tile, warp) partial of dA, head-major so that the last CTA sums
       // each head's partials as one contiguous run, in a fixed order
       float dap = dacc.x + dacc.y;
@@ -1240,7 +1274,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
   named_sync(1, NC);
   if (s_last) {
-    if (MODE == kBwdDt) {
+    if (MODE == kBwdDt && p.dx != nullptr) {
       // dA[h] = sum of head h's nc * B * NW partials (contiguous): warp per
       // head, a fixed split over lanes and a fixed shuffle tree, so the sum is
       // deterministic.  Loads are issued eight at a time before any is used:

@@ -43,18 +43,26 @@ def _check_inputs(x, dt, A, chunk_size):
 
 def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
                        initial_states: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                       return_final_states: bool = False):
-    """Forward.  Returns (y, chunk_start_states (B, nchunks, H, P) fp32, final_states or None)."""
+                       return_final_states: bool = False, state_only: bool = False):
+    """Forward.  Returns (y, chunk_start_states (B, nchunks, H, P) fp32, final_states or None).
+
+    ``state_only``: compute only the final state (y and the chunk states are not
+    written; returns (None, None, final)) -- the first pass of the sequence-
+    parallel forward, which reads x once and writes nothing else."""
     B, L, H, P = _check_inputs(x, dt, A, chunk_size)
     dev = x.device
     nc = -(-L // chunk_size)
     x_k = _lib.tma_ready(x)
     dt_k = dt.to(torch.float32).contiguous()
     A_k = A.to(torch.float32).contiguous()
-    if out is None:
+    if state_only:
+        assert out is None, "state_only writes no output"
+        return_final_states = True
+    elif out is None:
         out = torch.empty_like(x, memory_format=torch.contiguous_format)
-    assert out.shape == x.shape and out.dtype == x.dtype and _lib.tma_ok(out), "out must match x"
-    states = torch.empty(B, nc, H, P, dtype=torch.float32, device=dev)
+    if out is not None:
+        assert out.shape == x.shape and out.dtype == x.dtype and _lib.tma_ok(out), "out must match x"
+    states = None if state_only else torch.empty(B, nc, H, P, dtype=torch.float32, device=dev)
     final = torch.empty(B, H, P, dtype=torch.float32, device=dev) if return_final_states else None
     init = None
     if initial_states is not None:
@@ -69,11 +77,13 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
     a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
     a.dtype = _lib.DTYPE_CODES[x.dtype]
     a.x, a.x_stride = x_k.data_ptr(), _lib.strides3(x_k)
-    a.out, a.out_stride = out.data_ptr(), _lib.strides3(out)
+    if out is not None:
+        a.out, a.out_stride = out.data_ptr(), _lib.strides3(out)
     a.dt, a.A = dt_k.data_ptr(), A_k.data_ptr()
     a.initial_state = _lib.ptr(init)
-    s = states.stride()
-    a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
+    if states is not None:
+        s = states.stride()
+        a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
     a.final_state = _lib.ptr(final)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     with torch.cuda.device(dev):
@@ -83,8 +93,13 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
 
 def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, states: torch.Tensor,
                        dy: torch.Tensor, chunk_size: int = 256,
-                       d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False):
-    """Backward.  Returns (dx, ddt fp32 (B,L,H), dA fp32 (H,), d_initial_states or None)."""
+                       d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False,
+                       state_only: bool = False):
+    """Backward.  Returns (dx, ddt fp32 (B,L,H), dA fp32 (H,), d_initial_states or None).
+
+    ``state_only``: compute only the gradient w.r.t. the initial state (returns
+    (None, None, None, d_initial)) -- the first pass of the sequence-parallel
+    backward; dx, ddt and dA are not written."""
     B, L, H, P = _check_inputs(x, dt, A, chunk_size)
     dev = x.device
     nc = -(-L // chunk_size)
@@ -94,13 +109,18 @@ def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, state
     dy_k = _lib.tma_ready(dy if dy.dtype == x.dtype else dy.to(x.dtype))
     dt_k = dt.to(torch.float32).contiguous()
     A_k = A.to(torch.float32).contiguous()
-    dx = torch.empty_like(x, memory_format=torch.contiguous_format)
-    ddt = torch.empty(B, L, H, dtype=torch.float32, device=dev)
-    dA = torch.empty(H, dtype=torch.float32, device=dev)
+    if state_only:
+        need_d_initial = True
+        dx = ddt = dA = None
+    else:
+        dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+        ddt = torch.empty(B, L, H, dtype=torch.float32, device=dev)
+        dA = torch.empty(H, dtype=torch.float32, device=dev)
     d_init = torch.empty(B, H, P, dtype=torch.float32, device=dev) if need_d_initial else None
     dfin = None if d_final_states is None else d_final_states.to(torch.float32).contiguous()
     if x.numel() == 0:
-        dA.zero_()
+        if dA is not None:
+            dA.zero_()
         if d_init is not None:
             d_init.copy_(dfin if dfin is not None else torch.zeros_like(d_init))
         return dx, ddt, dA, d_init
@@ -110,12 +130,13 @@ def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, state
     a.dtype = _lib.DTYPE_CODES[x.dtype]
     a.x, a.x_stride = x_k.data_ptr(), _lib.strides3(x_k)
     a.dout, a.dout_stride = dy_k.data_ptr(), _lib.strides3(dy_k)
-    a.dx, a.dx_stride = dx.data_ptr(), _lib.strides3(dx)
+    if dx is not None:
+        a.dx, a.dx_stride = dx.data_ptr(), _lib.strides3(dx)
     a.dt, a.A = dt_k.data_ptr(), A_k.data_ptr()
     s = states.stride()
     a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
     a.d_final_state = _lib.ptr(dfin)
-    a.ddt, a.dA_out = ddt.data_ptr(), dA.data_ptr()
+    a.ddt, a.dA_out = _lib.ptr(ddt), _lib.ptr(dA)
     a.d_initial_state = _lib.ptr(d_init)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     with torch.cuda.device(dev):

@@ -1,0 +1,139 @@
+"""Sequence-parallel dt-form EMA over a torch.distributed process group.
+
+For sequences too long for one GPU's time budget (benchmark config 4:
+B1 L65536 H32 P64), rank r of a group of R owns tokens
+[r L/R, (r+1) L/R) of every (batch, head) chain.  The recurrence
+
+    h_t = exp(dt_t A_h) h_{t-1} + dt_t x_t
+
+is affine in h, so a span acts on its incoming state as h -> D h + S with
+D = exp(A_h sum_span dt) and S the span's end state from a zero start.
+
+Forward:
+  1. state-only pass over the local span (reads x once, writes nothing but
+     S_r, (B, H, P) fp32);
+  2. chain the spans with NCCL send/recv, r -> r+1: rank r receives its
+     incoming state Sin_r and sends D_r Sin_r + S_r on;
+  3. the local pass from the true incoming state (y, chunk start states).
+Backward, the mirror image:
+  1. state-only pass: the gradient w.r.t. the span's incoming state from the
+     local dy;
+  2. chain r+1 -> r: rank r receives the gradient w.r.t. its span's end state
+     Gin_r and sends D_r Gin_r + G_r back;
+  3. the local backward with d_final_states = Gin_r (dx, ddt and this span's
+     dA), then one all-reduce of the H per-head dA values.
+
+Messages are (B, H, P) fp32 (8 KB at config 4); the only collective on the
+data path is the per-head dA sum.  Every rank takes the same collective steps
+in the same order.  The local passes are injectable so the host logic can be
+tested on CPU ranks (gloo) against the float64 oracle.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from .ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+
+__all__ = ["span_decay", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
+
+
+def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
+    """D = exp(A_h * sum_t dt[b, t, h]) over the local span, (B, H) fp32."""
+    return torch.exp(dt.to(torch.float32).sum(dim=1) * A.to(torch.float32))
+
+
+def _peer(group, r):
+    """Global rank of group rank ``r`` (send/recv address global ranks)."""
+    return r if group is None else dist.get_global_rank(group, r)
+
+
+def _kernel_state_fwd(x, dt, A, chunk_size):
+    return ema_chunk_scan_fwd(x, dt, A, chunk_size, state_only=True)[2]
+
+
+def _kernel_fwd(x, dt, A, chunk_size, initial_states):
+    return ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states, return_final_states=True)
+
+
+def _kernel_state_bwd(x, dt, A, states, dy, chunk_size):
+    return ema_chunk_scan_bwd(x, dt, A, states, dy, chunk_size, state_only=True)[3]
+
+
+def _kernel_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial):
+    return ema_chunk_scan_bwd(x, dt, A, states, dy, chunk_size, d_final_states=d_final_states,
+                              need_d_initial=need_d_initial)
+
+
+def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Optional[torch.Tensor] = None,
+               state_fwd: Callable = _kernel_state_fwd, local_fwd: Callable = _kernel_fwd):
+    """Sequence-parallel forward of this rank's span.
+
+    Returns (y, chunk_start_states, Sin, final): ``Sin`` is the state entering
+    this span (saved for the backward), ``final`` this span's end state (the
+    sequence's final state on the last rank)."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    B, _, H, P = x.shape
+    S_loc = state_fwd(x, dt, A, chunk_size)
+    if rank == 0:
+        Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
+               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    else:
+        Sin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
+        dist.recv(Sin, src=_peer(group, rank - 1), group=group)
+    if rank + 1 < world:
+        Sout = span_decay(dt, A)[..., None] * Sin + S_loc
+        dist.send(Sout.to(torch.float32).contiguous(), dst=_peer(group, rank + 1), group=group)
+    y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
+    return y, states, Sin, final
+
+
+def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
+                d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False,
+                state_bwd: Callable = _kernel_state_bwd, local_bwd: Callable = _kernel_bwd):
+    """Sequence-parallel backward of this rank's span.
+
+    ``states`` are the chunk start states of this span's forward (which
+    started from its true incoming state).  Returns (dx, ddt, dA, d_initial):
+    dA is summed over the group; d_initial (rank 0, when asked) is the
+    gradient w.r.t. the sequence's initial state."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    B, _, H, P = x.shape
+    G_loc = state_bwd(x, dt, A, states, dy, chunk_size)
+    if rank == world - 1:
+        Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
+               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    else:
+        Gin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
+        dist.recv(Gin, src=_peer(group, rank + 1), group=group)
+    if rank > 0:
+        Gout = span_decay(dt, A)[..., None] * Gin + G_loc
+        dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
+    dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial and rank == 0)
+    dA = dA.to(torch.float32).contiguous()
+    dist.all_reduce(dA, group=group)
+    return dx, ddt, dA, d_init
+
+
+class _EmaChunkScanSPFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dt, A, chunk_size, group):
+        y, states, _, _ = sp_forward(x, dt, A, chunk_size, group)
+        ctx.save_for_backward(x, dt, A, states)
+        ctx.chunk_size, ctx.group = chunk_size, group
+        ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, dt, A, states = ctx.saved_tensors
+        dx, ddt, dA, _ = sp_backward(x, dt, A, states, dy.contiguous(), ctx.chunk_size, ctx.group)
+        return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, None
+
+
+def ema_chunk_scan_sp(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256, group=None):
+    """Autograd op over this rank's span of a sequence split across ``group``."""
+    return _EmaChunkScanSPFn.apply(x, dt, A, chunk_size, group)

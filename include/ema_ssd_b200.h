@@ -71,7 +71,7 @@ typedef struct EmaFwdArgs {
   int32_t seq_idx_type;  /* EMA_IDX_* (EMA_IDX_NONE when seq_idx is NULL) */
   const void* x;         /* (B,L,H,P) */
   int64_t x_stride[3];   /* element strides of batch, seqlen, head */
-  void* out;             /* (B,L,H,P), dtype */
+  void* out;             /* (B,L,H,P), dtype; NULL = state-only pass (needs final_state) */
   int64_t out_stride[3];
   const float* dA;       /* reference form, (B,H,L) contiguous, or NULL */
   const float* dt;       /* dt form, (B,L,H) contiguous, or NULL */
@@ -110,7 +110,7 @@ typedef struct EmaBwdArgs {
   int64_t x_stride[3];
   const void* dout;
   int64_t dout_stride[3];
-  void* dx;
+  void* dx;              /* NULL = state-only pass: only d_initial_state is written */
   int64_t dx_stride[3];
   const float* da_cs;     /* reference form */
   const float* da_cs_sum; /* reference form */

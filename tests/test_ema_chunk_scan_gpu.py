@@ -199,3 +199,56 @@ def test_concurrent_streams_use_separate_workspaces():
         torch.cuda.current_stream().wait_stream(s)
     for o in outs:
         torch.testing.assert_close(o, ref, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_state_only_passes_and_span_chaining(dtype):
+    """The sequence-parallel building blocks on one GPU: state-only passes give
+    the same final state / initial-state gradient as the full passes, and a
+    sequence split into spans, chained on the host as kernels/ema_sp.py chains
+    them over NCCL, reproduces the whole-sequence results."""
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    from kernels.ema_sp import span_decay
+    B, L, H, P, Q, R = 2, 1024, 3, 64, 128, 4
+    tx, tdt, tA, tdy = _inputs(B, L, H, P, 31, dtype)
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    y_full, st_full, fin_full = ema_chunk_scan_fwd(x, dt, A, Q, return_final_states=True)
+    dx_full, ddt_full, dA_full, _ = ema_chunk_scan_bwd(x, dt, A, st_full, dy, Q)
+
+    none_y, none_st, fin_so = ema_chunk_scan_fwd(x, dt, A, Q, state_only=True)
+    assert none_y is None and none_st is None
+    assert_fp32_close(fin_so, fin_full.cpu().numpy(), "state-only final state")
+    dinit_full = ema_chunk_scan_bwd(x, dt, A, st_full, dy, Q, need_d_initial=True)[3]
+    dx_so, ddt_so, dA_so, dinit_so = ema_chunk_scan_bwd(x, dt, A, st_full, dy, Q, state_only=True)
+    assert dx_so is None and ddt_so is None and dA_so is None
+    assert_fp32_close(dinit_so, dinit_full.cpu().numpy(), "state-only initial-state gradient")
+
+    span = L // R
+    sl = [slice(r * span, (r + 1) * span) for r in range(R)]
+    xs = [x[:, s].contiguous() for s in sl]
+    dts = [dt[:, s].contiguous() for s in sl]
+    dys = [dy[:, s].contiguous() for s in sl]
+    # forward chain r -> r+1
+    Sin, sins = torch.zeros(B, H, P, device=DEV), []
+    for r in range(R):
+        sins.append(Sin)
+        S_loc = ema_chunk_scan_fwd(xs[r], dts[r], A, Q, state_only=True)[2]
+        Sin = span_decay(dts[r], A)[..., None] * Sin + S_loc
+    outs = [ema_chunk_scan_fwd(xs[r], dts[r], A, Q, initial_states=sins[r]) for r in range(R)]
+    y_sp = torch.cat([o[0] for o in outs], dim=1)
+    # backward chain r+1 -> r
+    Gin, gins = torch.zeros(B, H, P, device=DEV), [None] * R
+    for r in reversed(range(R)):
+        gins[r] = Gin
+        G_loc = ema_chunk_scan_bwd(xs[r], dts[r], A, outs[r][1], dys[r], Q, state_only=True)[3]
+        Gin = span_decay(dts[r], A)[..., None] * Gin + G_loc
+    grads = [ema_chunk_scan_bwd(xs[r], dts[r], A, outs[r][1], dys[r], Q, d_final_states=gins[r])
+             for r in range(R)]
+    dx_sp = torch.cat([g[0] for g in grads], dim=1)
+    ddt_sp = torch.cat([g[1] for g in grads], dim=1)
+    dA_sp = sum(g[2] for g in grads)
+    check = assert_fp32_close if dtype == torch.float32 else assert_lowp_close
+    check(y_sp, y_full.float().cpu().numpy(), "span-chained y")
+    check(dx_sp, dx_full.float().cpu().numpy(), "span-chained dx")
+    check(ddt_sp, ddt_full.cpu().numpy(), "span-chained ddt")
+    check(dA_sp, dA_full.cpu().numpy(), "span-chained dA")
