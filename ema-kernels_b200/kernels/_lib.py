@@ -69,6 +69,36 @@ class EmaBwdArgs(ctypes.Structure):
     ]
 
 
+class SsdFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64), ("dstate", _i64), ("ngroups", _i64),
+        ("dtype", _i32), ("reserved", _i32),
+        ("x", _ptr), ("x_stride", _i64 * 3),
+        ("dt", _ptr), ("A", _ptr),
+        ("B", _ptr), ("B_stride", _i64 * 3),
+        ("C", _ptr), ("C_stride", _i64 * 3),
+        ("D", _ptr), ("initial_state", _ptr),
+        ("out", _ptr), ("out_stride", _i64 * 3),
+        ("chunk_states", _ptr), ("final_state", _ptr),
+    ]
+
+
+class SsdBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64), ("dstate", _i64), ("ngroups", _i64),
+        ("dtype", _i32), ("reserved", _i32),
+        ("x", _ptr), ("x_stride", _i64 * 3),
+        ("dt", _ptr), ("A", _ptr),
+        ("B", _ptr), ("B_stride", _i64 * 3),
+        ("C", _ptr), ("C_stride", _i64 * 3),
+        ("D", _ptr), ("chunk_states", _ptr),
+        ("dout", _ptr), ("dout_stride", _i64 * 3),
+        ("d_final_state", _ptr),
+        ("dx", _ptr), ("dx_stride", _i64 * 3),
+        ("ddt", _ptr), ("dA", _ptr), ("dB", _ptr), ("dC", _ptr), ("dD", _ptr), ("d_initial_state", _ptr),
+    ]
+
+
 lib.ema_scan_workspace_size.restype = ctypes.c_size_t
 lib.ema_scan_workspace_size.argtypes = [_i64] * 5
 lib.ema_fwd_launch.restype = ctypes.c_int
@@ -82,6 +112,12 @@ lib.ema_workspace_status.restype = ctypes.c_int
 lib.ema_workspace_status.argtypes = [_ptr, ctypes.POINTER(ctypes.c_uint32), _ptr]
 lib.ema_workspace_clear_status.restype = ctypes.c_int
 lib.ema_workspace_clear_status.argtypes = [_ptr, _ptr]
+lib.ssd_internal_chunks.restype = _i64
+lib.ssd_internal_chunks.argtypes = [_i64]
+lib.ssd_fwd_launch.restype = ctypes.c_int
+lib.ssd_fwd_launch.argtypes = [ctypes.POINTER(SsdFwdArgs), _ptr]
+lib.ssd_bwd_launch.restype = ctypes.c_int
+lib.ssd_bwd_launch.argtypes = [ctypes.POINTER(SsdBwdArgs), _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p
 lib.ema_version.restype = ctypes.c_char_p
 

@@ -1,0 +1,167 @@
+"""Mamba-2 SSD chunked scan (benchmark configs 3 and 5) on the B200 kernels.
+
+Drop-in for the op the reference benchmarks its EMA against,
+``mamba_ssm.ops.triton.ssd_combined.mamba_chunk_scan_combined(x, dt, A, B, C,
+chunk_size, ...)`` (kernels/benchmarks/bench_ema_total.py:72-76; the package is
+third-party and absent here).  Same argument names and layouts:
+
+    x (batch, seqlen, nheads, headdim) bf16, dt (batch, seqlen, nheads),
+    A (nheads,), B / C (batch, seqlen, ngroups, dstate) bf16, D (nheads,),
+    initial_states / final states (batch, nheads, headdim, dstate) fp32
+
+    s_t = exp(dt_t A_h) s_{t-1} + dt_t x_t B_t^T,   y_t = s_t C_t + D_h x_t
+
+``dt_bias`` / ``dt_softplus`` are applied before the scan (dt <- softplus(dt +
+dt_bias)) and differentiated by autograd.  Not supported yet: ``z`` gating,
+``seq_idx`` / ``cu_seqlens`` (packed sequences) and ``dt_limit`` other than the
+default.  headdim must be 64 and dstate 128 (the benchmark shapes).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+__all__ = ["ssd_chunk_scan_fwd", "ssd_chunk_scan_bwd", "mamba_chunk_scan_combined"]
+
+
+def _s3(t):
+    s = t.stride()
+    return (_lib._i64 * 3)(s[0], s[1], s[2])
+
+
+def _prep(x, dt, A, B, C, D):
+    assert x.is_cuda and dt.is_cuda and A.is_cuda and B.is_cuda and C.is_cuda, "All tensors must be on CUDA"
+    assert x.ndim == 4 and B.ndim == 4 and C.ndim == 4, "x (b,l,h,p); B, C (b,l,g,n)"
+    b_, L, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    assert dt.shape == (b_, L, H), "dt must be (batch, seqlen, nheads)"
+    assert A.shape == (H,), "A must be (nheads,)"
+    assert B.shape == (b_, L, G, N) and C.shape == B.shape, "B and C must be (batch, seqlen, ngroups, dstate)"
+    assert H % G == 0, "nheads must be a multiple of ngroups"
+    assert D is None or D.shape == (H,), "D must be (nheads,)"
+    assert x.dtype == torch.bfloat16, "the SSD kernels take bf16 x / B / C"
+
+    def ok(t):
+        return t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and all(s % 8 == 0 for s in t.stride()[:3])
+
+    xk = x if ok(x) else x.contiguous()
+    Bk = B.to(torch.bfloat16)
+    Bk = Bk if ok(Bk) else Bk.contiguous()
+    Ck = C.to(torch.bfloat16)
+    Ck = Ck if ok(Ck) else Ck.contiguous()
+    dtk = dt.to(torch.float32).contiguous()
+    Ak = A.to(torch.float32).contiguous()
+    Dk = None if D is None else D.to(torch.float32).contiguous()
+    return b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk
+
+
+def ssd_chunk_scan_fwd(x, dt, A, B, C, D=None, initial_states=None, return_final_states=False,
+                       save_states=True):
+    """Forward.  Returns (y, chunk_states or None, final_states or None)."""
+    b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk = _prep(x, dt, A, B, C, D)
+    dev = x.device
+    y = torch.empty(b_, L, H, P, dtype=x.dtype, device=dev)
+    nci = int(_lib.lib.ssd_internal_chunks(L))
+    cst = torch.empty(b_, nci, H, P, N, dtype=torch.float32, device=dev) if save_states else None
+    fin = torch.empty(b_, H, P, N, dtype=torch.float32, device=dev) if return_final_states else None
+    init = None
+    if initial_states is not None:
+        assert initial_states.shape == (b_, H, P, N), "initial_states must be (batch, nheads, headdim, dstate)"
+        init = initial_states.to(torch.float32).contiguous()
+    a = _lib.SsdFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.dstate, a.ngroups = b_, L, H, P, N, G
+    a.dtype = _lib.DTYPE_CODES[torch.bfloat16]
+    a.x, a.x_stride = xk.data_ptr(), _s3(xk)
+    a.dt, a.A = dtk.data_ptr(), Ak.data_ptr()
+    a.B, a.B_stride = Bk.data_ptr(), _s3(Bk)
+    a.C, a.C_stride = Ck.data_ptr(), _s3(Ck)
+    a.D = _lib.ptr(Dk)
+    a.initial_state = _lib.ptr(init)
+    a.out, a.out_stride = y.data_ptr(), _s3(y)
+    a.chunk_states = _lib.ptr(cst)
+    a.final_state = _lib.ptr(fin)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib.ssd_fwd_launch(a, _lib.stream_ptr(dev)), "ssd_chunk_scan_fwd")
+    return y, cst, fin
+
+
+def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=None, need_d_initial=False):
+    """Backward.  Returns (dx, ddt, dA, dB, dC, dD or None, d_initial_states or None);
+    dB / dC are fp32 (batch, seqlen, ngroups, dstate), summed over each group's heads."""
+    b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk = _prep(x, dt, A, B, C, D)
+    dev = x.device
+    assert dy.shape == x.shape
+    dyk = dy.to(torch.bfloat16)
+    dyk = dyk if (dyk.stride(-1) == 1 and dyk.data_ptr() % 16 == 0
+                  and all(s % 8 == 0 for s in dyk.stride()[:3])) else dyk.contiguous()
+    dx = torch.empty(b_, L, H, P, dtype=x.dtype, device=dev)
+    ddt = torch.empty(b_, L, H, dtype=torch.float32, device=dev)
+    dA = torch.empty(H, dtype=torch.float32, device=dev)
+    dB = torch.empty(b_, L, G, N, dtype=torch.float32, device=dev)
+    dC = torch.empty(b_, L, G, N, dtype=torch.float32, device=dev)
+    dD = torch.empty(H, dtype=torch.float32, device=dev) if D is not None else None
+    d_init = torch.empty(b_, H, P, N, dtype=torch.float32, device=dev) if need_d_initial else None
+    dfin = None if d_final_states is None else d_final_states.to(torch.float32).contiguous()
+    a = _lib.SsdBwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.dstate, a.ngroups = b_, L, H, P, N, G
+    a.dtype = _lib.DTYPE_CODES[torch.bfloat16]
+    a.x, a.x_stride = xk.data_ptr(), _s3(xk)
+    a.dt, a.A = dtk.data_ptr(), Ak.data_ptr()
+    a.B, a.B_stride = Bk.data_ptr(), _s3(Bk)
+    a.C, a.C_stride = Ck.data_ptr(), _s3(Ck)
+    a.D = _lib.ptr(Dk)
+    a.chunk_states = chunk_states.data_ptr()
+    a.dout, a.dout_stride = dyk.data_ptr(), _s3(dyk)
+    a.d_final_state = _lib.ptr(dfin)
+    a.dx, a.dx_stride = dx.data_ptr(), _s3(dx)
+    a.ddt, a.dA, a.dB, a.dC = ddt.data_ptr(), dA.data_ptr(), dB.data_ptr(), dC.data_ptr()
+    a.dD = _lib.ptr(dD)
+    a.d_initial_state = _lib.ptr(d_init)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib.ssd_bwd_launch(a, _lib.stream_ptr(dev)), "ssd_chunk_scan_bwd")
+    return dx, ddt, dA, dB, dC, dD, d_init
+
+
+class SsdChunkScanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dt, A, B, C, D, initial_states, return_final_states):
+        y, cst, fin = ssd_chunk_scan_fwd(x, dt, A, B, C, D, initial_states, return_final_states)
+        ctx.save_for_backward(x, dt, A, B, C, D, cst)
+        ctx.has_init = initial_states is not None
+        ctx.dtypes = (dt.dtype, A.dtype, B.dtype, C.dtype, None if D is None else D.dtype)
+        return (y, fin) if return_final_states else y
+
+    @staticmethod
+    def backward(ctx, dy, *rest):
+        x, dt, A, B, C, D, cst = ctx.saved_tensors
+        dfin = rest[0] if rest else None
+        if dy is None:
+            dy = torch.zeros_like(x)
+        dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(x, dt, A, B, C, cst, dy, D, dfin, ctx.has_init)
+        tdt, tA, tB, tC, tD = ctx.dtypes
+        return (dx, ddt.to(tdt), dA.to(tA), dB.to(tB), dC.to(tC), None if dD is None else dD.to(tD), d_init, None)
+
+
+def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bias=None, initial_states=None,
+                              seq_idx=None, cu_seqlens=None, dt_softplus=False, dt_limit=(0.0, float("inf")),
+                              return_final_states=False, return_varlen_states=False):
+    """mamba_ssm's ``mamba_chunk_scan_combined`` on the B200 SSD kernels (autograd).
+
+    Returns y, or (y, final_states) with ``return_final_states``.  ``chunk_size``
+    is accepted for signature compatibility; the result does not depend on it."""
+    assert z is None, "z gating is not supported yet"
+    assert seq_idx is None and cu_seqlens is None and not return_varlen_states, \
+        "packed sequences (seq_idx / cu_seqlens) are not supported yet"
+    assert tuple(dt_limit) == (0.0, float("inf")), "dt_limit is not supported yet"
+    assert chunk_size > 0 and math.log2(chunk_size).is_integer(), "chunk_size must be a power of two"
+    if dt_bias is not None:
+        dt = dt + dt_bias
+    if dt_softplus:
+        dt = F.softplus(dt)
+    return SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)

@@ -11,17 +11,18 @@ import pytest
 from conftest import ROOT
 
 HEADER = os.path.join(ROOT, "include", "ema_ssd_b200.h")
+SSD_HEADER = os.path.join(ROOT, "include", "ssd_b200.h")
 
 
 def _declared():
-    src = open(HEADER).read()
+    src = open(HEADER).read() + open(SSD_HEADER).read()
     return re.findall(r"EMA_API\s+[\w\s\*]+?\b(\w+)\s*\(", src)
 
 
 def test_header_declares_entry_points():
     names = _declared()
     for n in ("ema_fwd_launch", "ema_bwd_launch", "chunk_cumsum_launch", "ema_scan_workspace_size",
-              "ema_workspace_status", "ema_last_error"):
+              "ema_workspace_status", "ema_last_error", "ssd_fwd_launch", "ssd_bwd_launch", "ssd_internal_chunks"):
         assert n in names
 
 
@@ -50,6 +51,44 @@ def test_struct_layouts_match_header():
     assert sizes[1] == ctypes.sizeof(_lib.EmaBwdArgs)
     assert sizes[2] == _lib.EmaFwdArgs.workspace.offset
     assert sizes[3] == _lib.EmaBwdArgs.workspace.offset
+
+
+def test_ssd_struct_layouts_match_header():
+    """ctypes mirrors of SsdFwdArgs / SsdBwdArgs have the C sizes and field offsets."""
+    import subprocess
+    import tempfile
+    from kernels import _lib
+    fields_f = ["final_state", "chunk_states", "out", "D"]
+    fields_b = ["d_initial_state", "dD", "ddt", "dout", "chunk_states"]
+    code = ('#include "ssd_b200.h"\n#include <stdio.h>\n#include <stddef.h>\nint main(){printf("%zu %zu'
+            + ' %zu' * (len(fields_f) + len(fields_b)) + '\\n", sizeof(SsdFwdArgs), sizeof(SsdBwdArgs)'
+            + ''.join(f', offsetof(SsdFwdArgs, {f})' for f in fields_f)
+            + ''.join(f', offsetof(SsdBwdArgs, {f})' for f in fields_b) + ');return 0;}\n')
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        open(c, "w").write(code)
+        subprocess.run(["gcc", "-I", os.path.dirname(SSD_HEADER), c, "-o", exe], check=True)
+        out = [int(v) for v in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_lib.SsdFwdArgs)
+    assert out[1] == ctypes.sizeof(_lib.SsdBwdArgs)
+    for k, f in enumerate(fields_f):
+        assert out[2 + k] == getattr(_lib.SsdFwdArgs, f).offset, f
+    for k, f in enumerate(fields_b):
+        assert out[2 + len(fields_f) + k] == getattr(_lib.SsdBwdArgs, f).offset, f
+
+
+def test_ssd_validation_rejects_unsupported_shapes():
+    """Host-side checks run before any device work (no GPU needed)."""
+    from kernels import _lib
+    a = _lib.SsdFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.dstate, a.ngroups = 1, 64, 2, 32, 128, 1
+    a.dtype = _lib.DTYPE_CODES[__import__("torch").bfloat16]
+    assert _lib.lib.ssd_fwd_launch(a, None) == 2  # EMA_ERR_UNSUPPORTED: headdim 32
+    assert b"headdim" in _lib.lib.ema_last_error()
+    a.headdim, a.nheads, a.ngroups = 64, 3, 2
+    assert _lib.lib.ssd_fwd_launch(a, None) == 1  # nheads not a multiple of ngroups
+    assert _lib.lib.ssd_internal_chunks(4096) == 64 and _lib.lib.ssd_internal_chunks(65) == 2
 
 
 def test_workspace_size_grows_with_tiles():
