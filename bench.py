@@ -198,6 +198,170 @@ def run_reference_arm(args, rank, world):
     }), flush=True)
 
 
+def _event_ms(fn, K, warmup, stream, flush=None):
+    """K timed calls of fn() on `stream` (CUDA events around each), after warm-up."""
+    for _ in range(warmup):
+        if flush is not None:
+            flush()
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for k in range(K):
+        if flush is not None:
+            flush()
+        ev[k][0].record(stream)
+        fn()
+        ev[k][1].record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev)
+
+
+SSD_CFG = dict(B=8, L=4096, H=64, P=64, N=128, G=1)
+# minimum HBM bytes per token of SSD fwd+bwd (bf16 x, y, dy, dx: 10 H P; B, C read twice and dB, dC
+# written, fp32 gradients: 12 G N; dt read twice, ddt written: 12 H) -- 43,264 B at config 3
+SSD_BYTES_PER_TOKEN = 10 * 64 * 64 + 12 * 1 * 128 + 12 * 64
+# tensor-core flops per token of the chunked algorithm at 64-token chunks (fwd: C B^T, M x, C s^T,
+# x^T B; bwd: the nine contractions of ssd_bwd_kernel, state operands counted twice for the split)
+SSD_FLOPS_PER_TOKEN = 2 * 64 * (64 * 128 + 64 * 64 + 128 * 64 + 64 * 128) + \
+    2 * 64 * (64 * 128 + 64 * 64 + 64 * 64 + 2 * 128 * 64 + 64 * 128 + 64 * 64 + 64 * 128 + 2 * 64 * 128 + 2 * 64 * 128)
+
+
+def run_ssd(args, rank, world, local_rank):
+    """Config 3 (Mamba-2 SSD) fwd+bwd per rank; batch x heads shard with no collective."""
+    from oracle import ssd_oracle as so
+    from kernels.ssd_combined import ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    c = SSD_CFG
+    x, dt, A, Bm, Cm, D, dy = so.make_ssd_inputs(c["B"], c["L"], c["H"], c["P"], c["N"], c["G"], seed=11 + rank)
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # noqa: E731
+    x, Bm, Cm, dy = bf(x), bf(Bm), bf(Cm), bf(dy)
+    dt, A, D = (torch.from_numpy(a).to(dev) for a in (dt, A, D))
+    side = torch.cuda.Stream(dev)
+    with torch.cuda.stream(side):
+        y, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+        ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
+        side.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            y, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+            ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
+        K = max(1, min(args.steps, 50))
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        if dist is not None:
+            dist.barrier()
+        t0 = time.time()
+        ms = _event_ms(g.replay, K, args.warmup, side)
+        t1 = time.time()
+    clocks.window = (t0, t1)
+    clocks.stop()
+    tm = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms = float(tm.item()) / K
+    if rank == 0:
+        peak, kind = _peaks()
+        tflops_peak = _tc_peak()
+        tokens = c["B"] * c["L"]
+        gbs = SSD_BYTES_PER_TOKEN * tokens / (ms * 1e-3) / 1e9
+        tfl = SSD_FLOPS_PER_TOKEN * tokens / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "SSD fwd+bwd Mtokens/s (config 3: B8 L4096 H64 P64 N128 G1 bf16)",
+            "value": world * tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "Mamba-2 SSD fwd+bwd (config 3)", **c, "chunk_internal": 64,
+                       "l2": "step inputs 1.4 GB > 126 MB L2, no flush", "timing": "one CUDA graph per step"},
+            "roofline": {"bound": "ridge", "hbm": {"achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
+                         "tensor": {"achieved": tfl, "peak": tflops_peak, "unit": "TFLOP/s",
+                                    "frac": tfl / tflops_peak, "flops_per_token": SSD_FLOPS_PER_TOKEN}},
+            "gpu_launches": 2 * K, "clocks": clocks.summary(),
+            "cpu_baseline": {"value": None, "unit": "Mtokens/s", "cores": 0, "kind": "port",
+                             "sample": "none in the reference (SSD is the absent mamba_ssm package)"},
+        }), flush=True)
+    del g
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+SP_CFG = dict(B=1, L=65536, H=32, P=64, Q=256)
+
+
+def run_sp(args, rank, world, local_rank):
+    """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong scaling);
+    fwd+bwd through kernels.ema_sp (state-only pass, NCCL send/recv chain, local pass)."""
+    from oracle.ema_oracle import make_dt_inputs
+    from kernels import ema_sp
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    else:
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    c = SP_CFG
+    span = c["L"] // world
+    x, dt, A, dy = make_dt_inputs(c["B"], c["L"], c["H"], c["P"], seed=21)
+    sl = slice(rank * span, (rank + 1) * span)
+    x = torch.from_numpy(np.ascontiguousarray(x[:, sl])).to(torch.bfloat16).to(dev)
+    dy = torch.from_numpy(np.ascontiguousarray(dy[:, sl])).to(torch.bfloat16).to(dev)
+    dt = torch.from_numpy(np.ascontiguousarray(dt[:, sl])).to(dev)
+    A = torch.from_numpy(A).to(dev)
+    def step():
+        y, states, Sin, _ = ema_sp.sp_forward(x, dt, A, c["Q"])
+        ema_sp.sp_backward(x, dt, A, states, dy, c["Q"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    K = max(1, min(args.steps, 200))
+    dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev if world > 1 else "cpu")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank == 0:
+        peak, _ = _peaks()
+        tokens = c["B"] * c["L"]
+        gbs = BYTES_PER_TOKEN * tokens / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "EMA fwd+bwd Mtokens/s, sequence parallel (config 4: B1 L65536 H32 P64 bf16)",
+            "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "EMA dt-form fwd+bwd, one sequence split over the ranks", **c,
+                       "span_per_rank": span, "parallelism": f"sequence parallel over {world} GPU(s), "
+                       "NCCL send/recv state chain + dA all-reduce",
+                       "timing": "eager calls, CUDA events around K steps, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak,
+                         "note": "per-GPU algorithmic bytes of one fwd+bwd (the state-only passes "
+                                 "re-read x and dy)"},
+            "gpu_launches": K * (4 if world > 1 else 2),  # state-only passes only when split
+        }), flush=True)
+    dist.destroy_process_group()
+
+
+def _tc_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -208,6 +372,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "profile"], default="bench",
                     help="profile: run --steps eager fwd+bwd steps and exit (for ncu captures)")
+    ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
+                    help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
+                         "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -216,7 +383,19 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
 
     if args.impl == "reference":
+        if args.workload != "ema":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "workload": args.workload,
+                                  "unavailable": "the reference has no CPU path for this workload "
+                                                 "(SSD is the absent mamba_ssm package; SP is not in the reference)"}))
+            return
         run_reference_arm(args, rank, world)
+        return
+    if args.workload == "ssd":
+        run_ssd(args, rank, world, local_rank)
+        return
+    if args.workload == "sp":
+        run_sp(args, rank, world, local_rank)
         return
 
     torch.cuda.set_device(local_rank)

@@ -77,6 +77,11 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     sequence's final state on the last rank)."""
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, _, H, P = x.shape
+    if world == 1:  # one span: no chain, no state-only pass
+        init = None if initial_states is None else initial_states.to(torch.float32)
+        Sin = init if init is not None else torch.zeros(B, H, P, dtype=torch.float32, device=x.device)
+        y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
+        return y, states, Sin, final
     S_loc = state_fwd(x, dt, A, chunk_size)
     if rank == 0:
         Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
@@ -102,7 +107,7 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     gradient w.r.t. the sequence's initial state."""
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, _, H, P = x.shape
-    G_loc = state_bwd(x, dt, A, states, dy, chunk_size)
+    G_loc = state_bwd(x, dt, A, states, dy, chunk_size) if world > 1 else None
     if rank == world - 1:
         Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
@@ -114,7 +119,8 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
         dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
     dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial and rank == 0)
     dA = dA.to(torch.float32).contiguous()
-    dist.all_reduce(dA, group=group)
+    if world > 1:
+        dist.all_reduce(dA, group=group)
     return dx, ddt, dA, d_init
 
 
