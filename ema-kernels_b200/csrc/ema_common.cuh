@@ -1,6 +1,6 @@
 // Device-side helpers shared by the EMA / SSD scan kernels (sm_100a).
 //
-//  * mbarrier + TMA (cp.async.bulk.tensor) wrappers, no cluster multicast;
+//  * mbarrier + TMA (cp.async.bulk.tensor) wrappers, CTA-local forms only;
 //  * acquire/release accessors for the inter-CTA look-back protocol;
 //  * bounded waits: every spin gives up after a wall-clock limit, sets a bit
 //    in the workspace status word and returns, so a lost producer can never
