@@ -207,39 +207,6 @@ __device__ __forceinline__ bool lookback_warp(const ScanWorkspace& ws, uint32_t 
   return true;
 }
 
-// Transposed warp sum: v[j] summed over the 32 lanes lands in lanes 4j..4j+3.
-__device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
-  const unsigned FULL = 0xffffffffu;
-  {
-    const bool up = lane & 16;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float send = up ? v[k] : v[k + 4];
-      const float keep = up ? v[k + 4] : v[k];
-      v[k] = keep + __shfl_xor_sync(FULL, send, 16);
-    }
-  }
-  {
-    const bool up = lane & 8;
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float send = up ? v[k] : v[k + 2];
-      const float keep = up ? v[k + 2] : v[k];
-      v[k] = keep + __shfl_xor_sync(FULL, send, 8);
-    }
-  }
-  {
-    const bool up = lane & 4;
-    const float send = up ? v[0] : v[1];
-    const float keep = up ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(FULL, send, 4);
-  }
-  float r = v[0];
-  r += __shfl_xor_sync(FULL, r, 2);
-  r += __shfl_xor_sync(FULL, r, 1);
-  return r;
-}
-
 // Completion bookkeeping, by consumer thread 0 after all of its CTA's stores:
 // true in the last CTA of the launch.
 __device__ __forceinline__ bool count_cta_done(const ScanWorkspace& ws) {
@@ -379,20 +346,25 @@ __device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_t
 // access is a vector, and per-token sums over channels reduce across only the
 // CG lanes of a run.  Runs are chained inside the warp with shuffles,
 // segments inside the CTA through shared memory, tiles through the look-back.
-template <int BP, int CPL>
+template <int BP, int CPL, int RUN_>
 struct Lanes {
   static_assert(CPL == 4 || CPL == 8, "4 or 8 channels per lane");
+  static_assert(RUN_ == 8 || RUN_ == 16, "8 or 16 tokens per run");
   static constexpr int NPR = CPL / 2;   // fp32x2 pairs per lane
   static constexpr int CG = BP / CPL;   // lanes per token (channel groups)
   static constexpr int TS = 32 / CG;    // runs per warp
-  static constexpr int RUN = 8;         // tokens per run
+  static constexpr int RUN = RUN_;      // tokens per run
   static constexpr int SEG = TS * RUN;  // tokens per warp
+  static_assert(CG >= RUN, "a run's tokens reduce over its channel-group lanes");
 };
 
-// Padded index of per-token shared arrays: the runs of a warp (8 tokens
-// apart) then fall in different banks.
-__device__ __forceinline__ constexpr int tix(int t) { return t + (t >> 3); }
-constexpr int tix_size(int q) { return q + q / 8; }
+// Padded index of per-token shared arrays: the runs of a warp (RUN tokens
+// apart) then fall in different banks, and tix(r0 + u) = tix(r0) + u for a
+// run start r0 and u < RUN.
+template <int RUN>
+__device__ __forceinline__ constexpr int tix(int t) { return t + t / RUN; }
+template <int RUN>
+constexpr int tix_size(int q) { return q + q / RUN; }
 
 // Scan of the affine maps z -> D z + E over the TS runs of a warp, in token
 // order (inclusive and exclusive).  E holds this lane's 8 channels; lanes of
@@ -468,33 +440,24 @@ __device__ __forceinline__ void runs_scan_rev(float D, const float2 (&R)[NPR], i
 }
 
 // Sum of v[j] over the CG lanes of a channel-group run, transposed: lane cg
-// returns the total of v[cg & 7].
-template <int CG>
-__device__ __forceinline__ float group_reduce8(float (&v)[8], int cg) {
+// returns the total of v[cg % RUN] (RUN - 1 shuffles for the transposition,
+// then one per further doubling up to CG).
+template <int RUN, int CG>
+__device__ __forceinline__ float group_reduce(float (&v)[RUN], int cg) {
   const unsigned FULL = 0xffffffffu;
-  {
-    const bool up = cg & 4;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float send = up ? v[k] : v[k + 4];
-      const float keep = up ? v[k + 4] : v[k];
-      v[k] = keep + __shfl_xor_sync(FULL, send, 4);
+  for (int half = RUN / 2; half >= 1; half /= 2) {
+    const bool up = cg & half;
+#pragma unroll
+    for (int k = 0; k < half; ++k) {
+      const float send = up ? v[k] : v[k + half];
+      const float keep = up ? v[k + half] : v[k];
+      v[k] = keep + __shfl_xor_sync(FULL, send, half);
     }
   }
-  {
-    const bool up = cg & 2;
+  float r = v[0];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float send = up ? v[k] : v[k + 2];
-      const float keep = up ? v[k + 2] : v[k];
-      v[k] = keep + __shfl_xor_sync(FULL, send, 2);
-    }
-  }
-  const bool up = cg & 1;
-  const float send = up ? v[0] : v[1];
-  float r = (up ? v[1] : v[0]) + __shfl_xor_sync(FULL, send, 1);
-  if (CG >= 16) r += __shfl_xor_sync(FULL, r, 8);
-  if (CG >= 32) r += __shfl_xor_sync(FULL, r, 16);
+  for (int o = RUN; o < CG; o <<= 1) r += __shfl_xor_sync(FULL, r, o);
   return r;
 }
 
@@ -600,8 +563,8 @@ __device__ __forceinline__ void chain_segments_rev(float* s_R, const float* s_D,
 template <typename T, int BP, int Q>
 struct FwdCfg {
   static constexpr int CPL = 8;  // channels per compute lane
-  using Ln = Lanes<BP, CPL>;
-  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR;
+  using Ln = Lanes<BP, CPL, 8>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR, RUN = Ln::RUN;
   static constexpr int CPT = BP / 32;  // channels per lane of the look-back warp
   static constexpr int NW = Q / SEG;   // compute warps
   static constexpr int NC = NW * 32;   // compute threads
@@ -611,8 +574,8 @@ struct FwdCfg {
   static constexpr int kStage = align_up(kX + (Q + 4) * 4, 128);  // x tile | decay row | A_h
   // per-CTA state after the ring
   static constexpr int oTok = 0;                              // float4[tix]  (a, a, w, w)
-  static constexpr int oG = oTok + tix_size(Q) * 16;          // float2[tix]  decay from the run start through t
-  static constexpr int oL2 = oG + tix_size(Q) * 8;            // float[Q]     log2 decay
+  static constexpr int oG = oTok + tix_size<RUN>(Q) * 16;            // float2[tix]  decay from the run start through t
+  static constexpr int oL2 = oG + tix_size<RUN>(Q) * 8;              // float[Q]     log2 decay
   static constexpr int oE = align_up(oL2 + Q * 4, 16);        // float[NW][BP + pad]
   static constexpr int oD = oE + NW * (BP + kRowPad) * 4;     // float[NW]
   static constexpr int oG0 = oD + NW * 4;                     // float[NW]
@@ -635,7 +598,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     ema_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const FwdParams p) {
   using C = FwdCfg<T, BP, Q>;
   constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
-  constexpr int CPL = C::CPL, NPR = C::NPR;
+  constexpr int CPL = C::CPL, NPR = C::NPR, RUN = C::RUN;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
   float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
@@ -732,13 +695,13 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   // ------------------------------ compute warps ---------------------------
   const int ts = lane / CG, cg = lane % CG;
   const int s0 = warp * SEG;      // this warp's first token in the tile
-  const int r0 = s0 + ts * 8;     // this lane's run
+  const int r0 = s0 + ts * RUN;   // this lane's run
   const int ch = cg * CPL;        // this lane's channel group
   const int nch = min(CPL, p.P - ch);  // valid channels of the group (P is a multiple of 4)
   const unsigned FULL = 0xffffffffu;
-  // this run's per-token entries: r0 is a multiple of 8, so tix(r0 + u) = tix(r0) + u
-  const float4* tok_r = s_tok + tix(r0);
-  const float2* g_r = s_g + tix(r0);
+  // this run's per-token entries: r0 is a multiple of RUN, so tix(r0 + u) = tix(r0) + u
+  const float4* tok_r = s_tok + tix<RUN>(r0);
+  const float2* g_r = s_g + tix<RUN>(r0);
   const long long lane_off = static_cast<long long>(r0) * p.sy_l + ch;  // within a tile's output
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -774,13 +737,13 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       }
       float g = a;  // product of the decays from the run start through t
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        const float n = __shfl_up_sync(FULL, g, o, 8);
-        if ((i & 7) >= o) g *= n;
+      for (int o = 1; o < RUN; o <<= 1) {
+        const float n = __shfl_up_sync(FULL, g, o, RUN);
+        if ((i & (RUN - 1)) >= o) g *= n;
       }
       if (lane < SEG) {
-        s_tok[tix(s0 + i)] = make_float4(a, a, w, w);
-        s_g[tix(s0 + i)] = f2_bcast(g);
+        s_tok[tix<RUN>(s0 + i)] = make_float4(a, a, w, w);
+        s_g[tix<RUN>(s0 + i)] = f2_bcast(g);
         s_l2[s0 + i] = l2;
       }
     }
@@ -805,7 +768,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 
     // ---- pass 1: local scan of the run from zero, kept in registers -----------
     const T* x_r = s_x + r0 * BP + ch;
-    float2 zl[8][NPR];
+    float2 zl[RUN][NPR];
     float Dexc;
     float2 Eexc[NPR];
     {
@@ -813,7 +776,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 #pragma unroll
       for (int q = 0; q < NPR; ++q) z[q] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < RUN; ++u) {
         const float4 tk = tok_r[u];
         const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
         float2 xv[NPR];
@@ -826,7 +789,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       }
       float Dinc;
       float2 Einc[NPR];
-      runs_scan_fwd<CG, TS, NPR>(g_r[7].x, z, ts, Dinc, Einc, Dexc, Eexc);
+      runs_scan_fwd<CG, TS, NPR>(g_r[RUN - 1].x, z, ts, Dinc, Einc, Dexc, Eexc);
       if (ts == TS - 1) {
         st_row<NPR>(s_E + warp * (BP + kRowPad) + ch, Einc);  // the segment's end state from zero
         if (cg == 0) s_D[warp] = Dinc;
@@ -874,7 +837,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       const long long ystep = p.sy_l;
       const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < RUN; ++u) {
         const float2 g = g_r[u];
         float2 yv[NPR];
 #pragma unroll
@@ -892,11 +855,11 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 // ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct BwdCfg {
-  // channels per compute lane: 4 at BP = 64 gives 16-token segments, twice
-  // the compute warps per tile, at half the registers per lane
+  // 4 channels x 16 tokens per lane at BP = 64 (32-token segments: the
+  // per-tile work of a lane amortised over 16 tokens), 8 x 8 at BP = 128
   static constexpr int CPL = (BP == 64) ? 4 : 8;
-  using Ln = Lanes<BP, CPL>;
-  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR;
+  using Ln = Lanes<BP, CPL, (BP == 64) ? 16 : 8>;
+  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR, RUN = Ln::RUN;
   static constexpr int CPT = BP / 32;
   static constexpr int NW = Q / SEG;
   static constexpr int NC = NW * 32;
@@ -909,8 +872,8 @@ struct BwdCfg {
   static constexpr int oSt = oRaw + (Q + 4) * 4;
   static constexpr int kStage = align_up(oSt + BP * 4, 128);
   static constexpr int oTok = 0;                           // float4[tix]  (a, a, w, w)
-  static constexpr int oG = oTok + tix_size(Q) * 16;       // float2[tix]  decay after t through the run end
-  static constexpr int oE = align_up(oG + tix_size(Q) * 8, 16);  // float[NW][BP + pad]  forward prefix -> Zin
+  static constexpr int oG = oTok + tix_size<RUN>(Q) * 16;         // float2[tix]  decay after t through the run end
+  static constexpr int oE = align_up(oG + tix_size<RUN>(Q) * 8, 16);  // float[NW][BP + pad]  forward prefix -> Zin
   static constexpr int oR = oE + NW * (BP + kRowPad) * 4;  // float[NW][BP + pad]  reverse aggregate -> Rloc
   static constexpr int oD = oR + NW * (BP + kRowPad) * 4;  // float[NW]
   static constexpr int oHs = oD + NW * 4;                  // float[NW]
@@ -934,7 +897,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
                    const BwdParams p) {
   using C = BwdCfg<T, BP, Q>;
   constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
-  constexpr int CPL = C::CPL, NPR = C::NPR;
+  constexpr int CPL = C::CPL, NPR = C::NPR, RUN = C::RUN;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
   float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
@@ -1044,13 +1007,13 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   // ------------------------------ compute warps ---------------------------
   const int ts = lane / CG, cg = lane % CG;
   const int s0 = warp * SEG;
-  const int r0 = s0 + ts * 8;
+  const int r0 = s0 + ts * RUN;
   const int ch = cg * CPL;
   const int nch = min(CPL, p.P - ch);
   const unsigned FULL = 0xffffffffu;
-  // this run's per-token entries: r0 is a multiple of 8, so tix(r0 + u) = tix(r0) + u
-  const float4* tok_r = s_tok + tix(r0);
-  const float2* g_r = s_g + tix(r0);
+  // this run's per-token entries: r0 is a multiple of RUN, so tix(r0 + u) = tix(r0) + u
+  const float4* tok_r = s_tok + tix<RUN>(r0);
+  const float2* g_r = s_g + tix<RUN>(r0);
   const long long lane_off = static_cast<long long>(r0) * p.sdx_l + ch;  // within a tile's dx
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -1085,15 +1048,15 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       }
       float gb = a;  // product of the decays from t through the run end
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        const float m = __shfl_down_sync(FULL, gb, o, 8);
-        if ((i & 7) + o < 8) gb *= m;
+      for (int o = 1; o < RUN; o <<= 1) {
+        const float m = __shfl_down_sync(FULL, gb, o, RUN);
+        if ((i & (RUN - 1)) + o < RUN) gb *= m;
       }
-      float gr = __shfl_down_sync(FULL, gb, 1, 8);  // decay after t through the run end
-      if ((i & 7) == 7) gr = 1.f;
+      float gr = __shfl_down_sync(FULL, gb, 1, RUN);  // decay after t through the run end
+      if ((i & (RUN - 1)) == RUN - 1) gr = 1.f;
       if (lane < SEG) {
-        s_tok[tix(s0 + i)] = make_float4(a, a, w, w);
-        s_g[tix(s0 + i)] = f2_bcast(gr);
+        s_tok[tix<RUN>(s0 + i)] = make_float4(a, a, w, w);
+        s_g[tix<RUN>(s0 + i)] = f2_bcast(gr);
       }
     }
     __syncwarp();
@@ -1104,7 +1067,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     //                                               this run's dy only)
     const T* x_r = s_x + r0 * BP + ch;
     const T* dy_r = s_dy + r0 * BP + ch;
-    float2 gl[8][NPR];
+    float2 gl[RUN][NPR];
     float Dexc, Dsuf;
     float2 Eexc[NPR], Gexc[NPR];
     {
@@ -1113,7 +1076,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       for (int q = 0; q < NPR; ++q) z[q] = gc[q] = make_float2(0.f, 0.f);
       float2 an = make_float2(0.f, 0.f);  // a_{u+1}; nothing beyond the run end
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < RUN; ++i) {
         const float4 tk = tok_r[i];
         float2 xv[NPR];
         load_grp<T, NPR>(x_r + i * BP, xv);
@@ -1121,7 +1084,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         for (int q = 0; q < NPR; ++q)
           z[q] = (MODE == kBwdCumsum) ? f2_fma(make_float2(tk.x, tk.y), z[q], xv[q])
                                       : f2_fma(make_float2(tk.x, tk.y), z[q], f2_mul(make_float2(tk.z, tk.w), xv[q]));
-        const int u = 7 - i;
+        const int u = RUN - 1 - i;
         float2 dv[NPR];
         load_grp<T, NPR>(dy_r + u * BP, dv);
 #pragma unroll
@@ -1194,9 +1157,9 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         T* dxp = dx_r;
         const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
         const float2 A2 = f2_bcast(Ah);
-        float pr[8];
+        float pr[RUN];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < RUN; ++u) {
           const float4 tk = tok_r[u];
           const float2 gr = g_r[u];
           const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
@@ -1234,7 +1197,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         // reference does after its kernel (dx[:, -1] += d_ox_state)
         if (p.d_last != nullptr && nv > 0) {
           const int ul = p.L - 1 - (t0 + r0);
-          if (ul < 8) {
+          if (ul < RUN) {
             T* q_dx = dx_r + ul * dxstep;
             const float* dl = p.d_last + static_cast<size_t>(bh) * p.P + ch;
             float2 v[NPR];
@@ -1249,8 +1212,8 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
             store_grp_cs<T, NPR>(q_dx, v, nch);
           }
         }
-        const float Pr = group_reduce8<CG>(pr, cg);
-        if (cg < 8) {
+        const float Pr = group_reduce<RUN, CG>(pr, cg);
+        if (cg < RUN) {
           const int gt = t0 + r0 + cg;
           if (gt < p.L) {
             if (MODE == kBwdCumsum) p.dl[static_cast<size_t>(bh) * p.L + gt] = Pr;
