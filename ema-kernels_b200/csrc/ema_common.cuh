@@ -112,6 +112,17 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
       "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
       : "memory");
 }
+// L2 prefetch of a tensor-map box (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+// L2 prefetch of a contiguous range: 16-byte aligned address, size a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -358,6 +369,21 @@ __device__ __forceinline__ void store_grp_cs(T* p, const float2 (&v)[NPR], int n
     __stcs(reinterpret_cast<float4*>(p), make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
   } else {
     __stcs(reinterpret_cast<uint2*>(p), make_uint2(pack_pair<T>(v[0]), pack_pair<T>(v[1])));
+  }
+}
+
+// Plain (shared-memory) store of 2 * NPR elements as T.
+template <typename T, int NPR>
+__device__ __forceinline__ void store_grp(T* p, const float2 (&v)[NPR]) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int q = 0; q < NPR; q += 2)
+      reinterpret_cast<float4*>(p)[q / 2] = make_float4(v[q].x, v[q].y, v[q + 1].x, v[q + 1].y);
+  } else if constexpr (NPR == 2) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_pair<T>(v[0]), pack_pair<T>(v[1]));
+  } else {
+    *reinterpret_cast<uint4*>(p) =
+        make_uint4(pack_pair<T>(v[0]), pack_pair<T>(v[1]), pack_pair<T>(v[2]), pack_pair<T>(v[3]));
   }
 }
 

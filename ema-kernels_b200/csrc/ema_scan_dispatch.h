@@ -24,6 +24,7 @@ struct FwdLaunch {
 struct BwdLaunch {
   const CUtensorMap* map_x;
   const CUtensorMap* map_dy;
+  const CUtensorMap* map_dx;  // dx stored in boxes of bwd_segment_tokens(BP) tokens
   BwdParams params;
   int block_p, chunk, mode;
   long long tiles;

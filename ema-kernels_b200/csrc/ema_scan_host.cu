@@ -317,8 +317,10 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   r = make_tile_map(&mdy, a->dout, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dout_stride, BP,
                     Q, "dout");
   if (r) return r;
+  CUtensorMap mdx = mdy;  // a state-only pass stores no dx
   if (!state_only) {
-    r = check_tile_tensor(a->dx, a->dtype, a->dx_stride, "dx");
+    r = make_tile_map(&mdx, a->dx, a->dtype, a->batch, a->seqlen, a->nheads, a->headdim, a->dx_stride, BP,
+                      bwd_segment_tokens(BP), "dx");
     if (r) return r;
   }
   p.B = static_cast<int>(a->batch);
@@ -348,6 +350,7 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   p.sdx_h = a->dx_stride[2];
   l.map_x = &mx;
   l.map_dy = &mdy;
+  l.map_dx = &mdx;
   l.block_p = BP;
   l.chunk = Q;
   l.mode = ref_form ? kBwdCumsum : kBwdDt;

@@ -40,7 +40,7 @@ int launch_bwd(const BwdLaunch& l) {
     int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), C::kBytes, &mask);
     if (e) return e;
     fn<<<persistent_grid(l.tiles, l.num_sms, C::CTAS), C::NT, C::kBytes, l.stream>>>(*l.map_x, *l.map_dy,
-                                                                                     l.params);
+                                                                                     *l.map_dx, l.params);
     return static_cast<int>(cudaGetLastError());
   }
 }

@@ -284,16 +284,22 @@ __device__ __forceinline__ void gather_col(float* dst, const float* src, int str
 // counter's round trip (a microsecond or more under contention) overlaps the
 // wait for a free stage instead of adding to every refill.  Tickets are
 // still taken in increasing order per CTA, and each producer still draws
-// exactly one ticket past the last tile.
-template <int S, class Issue>
+// exactly one ticket past the last tile.  Before waiting for a free stage the
+// producer asks for the upcoming tile's data in L2 (`prefetch(ticket)`, lane
+// 0): its DRAM reads then start a stage earlier than the ring alone allows.
+template <int S, class Issue, class Prefetch>
 __device__ __forceinline__ void producer_loop(uint64_t* full, uint64_t* empty, uint64_t* tid_full, int* s_tile,
-                                              uint32_t* hdr, int total, int lane, Issue&& issue) {
+                                              uint32_t* hdr, int total, int lane, Issue&& issue,
+                                              Prefetch&& prefetch) {
   uint32_t* status = &hdr[kHdrStatus];
   uint32_t next = 0;
   if (lane == 0) next = atomicAdd(&hdr[kHdrTicket], 1u);
   for (int k = 0;; ++k) {
     const int s = k % S;
-    if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status, 128)) break;
+    if (k >= S) {
+      if (lane == 0 && next < static_cast<uint32_t>(total)) prefetch(static_cast<int>(next));
+      if (!mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1, status, 128)) break;
+    }
     const uint32_t ticket = __shfl_sync(0xffffffffu, next, 0);
     if (ticket < static_cast<uint32_t>(total) && lane == 0) next = atomicAdd(&hdr[kHdrTicket], 1u);
     if (ticket >= static_cast<uint32_t>(total)) {
@@ -312,12 +318,16 @@ __device__ __forceinline__ void producer_loop(uint64_t* full, uint64_t* empty, u
 // incoming vector (forward: state entering the tile; backward: gradient
 // arriving at its end) in vec[k % 2][BP] for the compute warps, while they
 // run the tile's first pass.  `body(tile, run)` fills this lane's channels.
-// Having read the tile id it arrives on the stage's empty barrier (which
-// counts the compute warps and this warp).
-template <int S, int BP, class Body>
+// `pre(k, s)` runs first, once slot k % 2 is free (it may prepare other
+// per-tile tables in that slot and signal them itself); returning false ends
+// the loop.  Having read the tile id the warp arrives on the stage's empty
+// barrier (which counts the compute warps and this warp): the compute warps
+// arrive only after `pre`'s consumers have finished, so `pre` may still read
+// the stage.
+template <int S, int BP, class Pre, class Body>
 __device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_tile, uint64_t* empty,
                                               uint64_t* vec_full, uint64_t* vec_empty, float* vec,
-                                              uint32_t* status, int lane, Body&& body) {
+                                              uint32_t* status, int lane, Pre&& pre, Body&& body) {
   constexpr int CPT = BP / 32;
   for (int k = 0;; ++k) {
     const int s = k % S;
@@ -327,6 +337,7 @@ __device__ __forceinline__ void lookback_loop(uint64_t* tid_full, const int* s_t
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (k >= 2 && !mbar_wait_bounded(&vec_empty[k & 1], ((k >> 1) - 1) & 1, status, 512)) break;
+    if (!pre(k, s)) break;
     float run[CPT];
     body(tile, run);
 #pragma unroll
@@ -526,11 +537,12 @@ __device__ __forceinline__ void chain_segments_fwd(float* s_E, const float* s_D,
 // gradient of the state before it, s_D[q] its decay.  Out: s_R[q][c] = the
 // gradient w.r.t. z at the end of segment q from later segments of the tile,
 // s_Hs[q] = decay of the segments after q, s_Rt[c] / *Hd = the tile's total
-// and its decay; `agg` as above.
+// and its decay; `agg` as above.  Threads 0 .. BP-1 of `tid` work (the
+// caller may offset tid to run this beside the forward chain).
 template <int BP, int NW>
 __device__ __forceinline__ void chain_segments_rev(float* s_R, const float* s_D, float* s_Hs, float* s_Rt,
                                                    float* Hd, uint64_t* agg, uint32_t tag, int tid) {
-  if (tid >= BP) return;
+  if (static_cast<unsigned>(tid) >= static_cast<unsigned>(BP)) return;
   constexpr int RS = BP + kRowPad;
   float r[NW], d[NW];
 #pragma unroll
@@ -666,12 +678,17 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       } else {
         load_row(raw, src, n, bulk, &full[s], lane);
       }
+    }, [&](int ticket) {
+      const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
+      const int b = fast_div(bh, p.div_h), h = bh - b * p.H;
+      tma_prefetch_l2_4d(&tm_x, 0, h, c * Q, b);
     });
     return;
   }
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
     lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Sin2, status, lane,
+                         [](int, int) { return true; },
                          [&](int tile, float(&run)[CPT]) {
                            const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
                            float rdec = 1.f;
@@ -853,6 +870,67 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
+// Per-token table of one backward tile, built by a single warp (the
+// look-back warp, off the compute warps' path): for token t of the tile,
+// tok[tix(t)] = (a_t, a_t, w_t, w_t) and g[tix(t)] = the product of the
+// decays after t through the end of its RUN-token run (1 at the run end).
+// dt form: a_t = exp(dt_t A_h), w_t = dt_t; reference form: a_t =
+// 2^(cs_t - cs_{t-1}), w_t = 1 (ema_fwd_triton's decay between rows,
+// kernels/ema_kernels/ema_fused.py).  Tokens at or past `n` get a = 1, w = 0.
+// Each lane owns Q / 32 consecutive tokens; the suffix product crosses the
+// lanes of a run with shuffles.
+template <int Q, int RUN, int MODE>
+__device__ __forceinline__ void bwd_token_table(const float* raw, float Ah, int n, float4* tok, float2* g,
+                                                int lane) {
+  constexpr int TPL = Q / 32;                          // tokens per lane
+  constexpr int LPR = RUN > TPL ? RUN / TPL : 1;       // lanes per run
+  static_assert(TPL >= 1 && TPL <= RUN && RUN % TPL == 0, "a lane's tokens lie in one run");
+  const int j0 = lane * TPL;
+  float a[TPL], w[TPL];
+#pragma unroll
+  for (int j = 0; j < TPL; ++j) {
+    const int t = j0 + j;
+    a[j] = 1.f;
+    w[j] = 0.f;
+    if (t < n) {
+      if (MODE == kBwdCumsum) {
+        const float prev = (t == 0) ? 0.f : raw[t - 1];
+        a[j] = exp2f(raw[t] - prev);
+        w[j] = 1.f;
+      } else {
+        const float d = raw[t];
+        a[j] = exp2f(d * Ah * kLog2e);
+        w[j] = d;
+      }
+    }
+  }
+  float suf[TPL];  // product of this lane's decays after token j
+  float prod = 1.f;
+#pragma unroll
+  for (int j = TPL - 1; j >= 0; --j) {
+    suf[j] = prod;
+    prod *= a[j];
+  }
+  // product of the decays of the later lanes of the same run
+  float incl = prod;
+#pragma unroll
+  for (int o = 1; o < LPR; o <<= 1) {
+    const float m = __shfl_down_sync(0xffffffffu, incl, o, LPR);
+    if ((lane % LPR) + o < LPR) incl *= m;
+  }
+  float after = __shfl_down_sync(0xffffffffu, incl, 1, LPR);
+  if (lane % LPR == LPR - 1) after = 1.f;
+#pragma unroll
+  for (int j = 0; j < TPL; ++j) {
+    tok[tix<RUN>(j0 + j)] = make_float4(a[j], a[j], w[j], w[j]);
+    g[tix<RUN>(j0 + j)] = f2_bcast(suf[j] * after);
+  }
+}
+
+// Tokens per compute-warp segment of the backward at block headdim BP: the
+// height of the box the host's dx tensor map stores per warp.
+constexpr int bwd_segment_tokens(int BP) { return BP == 64 ? 32 : 16; }
+
 template <typename T, int BP, int Q>
 struct BwdCfg {
   // 4 channels x 16 tokens per lane at BP = 64 (32-token segments: the
@@ -866,14 +944,17 @@ struct BwdCfg {
   static constexpr int NT = NC + 64;
   static_assert((BP == 64 || BP == 128) && Q % SEG == 0 && NC >= BP && NT <= 1024 && NW <= 32 && NW % 2 == 0,
                 "geometry");
+  static_assert(SEG == bwd_segment_tokens(BP), "the host's dx map stores SEG-token boxes");
   static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
   // stage: x tile | dy tile | decay row [Q] | A_h [4] | chunk start state [BP]
   static constexpr int oRaw = 2 * kX;
   static constexpr int oSt = oRaw + (Q + 4) * 4;
   static constexpr int kStage = align_up(oSt + BP * 4, 128);
-  static constexpr int oTok = 0;                           // float4[tix]  (a, a, w, w)
-  static constexpr int oG = oTok + tix_size<RUN>(Q) * 16;         // float2[tix]  decay after t through the run end
-  static constexpr int oE = align_up(oG + tix_size<RUN>(Q) * 8, 16);  // float[NW][BP + pad]  forward prefix -> Zin
+  static constexpr int kTix = tix_size<RUN>(Q);
+  // token tables, one per look-back slot (k % 2): built by the look-back warp
+  static constexpr int oTok = 0;                           // float4[2][tix]  (a, a, w, w)
+  static constexpr int oG = oTok + 2 * kTix * 16;          // float2[2][tix]  decay after t through the run end
+  static constexpr int oE = align_up(oG + 2 * kTix * 8, 16);  // float[NW][BP + pad]  forward prefix -> Zin
   static constexpr int oR = oE + NW * (BP + kRowPad) * 4;  // float[NW][BP + pad]  reverse aggregate -> Rloc
   static constexpr int oD = oR + NW * (BP + kRowPad) * 4;  // float[NW]
   static constexpr int oHs = oD + NW * 4;                  // float[NW]
@@ -882,8 +963,9 @@ struct BwdCfg {
   static constexpr int oMisc = oRt + BP * 4;               // float[8]
   static constexpr int oTile = oMisc + 8 * 4;              // int[kMaxStages]
   static constexpr int oInfo = align_up(oTile + kMaxStages * 4, 16);  // TileInfo[kMaxStages]
-  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));  // full, empty, tid_full, vec_full/empty
-  static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
+  // full, empty, tid_full, vec_full/empty, tok_full
+  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));
+  static constexpr int kPriv = oBar + (3 * kMaxStages + 6) * 8;
   using R = Ring<kStage, kPriv>;
   static constexpr int S = R::S;
   static constexpr int CTAS = R::CTAS;
@@ -894,7 +976,7 @@ struct BwdCfg {
 template <typename T, int BP, int Q, int MODE>
 __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     ema_bwd_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_dy,
-                   const BwdParams p) {
+                   const __grid_constant__ CUtensorMap tm_dx, const BwdParams p) {
   using C = BwdCfg<T, BP, Q>;
   constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
   constexpr int CPL = C::CPL, NPR = C::NPR, RUN = C::RUN;
@@ -916,6 +998,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   uint64_t* tid_full = empty + kMaxStages;
   uint64_t* vec_full = tid_full + kMaxStages;
   uint64_t* vec_empty = vec_full + 2;
+  uint64_t* tok_full = vec_empty + 2;
   __shared__ uint32_t s_epoch, s_last, s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -931,7 +1014,8 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&vec_full[i], 1);
-      mbar_init(&vec_empty[i], NW);
+      mbar_init(&vec_empty[i], NW);  // released once a compute warp's last pass is done with slot i
+      mbar_init(&tok_full[i], 1);
     }
     fence_mbar_init();
   }
@@ -978,12 +1062,29 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       } else {
         for (int i = lane; i < p.P; i += 32) cp_async_4(sst + i, srow + static_cast<long long>(i) * p.st_p);
       }
+    }, [&](int ticket) {
+      const int cr = fast_div(ticket, p.div_bh), bh = ticket - cr * BH;
+      const int c = p.nc - 1 - cr;
+      const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
+      tma_prefetch_l2_4d(&tm_x, 0, h, t0, b);
+      tma_prefetch_l2_4d(&tm_dy, 0, h, t0, b);
     });
     return;
   }
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
     lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Gn2, status, lane,
+                         [&](int k, int s) {
+                           // the tile's token table, once its data has landed
+                           if (!mbar_wait_bounded(&full[s], (k / S) & 1, status)) return false;
+                           const float* raw = reinterpret_cast<const float*>(smem + s * C::kStage + C::oRaw);
+                           const int n = min(Q, p.L - s_info[s].t0);
+                           bwd_token_table<Q, RUN, MODE>(raw, (MODE == kBwdDt) ? raw[Q] : 0.f, n,
+                                                         s_tok + (k & 1) * C::kTix, s_g + (k & 1) * C::kTix, lane);
+                           __syncwarp();
+                           if (lane == 0) mbar_arrive(&tok_full[k & 1]);
+                           return true;
+                         },
                          [&](int tile, float(&run)[CPT]) {
                            const int c = fast_div(tile, p.div_bh), bh = tile - c * BH;
                            float rdec = 1.f;
@@ -1011,10 +1112,6 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   const int ch = cg * CPL;
   const int nch = min(CPL, p.P - ch);
   const unsigned FULL = 0xffffffffu;
-  // this run's per-token entries: r0 is a multiple of RUN, so tix(r0 + u) = tix(r0) + u
-  const float4* tok_r = s_tok + tix<RUN>(r0);
-  const float2* g_r = s_g + tix<RUN>(r0);
-  const long long lane_off = static_cast<long long>(r0) * p.sdx_l + ch;  // within a tile's dx
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!compute_wait(&full[s], (k / S) & 1, status, warp, NC, &s_fail)) break;
@@ -1029,37 +1126,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     const float* raw = reinterpret_cast<const float*>(st + C::oRaw);
     const float* s_Sin = reinterpret_cast<const float*>(st + C::oSt);
     const float Ah = (MODE == kBwdDt) ? raw[Q] : 0.f;
-
-    // ---- this warp's tokens: decay, weight, decay after t within each run -----
-    {
-      const int i = lane & (SEG - 1);
-      const int t = t0 + s0 + i;
-      float a = 1.f, w = 0.f;
-      if (t < p.L) {
-        if (MODE == kBwdCumsum) {
-          const float prev = (s0 + i == 0) ? 0.f : raw[s0 + i - 1];
-          a = exp2f(raw[s0 + i] - prev);
-          w = 1.f;
-        } else {
-          const float d = raw[s0 + i];
-          a = exp2f(d * Ah * kLog2e);
-          w = d;
-        }
-      }
-      float gb = a;  // product of the decays from t through the run end
-#pragma unroll
-      for (int o = 1; o < RUN; o <<= 1) {
-        const float m = __shfl_down_sync(FULL, gb, o, RUN);
-        if ((i & (RUN - 1)) + o < RUN) gb *= m;
-      }
-      float gr = __shfl_down_sync(FULL, gb, 1, RUN);  // decay after t through the run end
-      if ((i & (RUN - 1)) == RUN - 1) gr = 1.f;
-      if (lane < SEG) {
-        s_tok[tix<RUN>(s0 + i)] = make_float4(a, a, w, w);
-        s_g[tix<RUN>(s0 + i)] = f2_bcast(gr);
-      }
-    }
-    __syncwarp();
+    // this run's per-token entries (built by the look-back warp in slot k % 2):
+    // r0 is a multiple of RUN, so tix(r0 + u) = tix(r0) + u
+    const float4* tok_r = s_tok + (k & 1) * C::kTix + tix<RUN>(r0);
+    const float2* g_r = s_g + (k & 1) * C::kTix + tix<RUN>(r0);
+    // a timeout is recorded and acted on at the next block barrier, together
+    if (!mbar_wait_bounded(&tok_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
 
     // ---- pass 1: forward aggregate; local gradients kept in registers ---------
     //   z  <- a_u z + w_u x_u                      (u ascending; only the end value)
@@ -1114,9 +1186,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
 
     // ---- chain segments: Zin (forward, true states) and Rloc (reverse); publish
     const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
+    // the two chains run side by side on different warps where there are enough
+    constexpr int kRevTid = (NC >= 2 * BP) ? BP : 0;
     chain_segments_fwd<BP, NW>(s_E, s_D, nullptr, nullptr, &s_misc[1], s_Sin, p.P, nullptr, 0u, tid);
     chain_segments_rev<BP, NW>(s_R, s_D, s_Hs, s_Rt, &s_misc[0],
-                               (c + 1 < p.nc && has_succ) ? ws.agg + slot * (BP + 1) : nullptr, tag, tid);
+                               (c + 1 < p.nc && has_succ) ? ws.agg + slot * (BP + 1) : nullptr, tag, tid - kRevTid);
     if (warp == NW - 1 && !mbar_wait_bounded(&vec_full[k & 1], (k >> 1) & 1, status) && lane == 0) s_fail = 1u;
     named_sync(1, NC);  // chained segments + the gradient arriving at the tile end
     if (s_fail) break;
@@ -1146,16 +1220,13 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         gend[q] = f2_fma(ds, f2_fma(hs, gn[q], rw[q]), Gexc[q]);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the arriving gradient
     float2 dacc = make_float2(0.f, 0.f);  // dt form: sum over this lane's tokens of dt a G z_{t-1}
     if (p.dx != nullptr) {  // (a state-only pass computes just the gradient at the span start)
       {
-        // running row pointer: one 64-bit add per token
-        const long long dxstep = p.sdx_l;
-        T* const dx_r = static_cast<T*>(p.dx) + ti.out_off + lane_off;
-        T* dxp = dx_r;
-        const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
+        // dx goes over this run's rows of the dy tile (dy is no longer read:
+        // gl holds it), then one TMA store per warp segment (it clips the
+        // rows past seqlen and the channels past headdim)
+        T* const dx_s = const_cast<T*>(s_dy) + r0 * BP + ch;
         const float2 A2 = f2_bcast(Ah);
         float pr[RUN];
 #pragma unroll
@@ -1169,8 +1240,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
             G[q] = f2_fma(gr, gend[q], gl[u][q]);
             dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
           }
-          if (u < nv) store_grp_cs<T, NPR>(dxp, dxv, nch);
-          dxp += dxstep;
+          store_grp<T, NPR>(dx_s + u * BP, dxv);
           load_grp<T, NPR>(x_r + u * BP, xv);
           if (MODE == kBwdCumsum) {
             // dl_t = a_t sum_p G_t z_{t-1}
@@ -1193,12 +1263,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
             pr[u] = m.x + m.y;
           }
         }
-        // the last token's extra gradient is added to the stored dx, as the
+        // the last token's extra gradient is added to the rounded dx, as the
         // reference does after its kernel (dx[:, -1] += d_ox_state)
-        if (p.d_last != nullptr && nv > 0) {
+        if (p.d_last != nullptr && nch > 0) {
           const int ul = p.L - 1 - (t0 + r0);
-          if (ul < RUN) {
-            T* q_dx = dx_r + ul * dxstep;
+          if (ul >= 0 && ul < RUN) {
+            T* q_dx = dx_s + ul * BP;
             const float* dl = p.d_last + static_cast<size_t>(bh) * p.P + ch;
             float2 v[NPR];
             load_grp<T, NPR>(q_dx, v);
@@ -1209,9 +1279,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
                 v[q].y += dl[2 * q + 1];
               }
             }
-            store_grp_cs<T, NPR>(q_dx, v, nch);
+            store_grp<T, NPR>(q_dx, v);
           }
         }
+        fence_proxy_async_smem();  // this lane's dx rows, for the TMA store
+
         const float Pr = group_reduce<RUN, CG>(pr, cg);
         if (cg < RUN) {
           const int gt = t0 + r0 + cg;
@@ -1223,7 +1295,15 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+    if (lane == 0) {
+      if (p.dx != nullptr) {
+        tma_store_4d(&tm_dx, s_dy + s0 * BP, 0, h, t0 + s0, b);
+        bulk_commit();
+        bulk_wait_read<0>();  // the stage may be refilled once the store has read it
+      }
+      mbar_arrive(&empty[s]);         // this warp no longer reads the stage
+      mbar_arrive(&vec_empty[k & 1]);  // nor slot k % 2 (arriving gradient, token table)
+    }
     if (MODE == kBwdDt && p.dx != nullptr) {
       // per-(tile, warp) partial of dA, head-major so that the last CTA sums
       // each head's partials as one contiguous run, in a fixed order
@@ -1233,6 +1313,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       if (lane == 0) ws.partial[((static_cast<size_t>(h) * p.nc + c) * p.B + b) * NW + warp] = dap;
     }
   }
+  if (lane == 0 && p.dx != nullptr) bulk_wait_all();  // this warp's dx stores have landed
   named_sync(1, NC);
   if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
   named_sync(1, NC);
