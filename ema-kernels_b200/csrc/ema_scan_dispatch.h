@@ -46,5 +46,10 @@ constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
 
 // Set the dynamic shared-memory opt-in of `fn` once per device.
 int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask);
+// Tiled tensor map of `rank` dims (dims[0] innermost), byte strides of dims
+// 1..rank-1, box extents; 128-byte swizzle or none.  EMA_OK or an error code
+// with the message set.
+int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
 
 }  // namespace emab

@@ -179,6 +179,30 @@ int map_dispatch_result(int r, const char* what) {
 
 void set_last_error(const char* msg) { g_last_error = msg; }
 
+int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  auto enc = encode_fn();
+  if (!enc) return fail(EMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return fail(EMA_ERR_INVALID_ARGUMENT, "TMA base not 16-byte aligned");
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1u;
+    if (i + 1 < rank) {
+      if (strides_bytes[i] % 16 != 0) return fail(EMA_ERR_INVALID_ARGUMENT, "TMA stride not a multiple of 16 bytes");
+      st[i] = strides_bytes[i];
+    }
+  }
+  CUresult r = enc(m, dt, rank, const_cast<void*>(ptr), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EMA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return EMA_OK;
+}
+
 int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

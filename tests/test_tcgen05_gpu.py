@@ -1,0 +1,38 @@
+"""The tcgen05 operand conventions the SSD kernels are built on, checked on the
+GPU before anything depends on them: 128-byte-swizzled TMA tiles read as
+K-major and MN-major MMA operands, a thread-written swizzled tile, fp32
+accumulation in tensor memory.  Each mode is one 128-row bf16 GEMM compared
+with a float64 product of the same bf16 inputs."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(mode, a, b, n):
+    from kernels import _lib
+    d = torch.full((128, n), float("nan"), device="cuda", dtype=torch.float32)
+    status = torch.zeros(1, device="cuda", dtype=torch.int32)
+    _lib.check(_lib.lib.tc_selftest_gemm(mode, a.data_ptr(), b.data_ptr(), d.data_ptr(), status.data_ptr(),
+                                         _lib.stream_ptr(a.device)), "tc_selftest_gemm")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, "device-side wait timed out"
+    return d
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_tcgen05_gemm_modes(mode):
+    g = torch.Generator(device="cuda").manual_seed(mode)
+    a = torch.randn(128, 128, device="cuda", generator=g).bfloat16()
+    n = 64 if mode == 1 else 128
+    b = torch.randn(128, n, device="cuda", generator=g).bfloat16()
+    if mode == 1:
+        ref = a.double() @ b.double()
+    elif mode == 2:
+        ref = a.double().t() @ b.double()
+    else:
+        b = torch.randn(128, 128, device="cuda", generator=g).bfloat16()
+        ref = a.double() @ b.double().t()
+    d = _run(mode, a.contiguous(), b.contiguous(), n)
+    torch.testing.assert_close(d.double(), ref, rtol=1e-5, atol=1e-4)
