@@ -32,6 +32,8 @@
 
 namespace emab {
 void set_last_error(const char* msg);  // ema_scan_host.cu: text returned by ema_last_error()
+int ssd_fwd_tc_launch(const SsdFwdArgs* a, cudaStream_t stream);  // ssd_fwd_tc.cu
+int ssd_tc_status(uint32_t* out, bool clear, cudaStream_t stream);
 
 namespace ssd {
 
@@ -751,6 +753,9 @@ extern "C" EMA_API int ssd_fwd_launch(const SsdFwdArgs* a, void* stream) {
   for (int i = 0; i < 3; ++i)
     if (a->out_stride[i] % 2 != 0) return fail(EMA_ERR_INVALID_ARGUMENT, "ssd_fwd: out strides must be even");
   if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
+  // the tensor-core kernel covers an even number of heads per group
+  r = emab::ssd_fwd_tc_launch(a, static_cast<cudaStream_t>(stream));
+  if (r != EMA_ERR_UNSUPPORTED) return r;
   Params p{};
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);
@@ -785,6 +790,11 @@ extern "C" EMA_API int ssd_fwd_launch(const SsdFwdArgs* a, void* stream) {
   if (r) return fail(EMA_ERR_CUDA, "ssd_fwd: %s", cudaGetErrorString(static_cast<cudaError_t>(r)));
   ssd_fwd_kernel<<<dim3(p.H, p.B), NTHR, sizeof(FwdSmem), static_cast<cudaStream_t>(stream)>>>(p);
   return launch_check("ssd_fwd");
+}
+
+extern "C" EMA_API int ssd_device_status(uint32_t* status, int clear, void* stream) {
+  if (status == nullptr) return emab::ssd::fail(EMA_ERR_INVALID_ARGUMENT, "ssd_device_status: status is NULL");
+  return emab::ssd_tc_status(status, clear != 0, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" EMA_API int ssd_bwd_launch(const SsdBwdArgs* a, void* stream) {

@@ -18,11 +18,13 @@
  *
  * s_t = exp(dt_t A_h) s_{t-1} + dt_t x_t B_t^T,  y_t = s_t C_t + D_h x_t.
  *
- * Supported: headdim 64, dstate 128, nheads a multiple of ngroups.  The kernels
- * work on 64-token chunks internally whatever chunk_size is given (the result
- * does not depend on it); the forward saves the state entering every internal
- * chunk for the backward in `chunk_states`, fp32 (batch, ssd_internal_chunks,
- * nheads, headdim, dstate).  Launchers allocate nothing and return an EMA_*
+ * Supported: headdim 64, dstate 128, nheads a multiple of ngroups.  The forward
+ * runs on the tcgen05 tensor cores (128-token chunks, two heads per CTA) when
+ * every group has an even number of heads, else on mma.sync tiles; whatever
+ * chunk_size is given (the result does not depend on it), it saves the state
+ * entering every 64-token internal chunk for the backward in `chunk_states`,
+ * fp32 (batch, ssd_internal_chunks, nheads, headdim, dstate), and the backward
+ * walks those 64-token chunks.  Launchers allocate nothing and return an EMA_*
  * status code (ema_ssd_b200.h); ema_last_error() holds the message.
  */
 #ifndef SSD_B200_H_
@@ -88,6 +90,10 @@ EMA_API int ssd_fwd_launch(const SsdFwdArgs* args, void* stream);
  * them on the stream first.  Their summation order is not fixed (atomics), so
  * they are not bitwise reproducible run to run. */
 EMA_API int ssd_bwd_launch(const SsdBwdArgs* args, void* stream);
+/* Error word of the tensor-core SSD kernels (0: none; 2: a bounded wait on the
+ * device timed out; 0x100: misaligned shared memory), read on `stream` after
+ * the work queued before it; zeroed afterwards when `clear` is non-zero. */
+EMA_API int ssd_device_status(uint32_t* status, int clear, void* stream);
 
 #ifdef __cplusplus
 }

@@ -25,7 +25,18 @@ def _f64(t):
     return t.float().double().numpy()
 
 
-@pytest.mark.parametrize("L,H,G,with_states", [(200, 4, 2, True), (128, 2, 1, False), (64, 2, 2, True)])
+def _device_status_clear():
+    import ctypes
+
+    from kernels import _lib
+    v = ctypes.c_uint32(0)
+    _lib.check(_lib.lib.ssd_device_status(ctypes.byref(v), 1, _lib.stream_ptr(torch.device(DEV))), "ssd_device_status")
+    return v.value
+
+
+# (H / G) even -> the tcgen05 forward (128-token chunks, head pairs); odd -> the mma.sync forward
+@pytest.mark.parametrize("L,H,G,with_states", [(200, 4, 2, True), (128, 2, 1, False), (64, 2, 2, True),
+                                               (320, 4, 1, True), (96, 6, 3, False), (130, 3, 3, True)])
 def test_ssd_forward_backward_match_oracle(L, H, G, with_states):
     from kernels.ssd_combined import ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
     B, P, N = 2, 64, 128
@@ -39,12 +50,18 @@ def test_ssd_forward_backward_match_oracle(L, H, G, with_states):
     dfin_t = torch.from_numpy(dfin).to(DEV) if dfin is not None else None
     dx, ddt, dA, dB, dC, dD, dinit = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D, dfin_t, need_d_initial=True)
     torch.cuda.synchronize()
+    assert _device_status_clear() == 0
 
     args = (_f64(tx), tdt.double().numpy(), tA.double().numpy(), _f64(tB), _f64(tC))
     r = so.ssd_fwd(*args, D=tD.double().numpy(), initial_state=s0)
     g = so.ssd_bwd(*args, _f64(tdy), D=tD.double().numpy(), initial_state=s0, d_final_state=dfin)
     assert_lowp_close(y, r["y"], "y")
     assert_lowp_close(fin, r["final_state"], "final_state")
+    # the saved state entering every 64-token chunk (what the backward reads)
+    nc = cst.shape[1]
+    ref_states = np.concatenate([s0[:, None] if s0 is not None else np.zeros((B, 1, H, P, N)),
+                                 r["states"][:, 63::64][:, :nc - 1]], axis=1)
+    assert_lowp_close(cst, ref_states, "chunk_states")
     for name, k in (("dx", dx), ("ddt", ddt), ("dB", dB), ("dC", dC), ("d_initial_state", dinit)):
         assert_lowp_close(k, g[name], name)
         assert_reference_rule(k, g[name], name)
