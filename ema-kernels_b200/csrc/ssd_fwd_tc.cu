@@ -64,9 +64,12 @@ constexpr int oM = oC + 2 * kReg;       // M: 2 heads x 2 key halves x [128 quer
 constexpr int oXw = oM + 4 * kReg;      // x_w: 2 heads x [128 tokens x 64 channels]
 constexpr int oS = oXw + 2 * kReg;      // S (bf16): 2 heads x 2 dstate halves x [64 channels x 64]
 constexpr int oCs = oS + 4 * kReg64;    // float cs[2][128]
-constexpr int oDt = oCs + 2 * Q * 4;    // float dt[2][128]
-constexpr int oBar = oDt + 2 * Q * 4;   // full, mma (u64); taddr, fail (u32)
-constexpr int kSmem = oBar + 24;
+constexpr int oDt = oCs + 2 * Q * 4;    // float dt[2][128], then the key factors (see the cumsum step)
+constexpr int oBar = oDt + 2 * Q * 4;   // full, mma (u64); taddr, fail, wide[2] (u32)
+constexpr int kSmem = oBar + 32;
+// exp(cs_i - cs_j) is factored per 16-key group g as exp(cs_i - cs_g) exp(cs_g - cs_j)
+// (cs_g: the group's first key) unless the cumsum spans more than this inside the group
+constexpr float kWideSpan = 60.f;
 
 // tensor-memory columns
 constexpr uint32_t cCB = 0;    // C B^T, then the state increment dS
@@ -157,6 +160,7 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t* bar_mma = bar_full + 1;
   uint32_t* s_taddr = reinterpret_cast<uint32_t*>(bar_full + 2);
   volatile uint32_t* s_fail = s_taddr + 1;  // a timed-out wait, acted on together after the next barrier
+  uint32_t* s_wide = s_taddr + 2;            // per head: bit g = key group g is not factored
   const uint32_t sbase = smem_u32(smem);
 
   if (tid == 0) {
@@ -264,8 +268,24 @@ __global__ void __launch_bounds__(NT, 1)
         if (lane >= o) incl += v;
       }
       const float excl = incl - run;
+      float cv[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) s_cs[warp * Q + 4 * lane + k] = Ah * (excl + c[k]);
+      for (int k = 0; k < 4; ++k) cv[k] = Ah * (excl + c[k]);
+      // key factors of the 16-token group (4 lanes): exp(cs_g - cs_j) dt_j, or dt_j
+      // itself where the group's cumsum span is too wide to factor in fp32
+      const float cg = __shfl_sync(0xffffffffu, cv[0], lane & ~3);
+      const float ce = __shfl_sync(0xffffffffu, cv[3], lane | 3);
+      const bool wide = fabsf(cg - ce) > kWideSpan;
+      const uint32_t wb = __ballot_sync(0xffffffffu, wide);
+      uint32_t gm = 0;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) gm |= ((wb >> (4 * g)) & 1u) << g;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        s_cs[warp * Q + 4 * lane + k] = cv[k];
+        s_dt[warp * Q + 4 * lane + k] = wide ? d[k] : __expf(cg - cv[k]) * d[k];
+      }
+      if (lane == 0) s_wide[warp] = gm;
     }
     if (tid == 0) bulk_wait_read_all();  // the states staged in the M buffer have been read
     if (tid == 0 && cc + 1 < p.ncq) {  // the next chunk's tiles towards L2
@@ -304,6 +324,7 @@ __global__ void __launch_bounds__(NT, 1)
     {
       const int i = 32 * q + lane;  // query row
       const float ci0 = s_cs[i], ci1 = s_cs[Q + i];
+      const uint32_t wide0 = s_wide[0], wide1 = s_wide[1];
 #pragma unroll 1
       for (int g = 0; g < GPW; ++g) {
         const int j0 = CPW * cw + 16 * g;
@@ -311,12 +332,26 @@ __global__ void __launch_bounds__(NT, 1)
         if (j0 <= 32 * q + 31) {  // warp-uniform: some key of the group is causal for some row of the warp
           tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cCB + j0), v);
           tc::tmem_wait_ld();
+          const int jg = j0 >> 4;
+          if (((wide0 | wide1) >> jg) & 1u) {  // warp-uniform: a wide group, one exp per element
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const int j = j0 + k;
-            const bool causal = j <= i;
-            m0[k] = causal ? v[k] * __expf(ci0 - s_cs[j]) * s_dt[j] : 0.f;
-            m1[k] = causal ? v[k] * __expf(ci1 - s_cs[Q + j]) * s_dt[Q + j] : 0.f;
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + k;
+              const bool causal = j <= i;
+              const float f0 = ((wide0 >> jg) & 1u) ? __expf(ci0 - s_cs[j]) : __expf(ci0 - s_cs[j0]);
+              const float f1 = ((wide1 >> jg) & 1u) ? __expf(ci1 - s_cs[Q + j]) : __expf(ci1 - s_cs[Q + j0]);
+              m0[k] = causal ? v[k] * f0 * s_dt[j] : 0.f;
+              m1[k] = causal ? v[k] * f1 * s_dt[Q + j] : 0.f;
+            }
+          } else {  // one row factor per head: exp(cs_i - cs_j0); the key factors are in s_dt
+            const float r0 = __expf(ci0 - s_cs[j0]), r1 = __expf(ci1 - s_cs[Q + j0]);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + k;
+              const bool causal = j <= i;
+              m0[k] = causal ? v[k] * r0 * s_dt[j] : 0.f;
+              m1[k] = causal ? v[k] * r1 * s_dt[Q + j] : 0.f;
+            }
           }
         } else {
 #pragma unroll
@@ -329,7 +364,8 @@ __global__ void __launch_bounds__(NT, 1)
       constexpr int TPP = NT / 256;  // threads per (token, head)
       const int pr = tid / TPP, j = pr >> 1, hh = pr & 1, xc0 = (tid % TPP) * XPT;
       const int jend = SAVE ? ((j < QH) ? QH - 1 : Q - 1) : Q - 1;
-      const float w = __expf(s_cs[hh * Q + jend] - s_cs[hh * Q + j]) * s_dt[hh * Q + j];
+      const int jref = ((s_wide[hh] >> (j >> 4)) & 1u) ? j : (j & ~15);  // s_dt: dt_j or exp(cs_g - cs_j) dt_j
+      const float w = __expf(s_cs[hh * Q + jend] - s_cs[hh * Q + jref]) * s_dt[hh * Q + j];
 #pragma unroll
       for (int g = 0; g < XPT / 16; ++g) {
         float xv[16];

@@ -92,3 +92,23 @@ def test_mamba_call_form_autograd():
     torch.testing.assert_close(leaves[3].grad, dB.to(torch.bfloat16), rtol=1e-2, atol=1e-2)
     torch.testing.assert_close(leaves[2].grad, dA, rtol=1e-3, atol=1e-3)
     torch.testing.assert_close(leaves[5].grad, dD, rtol=1e-3, atol=1e-3)
+
+
+def test_ssd_forward_steep_decay_matches_oracle():
+    """Large dt * A (cumsum spans over 60 within 16 tokens): the tcgen05 forward's
+    per-element decay path for such key groups, next to the factored one."""
+    from kernels.ssd_combined import ssd_chunk_scan_fwd
+    B, L, H, P, N, G = 1, 192, 2, 64, 128, 1
+    x, dt, A, Bm, Cm, D, _ = so.make_ssd_inputs(B, L, H, P, N, ngroups=G, seed=5, dt_range=(0.05, 2.0))
+    dt[:, :96] *= 0.05  # the first key groups stay narrow
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    tx, tB, tC = bf(x), bf(Bm), bf(Cm)
+    y, cst, fin = ssd_chunk_scan_fwd(tx.to(DEV), torch.from_numpy(dt).to(DEV), torch.from_numpy(A).to(DEV),
+                                     tB.to(DEV), tC.to(DEV), torch.from_numpy(D).to(DEV), return_final_states=True)
+    torch.cuda.synchronize()
+    assert _device_status_clear() == 0
+    r = so.ssd_fwd(_f64(tx), dt.astype(np.float64), A.astype(np.float64), _f64(tB), _f64(tC), D=D.astype(np.float64))
+    assert_lowp_close(y, r["y"], "y")
+    assert_lowp_close(fin, r["final_state"], "final_state")
+    ref_states = np.concatenate([np.zeros((B, 1, H, P, N)), r["states"][:, 63::64][:, :cst.shape[1] - 1]], axis=1)
+    assert_lowp_close(cst, ref_states, "chunk_states")
