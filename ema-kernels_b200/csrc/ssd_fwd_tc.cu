@@ -175,6 +175,17 @@ __global__ void __launch_bounds__(NT, 1)
   tc::fence_after_sync();
   const uint32_t tb = *s_taddr;
   uint32_t mma_phase = 0;
+  // operand descriptors of the fixed shared-memory tiles; a K step or region
+  // offset is added to the start-address field (bytes >> 4, no carry out of it)
+  const uint64_t dKC = tc::smem_desc_sw128(sbase + oC, 16, 1024);    // C, K-major
+  const uint64_t dKB = tc::smem_desc_sw128(sbase + oB, 16, 1024);    // B, K-major
+  const uint64_t dKM = tc::smem_desc_sw128(sbase + oM, 16, 1024);    // M_h, K-major
+  const uint64_t dKS = tc::smem_desc_sw128(sbase + oS, 16, 1024);    // S_h (bf16), K-major
+  const uint64_t dNX = tc::smem_desc_sw128(sbase + oX, kReg, 1024);  // x_h, MN-major
+  const uint64_t dNW = tc::smem_desc_sw128(sbase + oXw, kReg, 1024); // [x_w,h0 ; x_w,h1], MN-major
+  const uint64_t dNB = tc::smem_desc_sw128(sbase + oB, kReg, 1024);  // B, MN-major
+  auto kstep = [](int s) { return static_cast<uint64_t>(((s >> 2) * kReg + (s & 3) * 32) >> 4); };  // K-major
+  auto nstep = [](int s) { return static_cast<uint64_t>((s * 2048) >> 4); };                         // MN-major
 
   auto issue_loads = [&](int cc) {
     const int t0 = cc * Q;
@@ -304,12 +315,8 @@ __global__ void __launch_bounds__(NT, 1)
       if (wait_bar(bar_full, cc & 1, status)) {
         tc::fence_after_sync();
         const uint32_t id = tc::idesc_bf16(128, 128, false, false);
-#pragma unroll 1
-        for (int s = 0; s < 8; ++s) {
-          const uint32_t ko = (s >> 2) * kReg + (s & 3) * 32;
-          tc::mma_bf16(tb + cCB, tc::smem_desc_sw128(sbase + oC + ko, 16, 1024),
-                       tc::smem_desc_sw128(sbase + oB + ko, 16, 1024), id, s > 0);
-        }
+#pragma unroll
+        for (int s = 0; s < 8; ++s) tc::mma_bf16(tb + cCB, dKC + kstep(s), dKB + kstep(s), id, s > 0);
         tc::mma_commit(bar_mma);
       } else {
         *s_fail = 1u;
@@ -387,27 +394,21 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t idy = tc::idesc_bf16(128, 64, false, true);
       const uint32_t idi = tc::idesc_bf16(128, 64, false, false);
       const uint32_t ids = tc::idesc_bf16(128, 128, true, true);
-#pragma unroll 1
+#pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll 1
+        const uint64_t mh = static_cast<uint64_t>((hh * 2 * kReg) >> 4), xh = static_cast<uint64_t>((hh * kReg) >> 4);
+        const uint64_t sh = static_cast<uint64_t>((2 * hh * kReg64) >> 4);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) tc::mma_bf16(tb + cY + 64 * hh, dKM + mh + kstep(s), dNX + xh + nstep(s), idy, s > 0);
+#pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint32_t ko = (s >> 2) * kReg + (s & 3) * 32;
-          tc::mma_bf16(tb + cY + 64 * hh, tc::smem_desc_sw128(sbase + oM + hh * 2 * kReg + ko, 16, 1024),
-                       tc::smem_desc_sw128(sbase + oX + hh * kReg + s * 2048, kReg, 1024), idy, s > 0);
-        }
-#pragma unroll 1
-        for (int s = 0; s < 8; ++s) {
-          const uint32_t ko = (s >> 2) * kReg + (s & 3) * 32;
-          const uint32_t so = (2 * hh + (s >> 2)) * kReg64 + (s & 3) * 32;
-          tc::mma_bf16(tb + cYi + 64 * hh, tc::smem_desc_sw128(sbase + oC + ko, 16, 1024),
-                       tc::smem_desc_sw128(sbase + oS + so, 16, 1024), idi, s > 0);
+          const uint64_t so = static_cast<uint64_t>(((s >> 2) * kReg64 + (s & 3) * 32) >> 4);
+          tc::mma_bf16(tb + cYi + 64 * hh, dKC + kstep(s), dKS + sh + so, idi, s > 0);
         }
       }
-      const int sN = SAVE ? 4 : 8;
-#pragma unroll 1
-      for (int s = 0; s < sN; ++s)
-        tc::mma_bf16(tb + cCB, tc::smem_desc_sw128(sbase + oXw + s * 2048, kReg, 1024),
-                     tc::smem_desc_sw128(sbase + oB + s * 2048, kReg, 1024), ids, s > 0);
+      constexpr int sN = SAVE ? 4 : 8;
+#pragma unroll
+      for (int s = 0; s < sN; ++s) tc::mma_bf16(tb + cCB, dNW + nstep(s), dNB + nstep(s), ids, s > 0);
       tc::mma_commit(bar_mma);
     }
     wait_mma();
@@ -469,15 +470,15 @@ __global__ void __launch_bounds__(NT, 1)
         if (k1 < p.nc64) store_state(k1);
         else bulk_commit();
         const uint32_t ids = tc::idesc_bf16(128, 128, true, true);
-#pragma unroll 1
-        for (int s = 4; s < 8; ++s)
-          tc::mma_bf16(tb + cCB, tc::smem_desc_sw128(sbase + oXw + s * 2048, kReg, 1024),
-                       tc::smem_desc_sw128(sbase + oB + s * 2048, kReg, 1024), ids, s > 4);
+#pragma unroll
+        for (int s = 4; s < 8; ++s) tc::mma_bf16(tb + cCB, dNW + nstep(s), dNB + nstep(s), ids, s > 4);
         tc::mma_commit(bar_mma);
-        bulk_wait_read_all();  // the M buffer is staged into again below
+        bulk_wait_read_all();  // the M buffer is staged into again below, y has left the x tile
       }
       wait_mma();
       __syncthreads();
+      // x, B and C have no reader left in this chunk: the next chunk's tiles load under the state update
+      if (tid == 0 && cc + 1 < p.ncq) issue_loads(cc + 1);
       state_update(__expf(csh[Q - 1] - csh[QH - 1]), true, k2 < p.nc64, fin);
       fence_proxy_async_smem();  // the bf16 state for the next chunk's Yi, the staged state
       tc::fence_before_sync();
@@ -485,7 +486,6 @@ __global__ void __launch_bounds__(NT, 1)
       if (*s_fail) break;
       if (tid == 0) {
         if (k2 < p.nc64) store_state(k2);
-        if (cc + 1 < p.ncq) issue_loads(cc + 1);  // y has left the x tile (waited above)
       }
     } else {
       state_update(__expf(csh[Q - 1]), true, false, fin);
