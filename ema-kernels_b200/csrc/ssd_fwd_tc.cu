@@ -310,24 +310,53 @@ __global__ void __launch_bounds__(NT, 1)
     }
     __syncthreads();
 
-    // ---- CB = C B^T ------------------------------------------------------------
+    // ---- CB = C B^T (committed alone), then Yi_h = C S_h^T ------------------------
+    // Yi needs only C and the carried state, so it runs while the epilogue
+    // builds M; the next commit covers it.
     if (tid == 0) {
       if (wait_bar(bar_full, cc & 1, status)) {
         tc::fence_after_sync();
         const uint32_t id = tc::idesc_bf16(128, 128, false, false);
+        const uint32_t idi = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
         for (int s = 0; s < 8; ++s) tc::mma_bf16(tb + cCB, dKC + kstep(s), dKB + kstep(s), id, s > 0);
         tc::mma_commit(bar_mma);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint64_t sh = static_cast<uint64_t>((2 * hh * kReg64) >> 4);
+#pragma unroll
+          for (int s = 0; s < 8; ++s) {
+            const uint64_t so = static_cast<uint64_t>(((s >> 2) * kReg64 + (s & 3) * 32) >> 4);
+            tc::mma_bf16(tb + cYi + 64 * hh, dKC + kstep(s), dKS + sh + so, idi, s > 0);
+          }
+        }
       } else {
         *s_fail = 1u;
         mbar_arrive(bar_mma);  // nothing issued: release the others
       }
     }
-    wait_mma();
     // the TMA tiles are read by every thread below: observe their completion too
     if (tid != 0 && !wait_bar(bar_full, cc & 1, status)) *s_fail = 1u;
 
-    // ---- M_h (both heads) and x_w ------------------------------------------------
+    // ---- x_w (needs only x), while C B^T runs ----------------------------------------
+    {
+      constexpr int TPP = NT / 256;  // threads per (token, head)
+      const int pr = tid / TPP, j = pr >> 1, hh = pr & 1, xc0 = (tid % TPP) * XPT;
+      const int jend = SAVE ? ((j < QH) ? QH - 1 : Q - 1) : Q - 1;
+      const int jref = ((s_wide[hh] >> (j >> 4)) & 1u) ? j : (j & ~15);  // s_dt: dt_j or exp(cs_g - cs_j) dt_j
+      const float w = __expf(s_cs[hh * Q + jend] - s_cs[hh * Q + jref]) * s_dt[hh * Q + j];
+#pragma unroll
+      for (int g = 0; g < XPT / 16; ++g) {
+        float xv[16];
+        ld_sw16(smem + oX + hh * kReg, j, xc0 + 16 * g, xv);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) xv[k] *= w;
+        st_sw16(smem + oXw + hh * kReg, j, xc0 + 16 * g, xv);
+      }
+    }
+    wait_mma();
+
+    // ---- M_h (both heads) ------------------------------------------------------------
     {
       const int i = 32 * q + lane;  // query row
       const float ci0 = s_cs[i], ci1 = s_cs[Q + i];
@@ -367,20 +396,6 @@ __global__ void __launch_bounds__(NT, 1)
         st_sw16(smem + oM + (0 * 2 + j0 / 64) * kReg, i, j0 % 64, m0);
         st_sw16(smem + oM + (1 * 2 + j0 / 64) * kReg, i, j0 % 64, m1);
       }
-      // x_w: thread -> (token j, head hh, XPT channels)
-      constexpr int TPP = NT / 256;  // threads per (token, head)
-      const int pr = tid / TPP, j = pr >> 1, hh = pr & 1, xc0 = (tid % TPP) * XPT;
-      const int jend = SAVE ? ((j < QH) ? QH - 1 : Q - 1) : Q - 1;
-      const int jref = ((s_wide[hh] >> (j >> 4)) & 1u) ? j : (j & ~15);  // s_dt: dt_j or exp(cs_g - cs_j) dt_j
-      const float w = __expf(s_cs[hh * Q + jend] - s_cs[hh * Q + jref]) * s_dt[hh * Q + j];
-#pragma unroll
-      for (int g = 0; g < XPT / 16; ++g) {
-        float xv[16];
-        ld_sw16(smem + oX + hh * kReg, j, xc0 + 16 * g, xv);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) xv[k] *= w;
-        st_sw16(smem + oXw + hh * kReg, j, xc0 + 16 * g, xv);
-      }
     }
     fence_proxy_async_smem();
     tc::fence_before_sync();
@@ -388,23 +403,16 @@ __global__ void __launch_bounds__(NT, 1)
     if (*s_fail) break;
     if (warp < 2 && cc + 1 < p.ncq) fetch_dt(t0 + Q);  // s_dt has no reader left in this chunk
 
-    // ---- Y_h = M_h x_h, Yi_h = C S_h^T, dS (first half or all) ------------------
+    // ---- Y_h = M_h x_h, dS (first half or all); the commit also covers Yi --------
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t idy = tc::idesc_bf16(128, 64, false, true);
-      const uint32_t idi = tc::idesc_bf16(128, 64, false, false);
       const uint32_t ids = tc::idesc_bf16(128, 128, true, true);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const uint64_t mh = static_cast<uint64_t>((hh * 2 * kReg) >> 4), xh = static_cast<uint64_t>((hh * kReg) >> 4);
-        const uint64_t sh = static_cast<uint64_t>((2 * hh * kReg64) >> 4);
 #pragma unroll
         for (int s = 0; s < 8; ++s) tc::mma_bf16(tb + cY + 64 * hh, dKM + mh + kstep(s), dNX + xh + nstep(s), idy, s > 0);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const uint64_t so = static_cast<uint64_t>(((s >> 2) * kReg64 + (s & 3) * 32) >> 4);
-          tc::mma_bf16(tb + cYi + 64 * hh, dKC + kstep(s), dKS + sh + so, idi, s > 0);
-        }
       }
       constexpr int sN = SAVE ? 4 : 8;
 #pragma unroll
