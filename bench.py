@@ -421,14 +421,15 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     from kernels import _lib
-    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    QB = backward_chunk(Q)  # what the autograd op runs: 128-token backward tiles on half-chunk states
 
     hx, hdt, hA, hdy = _inputs(rank, dev)
     x, dt, A, dy = (t.to(dev) for t in (hx, hdt, hA, hdy))
     if args.mode == "profile":
         for _ in range(max(1, args.steps)):
-            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q)
-            ema_chunk_scan_bwd(x, dt, A, states, dy, Q)
+            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
+            ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
         torch.cuda.synchronize(dev)
         if dist is not None:
             dist.destroy_process_group()
@@ -438,15 +439,15 @@ def main():
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q)
-        ema_chunk_scan_bwd(x, dt, A, states, dy, Q)
+        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
+        ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_fwd, stream=side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q)
+        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
     with torch.cuda.graph(g_bwd, pool=g_fwd.pool(), stream=side):
-        dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, states, dy, Q)
+        dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB, read to clean the L2
 
@@ -572,7 +573,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world, "seq_len": L,
-                       "nheads": H, "headdim": P, "chunk_size": Q,
+                       "nheads": H, "headdim": P, "chunk_size": Q, "backward_chunk": QB,
                        "parallelism": f"batch x heads sharded over {world} GPU(s), no collective",
                        "l2": "flushed before every step outside the timed intervals: 256 MiB write, then "
                              "256 MiB read of another buffer; step inputs 272 MB > 126 MB L2",

@@ -283,6 +283,16 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   p.st_c = a->states_stride[1];
   p.st_h = a->states_stride[2];
   p.st_p = a->states_stride[3];
+  if (a->mid_states != nullptr) {
+    if (!dt_form || seq) return fail(EMA_ERR_UNSUPPORTED, "mid_states: dt form without seq_idx only");
+    if (Q % 2 != 0 || (Q / 2) % fwd_segment_tokens(BP) != 0)
+      return fail(EMA_ERR_UNSUPPORTED, "mid_states: chunk_size / 2 must be a multiple of %d", fwd_segment_tokens(BP));
+  }
+  p.mid_states = a->mid_states;
+  p.sm_b = a->mid_states_stride[0];
+  p.sm_c = a->mid_states_stride[1];
+  p.sm_h = a->mid_states_stride[2];
+  p.sm_p = a->mid_states_stride[3];
   p.da_cs = a->da_cs;
   p.da_cs_sum = a->da_cs_sum;
   p.final_state = a->final_state;

@@ -112,6 +112,8 @@ struct FwdParams {
   const float* init;  // (B,H,P)
   float* states;
   long long st_b, st_c, st_h, st_p;
+  float* mid_states;  // state entering token Q/2 of each chunk, or null
+  long long sm_b, sm_c, sm_h, sm_p;
   float* da_cs;      // (B,H,L)
   float* da_cs_sum;  // (B,H,nc)
   float* final_state;
@@ -572,6 +574,9 @@ __device__ __forceinline__ void chain_segments_rev(float* s_R, const float* s_D,
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
+// Tokens per compute-warp segment of the forward at block headdim BP.
+constexpr int fwd_segment_tokens(int BP) { return BP == 64 ? 32 : 16; }
+
 template <typename T, int BP, int Q>
 struct FwdCfg {
   static constexpr int CPL = 8;  // channels per compute lane
@@ -582,6 +587,7 @@ struct FwdCfg {
   static constexpr int NC = NW * 32;   // compute threads
   static constexpr int NT = NC + 64;   // + producer warp + look-back warp
   static_assert((BP == 64 || BP == 128) && Q % SEG == 0 && NC >= BP && NC >= Q && NW <= 32, "geometry");
+  static_assert(SEG == fwd_segment_tokens(BP), "segment size known to the host");
   static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
   static constexpr int kStage = align_up(kX + (Q + 4) * 4, 128);  // x tile | decay row | A_h
   // per-CTA state after the ring
@@ -833,6 +839,9 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       }
       if (p.states != nullptr && tid < p.P)
         p.states[b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h + tid * p.st_p] = s_Sin[tid];
+      if (p.mid_states != nullptr && tid < p.P)  // the state entering segment NW/2 = token Q/2
+        p.mid_states[b * p.sm_b + static_cast<long long>(c) * p.sm_c + h * p.sm_h + tid * p.sm_p] =
+            fmaf(s_G0[NW / 2], s_Sin[tid], s_E[(NW / 2) * (BP + kRowPad) + tid]);
     }
 
     // ---- pass 2: y = local scan + (run decay so far) x (state entering the run)

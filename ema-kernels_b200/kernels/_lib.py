@@ -51,6 +51,7 @@ class EmaFwdArgs(ctypes.Structure):
         ("states", _ptr), ("states_stride", _i64 * 4),
         ("da_cs", _ptr), ("da_cs_sum", _ptr), ("final_state", _ptr),
         ("workspace", _ptr), ("workspace_bytes", ctypes.c_size_t),
+        ("mid_states", _ptr), ("mid_states_stride", _i64 * 4),
     ]
 
 

@@ -43,12 +43,18 @@ def _check_inputs(x, dt, A, chunk_size):
 
 def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
                        initial_states: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                       return_final_states: bool = False, state_only: bool = False):
+                       return_final_states: bool = False, state_only: bool = False,
+                       half_chunk_states: bool = False):
     """Forward.  Returns (y, chunk_start_states (B, nchunks, H, P) fp32, final_states or None).
 
     ``state_only``: compute only the final state (y and the chunk states are not
     written; returns (None, None, final)) -- the first pass of the sequence-
-    parallel forward, which reads x once and writes nothing else."""
+    parallel forward, which reads x once and writes nothing else.
+
+    ``half_chunk_states``: the states returned are those entering every
+    chunk_size / 2 tokens, (B, ceil(L / (chunk_size / 2)), H, P) -- what
+    ``ema_chunk_scan_bwd`` takes with ``chunk_size // 2`` (chunk c's start
+    state at index 2c)."""
     B, L, H, P = _check_inputs(x, dt, A, chunk_size)
     dev = x.device
     nc = -(-L // chunk_size)
@@ -63,6 +69,10 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
     if out is not None:
         assert out.shape == x.shape and out.dtype == x.dtype and _lib.tma_ok(out), "out must match x"
     states = None if state_only else torch.empty(B, nc, H, P, dtype=torch.float32, device=dev)
+    mid = None
+    if half_chunk_states and not state_only:
+        fine = torch.empty(B, 2 * nc, H, P, dtype=torch.float32, device=dev)
+        states, mid = fine[:, 0::2], fine[:, 1::2]
     final = torch.empty(B, H, P, dtype=torch.float32, device=dev) if return_final_states else None
     init = None
     if initial_states is not None:
@@ -71,7 +81,7 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
     if x.numel() == 0:
         if final is not None:
             final.copy_(init if init is not None else torch.zeros_like(final))
-        return out, states, final
+        return out, (fine[:, :-(-L // (chunk_size // 2))] if mid is not None else states), final
     ws = _lib.workspace(dev, _lib.lib.ema_scan_workspace_size(B, L, H, P, chunk_size))
     a = _lib.EmaFwdArgs()
     a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
@@ -84,10 +94,15 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
     if states is not None:
         s = states.stride()
         a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
+    if mid is not None:
+        s = mid.stride()
+        a.mid_states, a.mid_states_stride = mid.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
     a.final_state = _lib.ptr(final)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.ema_fwd_launch(a, _lib.stream_ptr(dev)), "ema_chunk_scan_fwd")
+    if mid is not None:  # the chunk-start states of chunk_size / 2 (a short last chunk has no mid)
+        states = fine[:, :-(-L // (chunk_size // 2))]
     return out, states, final
 
 
@@ -144,13 +159,22 @@ def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, state
     return dx, ddt, dA, d_init
 
 
+def backward_chunk(chunk_size: int) -> int:
+    """Tile length the backward runs on for a forward of ``chunk_size``: 256-token
+    forwards hand the backward 128-token chunk states (two backward CTAs per SM,
+    measured faster on B200); otherwise the same length."""
+    return 128 if chunk_size == 256 else chunk_size
+
+
 class EmaChunkScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, dt, A, chunk_size, initial_states, return_final_states):
+        bq = backward_chunk(chunk_size)
         y, states, final = ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states,
-                                              return_final_states=return_final_states)
+                                              return_final_states=return_final_states,
+                                              half_chunk_states=bq != chunk_size)
         ctx.save_for_backward(x, dt, A, states)
-        ctx.chunk_size = chunk_size
+        ctx.chunk_size = bq
         ctx.has_init = initial_states is not None
         ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
         if return_final_states:

@@ -85,6 +85,12 @@ typedef struct EmaFwdArgs {
   float* final_state;    /* (B,H,P) contiguous or NULL */
   void* workspace;
   size_t workspace_bytes;
+  /* Not in the reference interface: the state entering token chunk_size / 2 of
+   * every chunk, or NULL (dt form only, no seq_idx).  Interleaved with `states`
+   * (chunk c at index 2c, its mid state at 2c + 1) it is the chunk-start state
+   * array of chunk_size / 2, so the backward can run on half-size chunks. */
+  float* mid_states;
+  int64_t mid_states_stride[4];
 } EmaFwdArgs;
 
 /* ---- EMA backward ---------------------------------------------------------

@@ -252,3 +252,42 @@ def test_state_only_passes_and_span_chaining(dtype):
     check(dx_sp, dx_full.float().cpu().numpy(), "span-chained dx")
     check(ddt_sp, ddt_full.cpu().numpy(), "span-chained ddt")
     check(dA_sp, dA_full.cpu().numpy(), "span-chained dA")
+
+
+@pytest.mark.parametrize("P,L", [(64, 1000), (128, 700), (64, 256), (64, 600)])
+def test_half_chunk_states_feed_the_half_chunk_backward(P, L):
+    """A 256-token forward with half_chunk_states returns the state entering
+    every 128 tokens (chunk c's start at 2c, matching the 128-token forward's
+    states); the backward on those 128-token chunks matches the oracle.  This
+    is the pair the autograd op runs at chunk_size 256."""
+    from kernels.ema_chunk_scan import (backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_combined,
+                                        ema_chunk_scan_fwd)
+    assert backward_chunk(256) == 128
+    tx, tdt, tA, tdy = _inputs(2, L, 3, P, 31 + L, torch.float32)
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    rng = np.random.default_rng(3)
+    init = torch.from_numpy(rng.standard_normal((2, 3, P)).astype(np.float32)).to(DEV)
+    y, fine, fin = ema_chunk_scan_fwd(x, dt, A, 256, initial_states=init, return_final_states=True,
+                                      half_chunk_states=True)
+    y128, st128, fin128 = ema_chunk_scan_fwd(x, dt, A, 128, initial_states=init, return_final_states=True)
+    nc128 = -(-L // 128)
+    assert fine.shape == (2, nc128, 3, P)
+    assert_fp32_close(fine, st128, "half-chunk states")
+    assert_fp32_close(y, y128, "y")
+    dfin = torch.from_numpy(rng.standard_normal((2, 3, P)).astype(np.float32)).to(DEV)
+    g128 = ema_chunk_scan_bwd(x, dt, A, fine, dy, 128, d_final_states=dfin, need_d_initial=True)
+    # the same backward on the 128-token forward's states (headdim 128 has no
+    # 256-token backward: its tiles do not fit in shared memory)
+    gref = ema_chunk_scan_bwd(x, dt, A, st128, dy, 128, d_final_states=dfin, need_d_initial=True)
+    for name, a, b in zip(("dx", "ddt", "dA", "d_init"), g128, gref):
+        assert_fp32_close(a, b, name)
+    g = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy(), initial_state=init.cpu().numpy(),
+                      d_final_state=dfin.cpu().numpy())
+    assert_fp32_close(g128[0], g["dx"], "dx vs oracle")
+    assert_fp32_close(g128[1], g["ddt"], "ddt vs oracle")
+    # the autograd op at chunk 256 (which takes this path) agrees too
+    xg = x.clone().requires_grad_()
+    yy = ema_chunk_scan_combined(xg, dt, A, chunk_size=256)
+    (yy * dy).sum().backward()
+    g0 = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy())
+    assert_fp32_close(xg.grad, g0["dx"], "autograd dx")
