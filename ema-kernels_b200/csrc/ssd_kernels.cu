@@ -184,6 +184,43 @@ __device__ __forceinline__ void load_tile(const bf16* src, long long gstride, in
   }
 }
 
+// The same for a tile whose shape is known at compile time: every load of the
+// thread is issued before any store, so the tile costs one memory round trip.
+template <int ROWS, int COLS>
+__device__ __forceinline__ void load_tile_batched(const bf16* src, long long gstride, int nvalid, bf16* dst, int ld,
+                                                  bf16* dstT, int ldT) {
+  constexpr int PER_ROW = COLS / 8, PER = ROWS * PER_ROW / NTHR;
+  static_assert(ROWS * PER_ROW % NTHR == 0, "whole iterations");
+  uint4 v[PER];
+#pragma unroll
+  for (int it = 0; it < PER; ++it) {
+    const int idx = threadIdx.x + it * NTHR, r = idx / PER_ROW, c8 = (idx - r * PER_ROW) * 8;
+    v[it] = (r < nvalid) ? __ldg(reinterpret_cast<const uint4*>(src + r * gstride + c8)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int it = 0; it < PER; ++it) {
+    const int idx = threadIdx.x + it * NTHR, r = idx / PER_ROW, c8 = (idx - r * PER_ROW) * 8;
+    *reinterpret_cast<uint4*>(dst + r * ld + c8) = v[it];
+    if (dstT != nullptr) {
+      const bf16* e = reinterpret_cast<const bf16*>(&v[it]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dstT[(c8 + k) * ldT + r] = e[k];
+    }
+  }
+}
+
+// L2 prefetch of `rows` rows of `bytes_per_row` (a multiple of 128) from `src`
+// with stride `gstride_bytes`, spread over the CTA's threads.
+__device__ __forceinline__ void prefetch_rows_l2(const void* src, long long gstride_bytes, int rows, int nvalid,
+                                                 int bytes_per_row) {
+  const int lines = bytes_per_row / 128;
+  for (int idx = threadIdx.x; idx < rows * lines; idx += NTHR) {
+    const int r = idx / lines, l = idx - r * lines;
+    if (r < nvalid)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char*>(src) + r * gstride_bytes + l * 128));
+  }
+}
+
 // Inclusive cumsum of v[0..63] by one warp (two elements per lane).
 __device__ __forceinline__ void warp_cumsum64(float* cs, const float* v, float scale, int lane) {
   float a = v[lane] * scale, b = v[32 + lane] * scale;
@@ -415,15 +452,15 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
   for (int c = p.nc - 1; c >= 0; --c) {
     const int t0 = c * Q;
     const int nq = min(Q, p.L - t0);
-    // ---- stage the chunk -------------------------------------------------
-    load_tile(p.x + b * p.sx_b + static_cast<long long>(t0) * p.sx_l + h * p.sx_h, p.sx_l, Q, P, nq, sm.x, LP,
-              nullptr, 0);
-    load_tile(p.dy + b * p.sdy_b + static_cast<long long>(t0) * p.sdy_l + h * p.sdy_h, p.sdy_l, Q, P, nq, sm.dy,
-              LP, sm.dyT, LQ);
-    load_tile(p.Bm + b * p.sb_b + static_cast<long long>(t0) * p.sb_l + grp * p.sb_g, p.sb_l, Q, N, nq, sm.Bm,
-              LN, sm.BT, LQ);
-    load_tile(p.Cm + b * p.sc_b + static_cast<long long>(t0) * p.sc_l + grp * p.sc_g, p.sc_l, Q, N, nq, sm.Cm,
-              LN, sm.CT, LQ);
+    // ---- stage the chunk (one memory round trip per tile) -----------------
+    load_tile_batched<Q, P>(p.x + b * p.sx_b + static_cast<long long>(t0) * p.sx_l + h * p.sx_h, p.sx_l, nq, sm.x,
+                            LP, nullptr, 0);
+    load_tile_batched<Q, P>(p.dy + b * p.sdy_b + static_cast<long long>(t0) * p.sdy_l + h * p.sdy_h, p.sdy_l, nq,
+                            sm.dy, LP, sm.dyT, LQ);
+    load_tile_batched<Q, N>(p.Bm + b * p.sb_b + static_cast<long long>(t0) * p.sb_l + grp * p.sb_g, p.sb_l, nq,
+                            sm.Bm, LN, sm.BT, LQ);
+    load_tile_batched<Q, N>(p.Cm + b * p.sc_b + static_cast<long long>(t0) * p.sc_l + grp * p.sc_g, p.sc_l, nq,
+                            sm.Cm, LN, sm.CT, LQ);
     if (tid < Q) {
       sm.dtv[tid] = (tid < nq) ? p.dt[(static_cast<size_t>(b) * p.L + t0 + tid) * p.H + h] : 0.f;
       sm.rowT[tid] = sm.colT[tid] = sm.colR[tid] = sm.inter[tid] = sm.V[tid] = 0.f;
@@ -433,12 +470,20 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
       // the state entering the chunk (transposed bf16) and sum dS . Sin over this thread's fragment
       const float* sin = p.chunk_states + ((static_cast<size_t>(b) * p.nc + c) * p.H + h) * P * N;
       float part = 0.f;
+      float2 svs[8][2];  // all of this thread's loads first: one round trip
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int r = 0; r < 4; r += 2) {
           const int pp = p0 + gq + 8 * (r >> 1), nn = n0 + nt * 8 + 2 * q4;
-          const float2 sv = *reinterpret_cast<const float2*>(sin + pp * N + nn);
+          svs[nt][r >> 1] = __ldg(reinterpret_cast<const float2*>(sin + pp * N + nn));
+        }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; r += 2) {
+          const int pp = p0 + gq + 8 * (r >> 1), nn = n0 + nt * 8 + 2 * q4;
+          const float2 sv = svs[nt][r >> 1];
           part = fmaf(ds[nt][r], sv.x, fmaf(ds[nt][r + 1], sv.y, part));
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -459,6 +504,18 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
     }
     __syncthreads();
     if (warp == 0) warp_cumsum64(sm.cs, sm.dtv, Ah, lane);
+    if (c > 0) {  // the next chunk (towards 0) into L2 while this one computes
+      const int tp = t0 - Q;
+      prefetch_rows_l2(p.x + b * p.sx_b + static_cast<long long>(tp) * p.sx_l + h * p.sx_h, p.sx_l * 2, Q, Q, P * 2);
+      prefetch_rows_l2(p.dy + b * p.sdy_b + static_cast<long long>(tp) * p.sdy_l + h * p.sdy_h, p.sdy_l * 2, Q, Q,
+                       P * 2);
+      prefetch_rows_l2(p.Bm + b * p.sb_b + static_cast<long long>(tp) * p.sb_l + grp * p.sb_g, p.sb_l * 2, Q, Q,
+                       N * 2);
+      prefetch_rows_l2(p.Cm + b * p.sc_b + static_cast<long long>(tp) * p.sc_l + grp * p.sc_g, p.sc_l * 2, Q, Q,
+                       N * 2);
+      prefetch_rows_l2(p.chunk_states + ((static_cast<size_t>(b) * p.nc + c - 1) * p.H + h) * P * N, 512, P, P,
+                       N * 4);
+    }
     __syncthreads();
     const float cs_end = sm.cs[Q - 1];
     // ---- CB = C B^T and DX = dy x^T -> MtT, ET, Ed and the dcs / ddt sums ---------

@@ -8,6 +8,9 @@
 //   mode 1: D[128x64]  = A X,    X (128 x 64) row-major: N contiguous (MN-major B)
 //   mode 2: D[128x128] = X^T Y,  X, Y (128 x 128) row-major: M / N contiguous (MN-major A and B)
 //   mode 3: mode 0 with A written into shared memory by the threads
+//   mode 4: an M = 64 MMA, D[64x64] = A B^T (A, B 64 x 128, K-major), written
+//           into zeroed tensor memory; all 128 lanes x 64 columns are read
+//           back, which shows where the 64 rows of D live
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,7 +36,9 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ uint64_t full, done;
   __shared__ uint32_t s_taddr;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int N = (mode == 1) ? 64 : 128;
+  const int N = (mode == 1 || mode == 4) ? 64 : 128;
+  const int R = (mode == 4) ? 64 : 128;  // operand rows
+  const int reg = R * 128;               // bytes of one 64-column region
   if (tid == 0) {
     mbar_init(&full, 1);
     mbar_init(&done, 1);
@@ -52,18 +57,28 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = s_taddr;
+  {  // zero the accumulator columns of every lane
+    float z[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) z[i] = 0.f;
+    for (int c0 = 0; c0 < 128; c0 += 16) tc::tmem_st16(tc::tmem_at(tbase, 32 * warp, c0), z);
+    tc::tmem_wait_st();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
   if (tid == 0) {
-    const uint32_t bytes = (mode == 3 ? 0u : 2u * kRegion) + (mode == 1 ? 1u * kRegion : 2u * kRegion);
+    const uint32_t bytes = (mode == 3 ? 0u : 2u * reg) + (mode == 1 ? 1u * kRegion : 2u * reg);
     mbar_arrive_expect_tx(&full, bytes);
     if (mode != 3) {
       tc::tma_load_2d(sa, &ma, &full, 0, 0);
-      tc::tma_load_2d(sa + kRegion, &ma, &full, 64, 0);
+      tc::tma_load_2d(sa + reg, &ma, &full, 64, 0);
     }
     if (mode == 1) {
       tc::tma_load_2d(sb, &mb, &full, 0, 0);  // 128 rows x 64 columns: one region of 16 KB
     } else {
       tc::tma_load_2d(sb, &mb, &full, 0, 0);
-      tc::tma_load_2d(sb + kRegion, &mb, &full, 64, 0);
+      tc::tma_load_2d(sb + reg, &mb, &full, 64, 0);
     }
     if (mbar_wait_bounded(&full, 0, status)) {
       tc::fence_after_sync();
@@ -71,6 +86,7 @@ __global__ void __launch_bounds__(128, 1)
       uint32_t idesc;
       if (mode == 1) idesc = tc::idesc_bf16(128, 64, false, true);
       else if (mode == 2) idesc = tc::idesc_bf16(128, 128, true, true);
+      else if (mode == 4) idesc = tc::idesc_bf16(64, 64, false, false);
       else idesc = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll 1
       for (int s = 0; s < 8; ++s) {  // K = 128 in steps of 16
@@ -79,9 +95,9 @@ __global__ void __launch_bounds__(128, 1)
           da = tc::smem_desc_sw128(a0 + s * 2048, kRegion, 1024);
           db = tc::smem_desc_sw128(b0 + s * 2048, kRegion, 1024);
         } else {
-          da = tc::smem_desc_sw128(a0 + (s / 4) * kRegion + (s % 4) * 32, 16, 1024);
+          da = tc::smem_desc_sw128(a0 + (s / 4) * reg + (s % 4) * 32, 16, 1024);
           db = (mode == 1) ? tc::smem_desc_sw128(b0 + s * 2048, kRegion, 1024)
-                           : tc::smem_desc_sw128(b0 + (s / 4) * kRegion + (s % 4) * 32, 16, 1024);
+                           : tc::smem_desc_sw128(b0 + (s / 4) * reg + (s % 4) * 32, 16, 1024);
         }
         tc::mma_bf16(tbase, da, db, idesc, s > 0);
       }
@@ -119,7 +135,7 @@ using namespace emab;
 
 extern "C" EMA_API int tc_selftest_gemm(int mode, const void* a, const void* b, float* d, uint32_t* status,
                                         void* stream) {
-  if (mode < 0 || mode > 3 || !a || !b || !d || !status) {
+  if (mode < 0 || mode > 4 || !a || !b || !d || !status) {
     set_last_error("tc_selftest_gemm: bad arguments");
     return EMA_ERR_INVALID_ARGUMENT;
   }
@@ -129,7 +145,13 @@ extern "C" EMA_API int tc_selftest_gemm(int mode, const void* a, const void* b, 
   const uint32_t box[2] = {64, 128};
   int r = encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, dims128, st256, box, true);
   if (r) return r;
-  if (mode == 1) {
+  if (mode == 4) {
+    const uint64_t d64[2] = {128, 64};
+    const uint32_t box64[2] = {64, 64};
+    r = encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, d64, st256, box64, true);
+    if (r) return r;
+    r = encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, d64, st256, box64, true);
+  } else if (mode == 1) {
     const uint64_t dims64[2] = {64, 128};
     const uint64_t st128[1] = {128};
     r = encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, dims64, st128, box, true);

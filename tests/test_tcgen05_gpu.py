@@ -36,3 +36,18 @@ def test_tcgen05_gemm_modes(mode):
         ref = a.double() @ b.double().t()
     d = _run(mode, a.contiguous(), b.contiguous(), n)
     torch.testing.assert_close(d.double(), ref, rtol=1e-5, atol=1e-4)
+
+
+def test_tcgen05_m64_accumulator_lanes():
+    """An M = 64 MMA (cta_group::1) writes row r of D to tensor-memory lane
+    32 (r // 16) + r % 16: the first 16 lanes of each warp's lane quarter."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    a = torch.randn(64, 128, device="cuda", generator=g).bfloat16().contiguous()
+    b = torch.randn(64, 128, device="cuda", generator=g).bfloat16().contiguous()
+    d = _run(4, a, b, 64)  # all 128 lanes x 64 columns, zeroed before the MMA
+    ref = a.double() @ b.double().t()
+    lanes = torch.tensor([32 * (r // 16) + r % 16 for r in range(64)], device="cuda")
+    torch.testing.assert_close(d[lanes].double(), ref, rtol=1e-5, atol=1e-4)
+    others = torch.ones(128, dtype=torch.bool, device="cuda")
+    others[lanes] = False
+    assert float(d[others].abs().max()) == 0.0
