@@ -99,32 +99,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_
   return mbar_wait_bounded(bar, parity, status);
 }
 
-// Store 16 floats as bf16 into a swizzled 64-column region at (row, col0..col0+15).
-__device__ __forceinline__ void st_sw16(unsigned char* region, int row, int col0, const float (&v)[16]) {
-  uint4 a, b;
-  a.x = pack_pair<bf16>(make_float2(v[0], v[1]));
-  a.y = pack_pair<bf16>(make_float2(v[2], v[3]));
-  a.z = pack_pair<bf16>(make_float2(v[4], v[5]));
-  a.w = pack_pair<bf16>(make_float2(v[6], v[7]));
-  b.x = pack_pair<bf16>(make_float2(v[8], v[9]));
-  b.y = pack_pair<bf16>(make_float2(v[10], v[11]));
-  b.z = pack_pair<bf16>(make_float2(v[12], v[13]));
-  b.w = pack_pair<bf16>(make_float2(v[14], v[15]));
-  *reinterpret_cast<uint4*>(region + tc::sw128_offset(row, col0)) = a;
-  *reinterpret_cast<uint4*>(region + tc::sw128_offset(row, col0 + 8)) = b;
-}
-// Load 16 bf16 from a swizzled region as floats.
-__device__ __forceinline__ void ld_sw16(const unsigned char* region, int row, int col0, float (&v)[16]) {
-  const uint4 a = *reinterpret_cast<const uint4*>(region + tc::sw128_offset(row, col0));
-  const uint4 b = *reinterpret_cast<const uint4*>(region + tc::sw128_offset(row, col0 + 8));
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float2 f = cvt_pair<bf16>(w[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
+using tc::st_sw16;
+using tc::ld_sw16;
 
 // Stage 16 floats of state row `row` (columns n0 .. n0 + 15) into four
 // 128-row x 32-float regions (128-byte swizzle), the layout a TMA store with
@@ -610,6 +586,11 @@ int ssd_fwd_tc_launch(const SsdFwdArgs* a, cudaStream_t stream) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "ssd_fwd launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
+}
+
+uint32_t* ssd_tc_status_device_ptr() {
+  void* ptr = nullptr;
+  return cudaGetSymbolAddress(&ptr, ssdtc::g_status) == cudaSuccess ? static_cast<uint32_t*>(ptr) : nullptr;
 }
 
 // Device status of the tensor-core SSD kernels (bit 1: a wait timed out, bit 2:

@@ -34,6 +34,7 @@ namespace emab {
 void set_last_error(const char* msg);  // ema_scan_host.cu: text returned by ema_last_error()
 int ssd_fwd_tc_launch(const SsdFwdArgs* a, cudaStream_t stream);  // ssd_fwd_tc.cu
 int ssd_tc_status(uint32_t* out, bool clear, cudaStream_t stream);
+int ssd_bwd_tc_launch(const SsdBwdArgs* a, cudaStream_t stream);  // ssd_bwd_tc.cu
 
 namespace ssd {
 
@@ -878,6 +879,9 @@ extern "C" EMA_API int ssd_bwd_launch(const SsdBwdArgs* a, void* stream) {
   if (e == cudaSuccess && a->dD != nullptr) e = cudaMemsetAsync(a->dD, 0, a->nheads * sizeof(float), s);
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "ssd_bwd: %s", cudaGetErrorString(e));
   if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
+  // the tensor-core kernel, wherever its TMA and vector-store alignment holds
+  r = emab::ssd_bwd_tc_launch(a, s);
+  if (r != EMA_ERR_UNSUPPORTED) return r;
   Params p{};
   p.B = static_cast<int>(a->batch);
   p.L = static_cast<int>(a->seqlen);

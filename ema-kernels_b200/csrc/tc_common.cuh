@@ -19,6 +19,7 @@
 //    warp w of a warpgroup reads lanes [32 (w % 4), 32 (w % 4) + 32).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +34,33 @@ namespace tc {
 __device__ __forceinline__ uint32_t sw128_offset(int row, int col) {
   const uint32_t o = static_cast<uint32_t>(row) * 128u + static_cast<uint32_t>(col) * 2u;
   return o ^ (((o >> 7) & 7u) << 4);
+}
+
+// Store 16 floats as bf16 into a swizzled 64-column region at (row, col0..col0+15).
+__device__ __forceinline__ void st_sw16(unsigned char* region, int row, int col0, const float (&v)[16]) {
+  uint4 a, b;
+  a.x = pack_pair<__nv_bfloat16>(make_float2(v[0], v[1]));
+  a.y = pack_pair<__nv_bfloat16>(make_float2(v[2], v[3]));
+  a.z = pack_pair<__nv_bfloat16>(make_float2(v[4], v[5]));
+  a.w = pack_pair<__nv_bfloat16>(make_float2(v[6], v[7]));
+  b.x = pack_pair<__nv_bfloat16>(make_float2(v[8], v[9]));
+  b.y = pack_pair<__nv_bfloat16>(make_float2(v[10], v[11]));
+  b.z = pack_pair<__nv_bfloat16>(make_float2(v[12], v[13]));
+  b.w = pack_pair<__nv_bfloat16>(make_float2(v[14], v[15]));
+  *reinterpret_cast<uint4*>(region + sw128_offset(row, col0)) = a;
+  *reinterpret_cast<uint4*>(region + sw128_offset(row, col0 + 8)) = b;
+}
+// Load 16 bf16 from a swizzled region as floats.
+__device__ __forceinline__ void ld_sw16(const unsigned char* region, int row, int col0, float (&v)[16]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(region + sw128_offset(row, col0));
+  const uint4 b = *reinterpret_cast<const uint4*>(region + sw128_offset(row, col0 + 8));
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = cvt_pair<__nv_bfloat16>(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
 }
 
 // ---- descriptors -----------------------------------------------------------
