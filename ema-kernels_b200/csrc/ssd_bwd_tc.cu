@@ -12,10 +12,10 @@
 //             -> Mq = CB a dt, E = a DX, Ed = a DX dt (bf16 operand tiles), the
 //                row / column sums of T = CB a dt DX and R = CB a DX, the
 //                per-token terms inter_i = e_i G8_i . C_i and V_j, and dC += e G8
-//   phase 2   dXi = Mq^T dy, dBi = E^T C
-//             -> dx = dXi + w dXs + D dy, dB += dt dBi
-//   phase 3   dBs = x dS, G7 = Ed B, G9 = (e dy)^T C (head + residual)
-//             -> dB += w dBs, dC += G7, dS = exp(cs_end) dS + G9
+//   phase 2   dXi = Mq^T dy, dB = Ed^T C + x_w dS (x_w = w x, one accumulator)
+//             -> dx = dXi + w dXs + D dy, dB (one atomic pass)
+//   phase 3   G7 = Ed B, G9 = (e dy)^T C (head + residual)
+//             -> dC += G7, dS = exp(cs_end) dS + G9
 //   then      dcs, its reverse cumsum within the chunk, ddt and dA (one warp).
 //
 // Every operand is an M = 64 tile (token or headdim rows): D row r lives in
@@ -64,14 +64,17 @@ constexpr int oSL = oSH + 2 * R64;  // Sin bf16 residual
 constexpr int oDH = oSL + 2 * R64;  // dS bf16 head  [64 p][128 n]
 constexpr int oDL = oDH + 2 * R64;  // dS bf16 residual
 constexpr int oMq = oDL + 2 * R64;  // CB a dt [64 i][64 j]
-constexpr int oE = oMq + R64;       // a DX
-constexpr int oEd = oE + R64;       // a DX dt
+constexpr int oXW = oMq + R64;      // x_w = w x [64 tokens][64 p]
+constexpr int oEd = oXW + R64;      // a DX dt
 constexpr int oYH = oEd + R64;      // e dy head [64 i][64 p]
 constexpr int oYL = oYH + R64;      // e dy residual
 constexpr int oF = oYL + R64;       // floats below
 // float offsets within oF
 constexpr int fCs = 0, fDt = 64, fRow = 192, fColT = 320, fColR = 384, fInter = 448, fV = 576, fMisc = 704;
-constexpr int kFloats = 712;
+constexpr int fEcol = 712;  // exp(cs_g - cs_j) per key j (g: first key of its 16-key group), and a wide-group mask
+constexpr int kFloats = 780;
+// exp(cs_i - cs_j) is factored per 16-key group unless the cumsum spans more than this inside it
+constexpr float kWideSpan = 60.f;
 constexpr int kTP = 65;                     // padded row of the staged T / R tiles
 constexpr int oT = oF + kFloats * 4;        // float T[64][65] = CB a dt DX (masked), for its column sums
 constexpr int oR = oT + 64 * kTP * 4;       // float R[64][65] = CB a DX
@@ -82,7 +85,7 @@ static_assert(kSmem <= 232448, "shared memory");
 // tensor-memory columns (M = 64 accumulators)
 constexpr uint32_t cCB = 0, cDX = 64, cXS = 128, cG8 = 192;  // phase 1
 constexpr uint32_t cXI = 0, cBI = 192;                       // phase 2
-constexpr uint32_t cBS = 0, cG7 = 128, cG9 = 256;            // phase 3
+constexpr uint32_t cG7 = 128, cG9 = 256;                     // phase 3
 constexpr uint32_t cS = 384;                                 // state gradient, persistent
 constexpr uint32_t kCols = 512;
 
@@ -141,6 +144,8 @@ __global__ void __launch_bounds__(NT, 1)
   float* s_inter = F + fInter;  // [2][64]
   float* s_V = F + fV;          // [2][64]
   float* s_misc = F + fMisc;
+  float* s_ecol = F + fEcol;
+  uint32_t* s_wide = reinterpret_cast<uint32_t*>(F + fEcol + 64);
   uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + oBar);
   uint64_t* bar_mma = bar_full + 1;
   uint32_t* s_taddr = reinterpret_cast<uint32_t*>(bar_full + 2);
@@ -172,7 +177,8 @@ __global__ void __launch_bounds__(NT, 1)
   const uint64_t nC = tc::smem_desc_sw128(sbase + oC, R64, 1024);
   const uint64_t nSH = tc::smem_desc_sw128(sbase + oSH, R64, 1024), nSL = tc::smem_desc_sw128(sbase + oSL, R64, 1024);
   const uint64_t nDH = tc::smem_desc_sw128(sbase + oDH, R64, 1024);
-  const uint64_t nMq = tc::smem_desc_sw128(sbase + oMq, R64, 1024), nE = tc::smem_desc_sw128(sbase + oE, R64, 1024);
+  const uint64_t nMq = tc::smem_desc_sw128(sbase + oMq, R64, 1024), nEd = tc::smem_desc_sw128(sbase + oEd, R64, 1024);
+  const uint64_t kXW = tc::smem_desc_sw128(sbase + oXW, 16, 1024);
   const uint64_t nYH = tc::smem_desc_sw128(sbase + oYH, R64, 1024), nYL = tc::smem_desc_sw128(sbase + oYL, R64, 1024);
   auto kst = [](int s) { return static_cast<uint64_t>(((s >> 2) * R64 + (s & 3) * 32) >> 4); };  // K-major step
   auto nst = [](int s) { return static_cast<uint64_t>((s * 2048) >> 4); };                        // MN-major step
@@ -262,6 +268,14 @@ __global__ void __launch_bounds__(NT, 1)
       a1 += __shfl_sync(0xffffffffu, a0, 31);
       s_cs[lane] = a0;
       s_cs[32 + lane] = a1;
+      // key factors per 16-key group: lanes 0-15 / 16-31 hold groups 0 / 1 (a0) and 2 / 3 (a1)
+      const float g0 = __shfl_sync(0xffffffffu, a0, lane & ~15), e0 = __shfl_sync(0xffffffffu, a0, lane | 15);
+      const float g1 = __shfl_sync(0xffffffffu, a1, lane & ~15), e1 = __shfl_sync(0xffffffffu, a1, lane | 15);
+      const bool w0 = fabsf(g0 - e0) > kWideSpan, w1 = fabsf(g1 - e1) > kWideSpan;
+      s_ecol[lane] = w0 ? 0.f : __expf(g0 - a0);
+      s_ecol[32 + lane] = w1 ? 0.f : __expf(g1 - a1);
+      const uint32_t b0 = __ballot_sync(0xffffffffu, w0), b1 = __ballot_sync(0xffffffffu, w1);
+      if (lane == 0) *s_wide = (b0 & 1u) | (((b0 >> 16) & 1u) << 1) | ((b1 & 1u) << 2) | (((b1 >> 16) & 1u) << 3);
     }
     if (tid < 4) s_misc[tid] = 0.f;
     {
@@ -307,6 +321,12 @@ __global__ void __launch_bounds__(NT, 1)
       for (int k = 0; k < 16; ++k) split_bf16(e * v[k], hi[k], lo[k]);
       st_sw16(smem + oYH, i, p0, hi);
       st_sw16(smem + oYL, i, p0, lo);
+      // x_w = dt exp(cs_end - cs) x (the state part of dB, folded into its operand)
+      const float wi = dtv[i] * __expf(s_cs[Q - 1] - s_cs[i]);
+      ld_sw16(smem + oX, i, p0, v);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] *= wi;
+      st_sw16(smem + oXW, i, p0, v);
     }
     if (warp == 0 && c > 0) fetch_dt(c - 1);
     fence_proxy_async_smem();
@@ -337,6 +357,7 @@ __global__ void __launch_bounds__(NT, 1)
     {
       const int i = row;
       const float ci = s_cs[i];
+      const uint32_t wide = *s_wide;
       // (a) masked products -> Mq, E, Ed tiles; row / column sums of T and R
       float rsum = 0.f;
 #pragma unroll 1
@@ -346,12 +367,14 @@ __global__ void __launch_bounds__(NT, 1)
         tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cCB + j0), cb);
         tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cDX + j0), dxm);
         tc::tmem_wait_ld();
+        const bool wg = (wide >> (j0 >> 4)) & 1u;  // warp-uniform
+        const float rf = __expf(ci - s_cs[j0]);       // row factor of the group
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const int j = j0 + k;
           mq[k] = ev[k] = ed[k] = tv[k] = rv[k] = 0.f;
           if (act && j <= i) {
-            const float a = __expf(ci - s_cs[j]);
+            const float a = wg ? __expf(ci - s_cs[j]) : rf * s_ecol[j];
             const float dtj = dtv[j];
             mq[k] = cb[k] * a * dtj;
             ev[k] = a * dxm[k];
@@ -363,7 +386,6 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (act) {
           st_sw16(smem + oMq, i, j0, mq);
-          st_sw16(smem + oE, i, j0, ev);
           st_sw16(smem + oEd, i, j0, ed);
           // staged for the column sums (summed by other threads during phase 2)
           float* tr = reinterpret_cast<float*>(smem + oT) + i * kTP + j0;
@@ -428,8 +450,11 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t idMM64 = tc::idesc_bf16(64, 64, true, true), idMM128 = tc::idesc_bf16(64, 128, true, true);
 #pragma unroll
       for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cXI, nMq + nst(s), nDY + nst(s), idMM64, s > 0);  // Mq^T dy
+      const uint32_t idKM128 = tc::idesc_bf16(64, 128, false, true);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cBI, nE + nst(s), nC + nst(s), idMM128, s > 0);   // E^T C
+      for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cBI, nEd + nst(s), nC + nst(s), idMM128, s > 0);  // Ed^T C
+#pragma unroll
+      for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cBI, kXW + kst(s), nDH + nst(s), idKM128, true);  // x_w dS
       tc::mma_commit(bar_mma);
     }
     if (tid >= 64 && tid < 192) {  // column sums of T and R while the MMAs run
@@ -467,7 +492,7 @@ __global__ void __launch_bounds__(NT, 1)
           *reinterpret_cast<uint4*>(dxrow + p0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
-      // dB += dt E^T C
+      // dB (both parts, summed over the group's heads by the atomics)
       float* dbrow = p.dB + ((static_cast<size_t>(b) * p.L + t0 + j) * p.G + grp) * N;
 #pragma unroll 1
       for (int g = 0; g < 4; ++g) {
@@ -478,8 +503,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (act && j < nq)
 #pragma unroll
           for (int k = 0; k < 16; k += 4)
-            atomicAdd(reinterpret_cast<float4*>(dbrow + n0 + k),
-                      make_float4(dtj * v[k], dtj * v[k + 1], dtj * v[k + 2], dtj * v[k + 3]));
+            atomicAdd(reinterpret_cast<float4*>(dbrow + n0 + k), make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]));
       }
     }
     tc::fence_before_sync();
@@ -489,8 +513,6 @@ __global__ void __launch_bounds__(NT, 1)
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t idKM128 = tc::idesc_bf16(64, 128, false, true), idMM128 = tc::idesc_bf16(64, 128, true, true);
-#pragma unroll
-      for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cBS, kX + kst(s), nDH + nst(s), idKM128, s > 0);   // x dS
 #pragma unroll
       for (int s = 0; s < 4; ++s) tc::mma_bf16(tb + cG7, kEd + kst(s), nB + nst(s), idKM128, s > 0);   // Ed B
 #pragma unroll
@@ -503,27 +525,21 @@ __global__ void __launch_bounds__(NT, 1)
     // x, dy, B, C and Sin have no reader left: the next chunk's tiles load under the epilogue
     if (tid == 0 && c > 0) issue_loads(c - 1);
     {
-      const int r = row;  // token (dB, dC) or headdim row (dS)
-      const float wj = dtv[r] * __expf(cs_end - s_cs[r]);
-      float* dbrow = p.dB + ((static_cast<size_t>(b) * p.L + t0 + r) * p.G + grp) * N;
+      const int r = row;  // token (dC) or headdim row (dS)
       float* dcrow = p.dC + ((static_cast<size_t>(b) * p.L + t0 + r) * p.G + grp) * N;
       const float dec = __expf(cs_end);
 #pragma unroll 1
       for (int g = 0; g < 4; ++g) {
         const int n0 = 64 * hw + 16 * g;
-        float bs[16], c7[16], g9[16], sv[16];
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cBS + n0), bs);
+        float c7[16], g9[16], sv[16];
         tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cG7 + n0), c7);
         tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cG9 + n0), g9);
         tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cS + n0), sv);
         tc::tmem_wait_ld();
         if (act && r < nq) {
 #pragma unroll
-          for (int k = 0; k < 16; k += 4) {
-            atomicAdd(reinterpret_cast<float4*>(dbrow + n0 + k),
-                      make_float4(wj * bs[k], wj * bs[k + 1], wj * bs[k + 2], wj * bs[k + 3]));
+          for (int k = 0; k < 16; k += 4)
             atomicAdd(reinterpret_cast<float4*>(dcrow + n0 + k), make_float4(c7[k], c7[k + 1], c7[k + 2], c7[k + 3]));
-          }
         }
 #pragma unroll
         for (int k = 0; k < 16; ++k) sv[k] = fmaf(dec, sv[k], g9[k]);

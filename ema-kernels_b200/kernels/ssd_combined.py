@@ -91,16 +91,24 @@ def ssd_chunk_scan_fwd(x, dt, A, B, C, D=None, initial_states=None, return_final
     return y, cst, fin
 
 
-def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=None, need_d_initial=False):
+def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=None, need_d_initial=False,
+                       dx_out=None):
     """Backward.  Returns (dx, ddt, dA, dB, dC, dD or None, d_initial_states or None);
-    dB / dC are fp32 (batch, seqlen, ngroups, dstate), summed over each group's heads."""
+    dB / dC are fp32 (batch, seqlen, ngroups, dstate), summed over each group's heads.
+    ``dx_out``: a (batch, seqlen, nheads, headdim) bf16 buffer to write dx into
+    (headdim stride 1, other strides even); the tensor-core kernel needs them to
+    be multiples of 8 and 16-byte alignment, else the mma.sync kernel runs."""
     b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk = _prep(x, dt, A, B, C, D)
     dev = x.device
     assert dy.shape == x.shape
     dyk = dy.to(torch.bfloat16)
     dyk = dyk if (dyk.stride(-1) == 1 and dyk.data_ptr() % 16 == 0
                   and all(s % 8 == 0 for s in dyk.stride()[:3])) else dyk.contiguous()
-    dx = torch.empty(b_, L, H, P, dtype=x.dtype, device=dev)
+    if dx_out is not None:
+        assert dx_out.shape == x.shape and dx_out.dtype == x.dtype and dx_out.stride(-1) == 1, "dx_out"
+        dx = dx_out
+    else:
+        dx = torch.empty(b_, L, H, P, dtype=x.dtype, device=dev)
     ddt = torch.empty(b_, L, H, dtype=torch.float32, device=dev)
     dA = torch.empty(H, dtype=torch.float32, device=dev)
     dB = torch.empty(b_, L, G, N, dtype=torch.float32, device=dev)

@@ -95,11 +95,11 @@ def test_mamba_call_form_autograd():
 
 
 def test_ssd_forward_steep_decay_matches_oracle():
-    """Large dt * A (cumsum spans over 60 within 16 tokens): the tcgen05 forward's
+    """Large dt * A (cumsum spans over 60 within 16 tokens): the tcgen05 kernels'
     per-element decay path for such key groups, next to the factored one."""
     from kernels.ssd_combined import ssd_chunk_scan_fwd
     B, L, H, P, N, G = 1, 192, 2, 64, 128, 1
-    x, dt, A, Bm, Cm, D, _ = so.make_ssd_inputs(B, L, H, P, N, ngroups=G, seed=5, dt_range=(0.05, 2.0))
+    x, dt, A, Bm, Cm, D, dy = so.make_ssd_inputs(B, L, H, P, N, ngroups=G, seed=5, dt_range=(0.05, 2.0))
     dt[:, :96] *= 0.05  # the first key groups stay narrow
     bf = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
     tx, tB, tC = bf(x), bf(Bm), bf(Cm)
@@ -112,3 +112,39 @@ def test_ssd_forward_steep_decay_matches_oracle():
     assert_lowp_close(fin, r["final_state"], "final_state")
     ref_states = np.concatenate([np.zeros((B, 1, H, P, N)), r["states"][:, 63::64][:, :cst.shape[1] - 1]], axis=1)
     assert_lowp_close(cst, ref_states, "chunk_states")
+    # and the backward's per-element decay path for the same steep key groups
+    from kernels.ssd_combined import ssd_chunk_scan_bwd
+    tdy = bf(dy)
+    dx, ddt, dA, dB, dC, dD, _ = ssd_chunk_scan_bwd(tx.to(DEV), torch.from_numpy(dt).to(DEV),
+                                                    torch.from_numpy(A).to(DEV), tB.to(DEV), tC.to(DEV), cst,
+                                                    tdy.to(DEV), torch.from_numpy(D).to(DEV))
+    torch.cuda.synchronize()
+    assert _device_status_clear() == 0
+    g = so.ssd_bwd(_f64(tx), dt.astype(np.float64), A.astype(np.float64), _f64(tB), _f64(tC), _f64(tdy),
+                   D=D.astype(np.float64))
+    for name, k in (("dx", dx), ("ddt", ddt), ("dB", dB), ("dC", dC)):
+        assert_lowp_close(k, g[name], name)
+
+
+def test_ssd_backward_mma_sync_kernel_on_strided_dx():
+    """A dx buffer whose strides the tensor-core backward cannot store into (not
+    multiples of 8 elements) runs the mma.sync backward; both kernels match the
+    oracle on the same inputs."""
+    from kernels.ssd_combined import ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
+    B, L, H, P, N, G = 1, 160, 2, 64, 128, 1
+    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=21)
+    x, dt, A, Bm, Cm, D, dy = (t.to(DEV) for t in (tx, tdt, tA, tB, tC, tD, tdy))
+    y, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+    pad = torch.zeros(B, L, H, P + 2, dtype=torch.bfloat16, device=DEV)  # head stride 66
+    dx_view = pad[..., :P]
+    outs_old = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D, dx_out=dx_view)
+    outs_new = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
+    torch.cuda.synchronize()
+    assert _device_status_clear() == 0
+    args = (_f64(tx), tdt.double().numpy(), tA.double().numpy(), _f64(tB), _f64(tC))
+    g = so.ssd_bwd(*args, _f64(tdy), D=tD.double().numpy())
+    for outs in (outs_old, outs_new):
+        dx, ddt, dA, dB, dC, dD, _ = outs
+        for name, k in (("dx", dx), ("ddt", ddt), ("dB", dB), ("dC", dC)):
+            assert_lowp_close(k, g[name], name)
+    assert float(pad[..., P:].abs().max()) == 0.0  # nothing written outside the view
