@@ -206,6 +206,34 @@ __global__ void __launch_bounds__(NT, 1)
       else *dst = 0.f;
     }
   };
+  // Chunk c's saved state: fp32 (landed by TMA) -> bf16 head and residual
+  // tiles, and <dS, Sin> (dS from its bf16 head + residual tiles) into
+  // s_misc[c & 1].  Run by the 128 threads t0 .. t0 + 127, which first observe
+  // the chunk's TMA completion.
+  auto stage_state = [&](int c, int t) {
+    if (!mbar_wait_bounded(bar_full, (p.nc - 1 - c) & 1, status)) *s_fail = 1u;
+    const int pr = t >> 1, n0 = (t & 1) * 64;
+    float part = 0.f;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+      const int n = n0 + 16 * g;
+      float v[16], hi[16], lo[16], dh[16], dl[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = *sf_at(smem + oSF, pr, n + k);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) split_bf16(v[k], hi[k], lo[k]);
+      st_sw16(smem + oSH + (n >> 6) * R64, pr, n & 63, hi);
+      st_sw16(smem + oSL + (n >> 6) * R64, pr, n & 63, lo);
+      ld_sw16(smem + oDH + (n >> 6) * R64, pr, n & 63, dh);
+      ld_sw16(smem + oDL + (n >> 6) * R64, pr, n & 63, dl);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) part = fmaf(dh[k] + dl[k], v[k], part);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((t & 31) == 0) atomicAdd(&s_misc[c & 1], part);
+    fence_proxy_async_smem();  // the bf16 state tiles, for the chunk's MMAs
+  };
   auto wait_mma = [&]() {
     if (!mbar_wait_bounded(bar_mma, mma_phase & 1u, status)) *s_fail = 1u;
     ++mma_phase;
@@ -241,8 +269,10 @@ __global__ void __launch_bounds__(NT, 1)
     issue_loads(p.nc - 1);
   }
   if (warp == 0) fetch_dt(p.nc - 1);
+  if (tid < 4) s_misc[tid] = 0.f;
   tc::fence_before_sync();
   __syncthreads();
+  if (tid >= 128) stage_state(p.nc - 1, tid - 128);
 
   float dA_acc = 0.f, dD_acc = 0.f;
   const uint32_t id64 = tc::idesc_bf16(64, 64, false, false);
@@ -277,40 +307,8 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t b0 = __ballot_sync(0xffffffffu, w0), b1 = __ballot_sync(0xffffffffu, w1);
       if (lane == 0) *s_wide = (b0 & 1u) | (((b0 >> 16) & 1u) << 1) | ((b1 & 1u) << 2) | (((b1 >> 16) & 1u) << 3);
     }
-    if (tid < 4) s_misc[tid] = 0.f;
-    {
-      // Sin (fp32, staged by TMA) -> bf16 head and residual, [p][n] MN-major
-      const int pr = tid >> 2, n0 = (tid & 3) * 32;
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        float v[16], hi[16], lo[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = *sf_at(smem + oSF, pr, n0 + 16 * g + k);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) split_bf16(v[k], hi[k], lo[k]);
-        const int n = n0 + 16 * g;
-        st_sw16(smem + oSH + (n >> 6) * R64, pr, n & 63, hi);
-        st_sw16(smem + oSL + (n >> 6) * R64, pr, n & 63, lo);
-      }
-    }
-    {
-      // sum dS . Sin over this thread's row and columns (the chunk-end decay term)
-      float part = 0.f;
-#pragma unroll 1
-      for (int g = 0; g < 4; ++g) {
-        const int n0 = 64 * hw + 16 * g;
-        float v[16];
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cS + n0), v);
-        tc::tmem_wait_ld();
-        if (act)
-#pragma unroll
-          for (int k = 0; k < 16; ++k) part = fmaf(v[k], *sf_at(smem + oSF, row, n0 + k), part);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      __syncthreads();  // misc zeroed, cumsum written
-      if (lane == 0) atomicAdd(&s_misc[0], part);
-    }
+    if (tid == 0) s_misc[(c + 1) & 1] = 0.f;  // the slot the previous chunk consumed: the next chunk's sum
+    __syncthreads();  // the cumsum and this chunk's state tiles are written
     {
       // e_i dy_i -> bf16 head and residual, [i][p]
       const int i = tid >> 2, p0 = (tid & 3) * 16;
@@ -578,7 +576,7 @@ __global__ void __launch_bounds__(NT, 1)
       float usum = dtk[0] * (s_V[lane] + s_V[64 + lane]) + dtk[1] * (s_V[32 + lane] + s_V[96 + lane]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) usum += __shfl_xor_sync(0xffffffffu, usum, o);
-      if (lane == 31) dcs[1] += usum + __expf(cs_end) * s_misc[0];
+      if (lane == 31) dcs[1] += usum + __expf(cs_end) * s_misc[c & 1];
       float r1 = dcs[1], r0 = dcs[0];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -600,6 +598,8 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) da += __shfl_xor_sync(0xffffffffu, da, o);
       dA_acc += da;
+    } else if (warp >= 4 && c > 0) {
+      stage_state(c - 1, tid - 128);  // the next chunk's state tiles, off its critical path
     }
     __syncthreads();  // the per-token sums are read; the next chunk rewrites them
     if (*s_fail) break;
