@@ -287,7 +287,7 @@ def run_ssd(args, rank, world, local_rank):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "Mamba-2 SSD fwd+bwd (config 3)", **c,
                        "kernels": "forward: tcgen05/TMEM, 128-token chunks, 2 heads per CTA; "
-                                  "backward: mma.sync, 64-token chunks",
+                                  "backward: tcgen05/TMEM, 64-token chunks, 1 head per CTA",
                        "l2": "step inputs 1.4 GB > 126 MB L2, no flush", "timing": "one CUDA graph per step"},
             "roofline": {"bound": "ridge", "hbm": {"achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
                          "tensor": {"achieved": tfl, "peak": tflops_peak, "unit": "TFLOP/s",
