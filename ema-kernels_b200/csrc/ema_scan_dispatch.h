@@ -42,6 +42,15 @@ int bwd_dispatch_f32(const BwdLaunch& l);
 int bwd_dispatch_bf16(const BwdLaunch& l);
 int bwd_dispatch_f16(const BwdLaunch& l);
 
+// Tensor-core backward (ema_bwd_tc.cu): bf16, headdim 64, 128-token chunks,
+// dx requested.  Returns 1 when the case is not covered (run the CUDA-core
+// kernel instead), 0 when launched, -3 when a tensor map could not be
+// encoded (message set), otherwise a cudaError_t.
+int bwd_tc_launch(const BwdLaunch& l, int dtype, const void* x, const int64_t xs[3], const void* dy,
+                  const int64_t dys[3], void* dx, const int64_t dxs[3]);
+// Whether the tensor-core kernels are used where they apply (default on).
+bool tensor_core_path_enabled();
+
 constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
 
 // Set the dynamic shared-memory opt-in of `fn` once per device.

@@ -39,6 +39,23 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// The driver's tensor-map encoder needs a current context on the calling
+// thread.  A thread that has made no runtime call that binds one (an autograd
+// worker whose first CUDA work is this launch, for instance) has none, and
+// the encoder then fails with CUDA_ERROR_INVALID_CONTEXT: bind the current
+// device's primary context first (once per thread and device).
+int bind_thread_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (bound == dev) return EMA_OK;
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+  bound = dev;
+  return EMA_OK;
+}
+
 int elem_size(int dtype) { return dtype == EMA_DTYPE_F32 ? 4 : 2; }
 
 CUtensorMapDataType map_dtype(int dtype) {
@@ -77,6 +94,7 @@ int make_tile_map(CUtensorMap* m, const void* ptr, int dtype, int64_t B, int64_t
                   "%s: stride %d (%lld elements) must be positive and a multiple of 16 bytes", name, i,
                   static_cast<long long>(st[i]));
   }
+  if (int r = bind_thread_context()) return r;
   auto enc = encode_fn();
   if (!enc) return fail(EMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(P), static_cast<cuuint64_t>(H),
@@ -179,8 +197,16 @@ int map_dispatch_result(int r, const char* what) {
 
 void set_last_error(const char* msg) { g_last_error = msg; }
 
+namespace {
+// off by default: the tensor-core backward is exact to tolerance but not yet
+// faster than the CUDA-core kernel on the benchmark shape
+std::atomic<int> g_tensor_core_path{0};
+}
+bool tensor_core_path_enabled() { return g_tensor_core_path.load(std::memory_order_relaxed) != 0; }
+
 int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const uint64_t* dims,
                const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  if (int r = bind_thread_context()) return r;
   auto enc = encode_fn();
   if (!enc) return fail(EMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return fail(EMA_ERR_INVALID_ARGUMENT, "TMA base not 16-byte aligned");
@@ -392,6 +418,12 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
+  if (tensor_core_path_enabled()) {
+    r = bwd_tc_launch(l, a->dtype, a->x, a->x_stride, a->dout, a->dout_stride, a->dx, a->dx_stride);
+    if (r == 0) return EMA_OK;
+    if (r == -3) return EMA_ERR_CUDA;
+    if (r != 1) return map_dispatch_result(r, "ema_bwd (tensor cores)");
+  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = bwd_dispatch_f16(l); break;
@@ -447,6 +479,11 @@ int ema_workspace_clear_status(void* workspace, void* stream) {
   cudaError_t e = cudaMemsetAsync(word, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "status clear failed: %s", cudaGetErrorString(e));
   return EMA_OK;
+}
+
+int ema_set_tensor_core_path(int32_t enable) {
+  const int prev = g_tensor_core_path.exchange(enable ? 1 : 0);
+  return prev;
 }
 
 const char* ema_last_error(void) { return g_last_error.c_str(); }

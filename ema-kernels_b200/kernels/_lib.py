@@ -113,6 +113,8 @@ lib.ema_workspace_status.restype = ctypes.c_int
 lib.ema_workspace_status.argtypes = [_ptr, ctypes.POINTER(ctypes.c_uint32), _ptr]
 lib.ema_workspace_clear_status.restype = ctypes.c_int
 lib.ema_workspace_clear_status.argtypes = [_ptr, _ptr]
+lib.ema_set_tensor_core_path.restype = ctypes.c_int
+lib.ema_set_tensor_core_path.argtypes = [ctypes.c_int32]
 lib.ssd_internal_chunks.restype = _i64
 lib.ssd_internal_chunks.argtypes = [_i64]
 lib.ssd_fwd_launch.restype = ctypes.c_int

@@ -174,6 +174,14 @@ EMA_API int ema_fwd_launch_noalloc(const EmaFwdArgs* args, void* stream);
 EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);
 /* Clears the workspace status word (asynchronously on `stream`). */
 EMA_API int ema_workspace_clear_status(void* workspace, void* stream);
+/* Selects whether the launchers use their tensor-core (tcgen05) kernels where
+ * one applies (today: the backward for bf16, headdim 64, chunk_size 128, dx
+ * requested) or always the CUDA-core kernels; process-wide, default 0 (the
+ * CUDA-core kernels).  Returns the previous setting.  No counterpart in the
+ * reference: the two kernels agree within the bf16 tolerance, and this switch
+ * lets a caller pick one.
+ */
+EMA_API int ema_set_tensor_core_path(int32_t enable);
 /* Human-readable detail of the last error returned on the calling thread. */
 EMA_API const char* ema_last_error(void);
 /* Library version string. */
