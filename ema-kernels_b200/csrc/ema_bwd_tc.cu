@@ -36,18 +36,18 @@
 // more than kWideSpan.
 //
 // Warp roles (one CTA per SM; tiles flow builder -> MMA -> epilogue):
-//   warps 0-3  builders: the tile's cumsum and key factors, then L (the 8-key
-//              chunks of rows i and 128 - i split over a pair of threads, so
-//              every thread has about the same share of the triangle) and X
-//              (thread i: row i).  L_hi of tile k+1 is written once the
-//              MMAs of tile k that read L_hi are done, L_lo and X once all of
-//              them are;
-//   warps 4-7  epilogue: thread i reads lane i of the accumulators and writes
+//   warps 0-7  builders: the tile's cumsum and key factors (warps 0-3, one
+//              token per thread), then L (the 8-key chunks of rows i and
+//              128 - i split over a quad of threads, so every thread has about
+//              the same share of the triangle) and X (a thread pair per row).
+//              L_hi of tile k+1 is written once the MMAs of tile k that read
+//              L_hi are done, L_lo and X once all of them are;
+//   warps 8-11 epilogue: thread i reads lane i of the accumulators and writes
 //              dx (into a staging tile, then one TMA store), dl / ddt,
 //              the dA partials and the tile's look-back records;
-//   warp 8     producer (TMA ring, as the CUDA-core kernel);
-//   warp 9     look-back warp (the gradient arriving at each tile's end);
-//   warp 10    MMA issue: two commits per tile (the L_hi products, then the
+//   warp 12    producer (TMA ring, as the CUDA-core kernel);
+//   warp 13    look-back warp (the gradient arriving at each tile's end);
+//   warp 14    MMA issue: two commits per tile (the L_hi products, then the
 //              L_lo ones) into one of two tensor-memory accumulator sets.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -64,10 +64,10 @@ using bf16 = __nv_bfloat16;
 
 constexpr int Q = 128;             // tokens per tile
 constexpr int BP = 64;             // channels per tile (headdim)
-constexpr int NBT = 128;           // builder threads (warps 0-3)
-constexpr int NET = 128;           // epilogue threads (warps 4-7): thread i owns token i
-constexpr int kProdWarp = 8, kLbWarp = 9, kMmaWarp = 10;
-constexpr int NT = 352;
+constexpr int NBT = 256;           // builder threads (warps 0-7)
+constexpr int NET = 128;           // epilogue threads (warps 8-11): thread i owns token i
+constexpr int kProdWarp = 12, kLbWarp = 13, kMmaWarp = 14;
+constexpr int NT = 480;
 constexpr int S = 3;               // ring stages
 constexpr int kTile = Q * BP * 2;  // one 128-row x 128-byte swizzled bf16 tile
 constexpr float kWideSpan = 60.f;
@@ -332,8 +332,9 @@ __global__ void __launch_bounds__(NT, 1)
     return;
   }
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ------------------------------ builders ------------------------------
+    const bool tok = tid < Q;  // warps 0-3 own one token each for the cumsum
     const int i = tid;
     for (int k = 0;; ++k) {
       const int s = k % S, kb = k & 1;
@@ -348,111 +349,117 @@ __global__ void __launch_bounds__(NT, 1)
       if (k >= 2 && !group_wait(&tmem_empty[kb], ((k - 2) >> 1) & 1, status, warp == 0, kBarBuild, NBT, s_fail_b))
         break;
 
-      // ---- per-token decay, weight and within-tile cumsum --------------------
-      float w, cs;
+      // ---- per-token decay, weight and within-tile cumsum (warps 0-3) ----------
+      float* csb = s_cs2 + kb * Q;
+      float w = 0.f, cs = 0.f;
       if (MODE == kBwdDt) {
-        const float Ah = *reinterpret_cast<const float*>(st + oSA);
-        const float d = valid ? raw[i] : 0.f;
-        w = d;
-        float v = d * Ah;
+        float d = 0.f, v = 0.f;
+        if (tok) {
+          const float Ah = *reinterpret_cast<const float*>(st + oSA);
+          d = valid ? raw[i] : 0.f;
+          v = d * Ah;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float nv = __shfl_up_sync(FULL, v, o);
-          if (lane >= o) v += nv;
+          for (int o = 1; o < 32; o <<= 1) {
+            const float nv = __shfl_up_sync(FULL, v, o);
+            if (lane >= o) v += nv;
+          }
+          if (lane == 31) s_wsum[warp] = v;
         }
-        if (lane == 31) s_wsum[warp] = v;
         named_sync(kBarBuild, NBT);
         float pre = 0.f;
 #pragma unroll
         for (int ww = 0; ww < 3; ++ww)
           if (ww < warp) pre += s_wsum[ww];
+        w = d;
         cs = v + pre;
-      } else {
+      } else if (tok) {
         w = valid ? 1.f : 0.f;
         cs = raw[valid ? i : n - 1] * kLn2;
       }
-      const float cref = __shfl_sync(FULL, cs, lane & ~15);
-      float span = fabsf(cref - cs);
+      if (tok) {
+        const float cref = __shfl_sync(FULL, cs, lane & ~15);
+        float span = fabsf(cref - cs);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) span = fmaxf(span, __shfl_xor_sync(FULL, span, o));
-      const bool wide = span > kWideSpan;
-      float* csb = s_cs2 + kb * Q;
-      csb[i] = cs;
-      s_w2[kb * Q + i] = w;
-      s_v[i] = wide ? 0.f : __expf(cref - cs);
-      if ((lane & 15) == 0) s_ref[i >> 4] = cref;
-      const uint32_t wb = __ballot_sync(FULL, wide);
-      if (lane == 0) s_wide[warp] = ((wb & 1u) | ((wb >> 15) & 2u)) << (2 * warp);
+        for (int o = 8; o > 0; o >>= 1) span = fmaxf(span, __shfl_xor_sync(FULL, span, o));
+        const bool wide = span > kWideSpan;
+        csb[i] = cs;
+        s_w2[kb * Q + i] = w;
+        s_v[i] = wide ? 0.f : __expf(cref - cs);
+        if ((lane & 15) == 0) s_ref[i >> 4] = cref;
+        const uint32_t wb = __ballot_sync(FULL, wide);
+        if (lane == 0) s_wide[warp] = ((wb & 1u) | ((wb >> 15) & 2u)) << (2 * warp);
+      }
       named_sync(kBarBuild, NBT);
       const uint32_t wmask = s_wide[0] | s_wide[1] | s_wide[2] | s_wide[3];
 
       // ---- L: hi once tile k-1's L_hi products are done, lo once all are ---------
       if (k >= 1 && !group_wait(mma_a, (k - 1) & 1, status, warp == 0, kBarBuild, NBT, s_fail_b)) break;
-      // thread pair pr builds rows pr + 1 and 127 - pr (row 64 alone for the
-      // last pair): about 17.5 chunks per pair, interleaved over its two
-      // threads.  Rolled loops (each body is reused), lo recomputed in a second
-      // pass once tile k-1's L_lo products are done.
-      const int pr = tid >> 1, hf = tid & 1;
+      // a quad of threads builds rows pr + 1 and 127 - pr (row 64 alone for the
+      // last quad): about 17.5 chunks per quad, interleaved over its threads
+      // (at most five each); lo stays in registers until it may be written
+      const int pr = tid >> 2, sub = tid & 3;
       const int ra = pr + 1, rb = 127 - pr;
       const int na = ((ra - 1) >> 3) + 1;
       const int nab = na + ((pr == Q / 2 - 1) ? 0 : ((rb - 1) >> 3) + 1);
       const float csa = csb[ra], csr = csb[rb];
-      auto chunk = [&](int idx, uint32_t& off, uint4& hi, uint4& lo) {
-        const bool ina = idx < na;
-        const int ri = ina ? ra : rb;
-        const int cc = ina ? idx : idx - na;
-        const float ci = ina ? csa : csr;
-        const int j0 = 8 * cc, g = cc >> 1;
-        float v8[8];
-        if (!((wmask >> g) & 1u)) {
-          const float uu = __expf(ci - s_ref[g]);
-          const float4 a = *reinterpret_cast<const float4*>(s_v + j0);
-          const float4 bq = *reinterpret_cast<const float4*>(s_v + j0 + 4);
-          v8[0] = uu * a.x; v8[1] = uu * a.y; v8[2] = uu * a.z; v8[3] = uu * a.w;
-          v8[4] = uu * bq.x; v8[5] = uu * bq.y; v8[6] = uu * bq.z; v8[7] = uu * bq.w;
-        } else {
+      uint4 lo[5];
+      uint32_t offs[5];
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) v8[kk] = __expf(ci - csb[j0 + kk]);
+      for (int q = 0; q < 5; ++q) {
+        const int idx = sub + 4 * q;
+        offs[q] = 0u;
+        lo[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (idx < nab) {
+          const bool ina = idx < na;
+          const int ri = ina ? ra : rb;
+          const int cc = ina ? idx : idx - na;
+          const float ci = ina ? csa : csr;
+          const int j0 = 8 * cc, g = cc >> 1;
+          float v8[8];
+          if (!((wmask >> g) & 1u)) {
+            const float uu = __expf(ci - s_ref[g]);
+            const float4 a = *reinterpret_cast<const float4*>(s_v + j0);
+            const float4 bq = *reinterpret_cast<const float4*>(s_v + j0 + 4);
+            v8[0] = uu * a.x; v8[1] = uu * a.y; v8[2] = uu * a.z; v8[3] = uu * a.w;
+            v8[4] = uu * bq.x; v8[5] = uu * bq.y; v8[6] = uu * bq.z; v8[7] = uu * bq.w;
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) v8[kk] = __expf(ci - csb[j0 + kk]);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            if (j0 + kk >= ri) v8[kk] = 0.f;
+          uint4 hi;
+          split8(v8, hi, lo[q]);
+          offs[q] = (j0 >> 6) * kTile + chunk_off(ri, (j0 & 63) >> 3);
+          *reinterpret_cast<uint4*>(smem + oLh + offs[q]) = hi;
         }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          if (j0 + kk >= ri) v8[kk] = 0.f;
-        split8(v8, hi, lo);
-        off = (j0 >> 6) * kTile + chunk_off(ri, (j0 & 63) >> 3);
-      };
-#pragma unroll 1
-      for (int idx = hf; idx < nab; idx += 2) {
-        uint32_t off;
-        uint4 hi, lo;
-        chunk(idx, off, hi, lo);
-        *reinterpret_cast<uint4*>(smem + oLh + off) = hi;
       }
       if (k >= 1 && !group_wait(&mma_b[kb ^ 1], ((k - 1) >> 1) & 1, status, warp == 0, kBarBuild, NBT, s_fail_b))
         break;
-#pragma unroll 1
-      for (int idx = hf; idx < nab; idx += 2) {
-        uint32_t off;
-        uint4 hi, lo;
-        chunk(idx, off, hi, lo);
-        *reinterpret_cast<uint4*>(smem + oLl + off) = lo;
-      }
+#pragma unroll
+      for (int q = 0; q < 5; ++q)
+        if (sub + 4 * q < nab) *reinterpret_cast<uint4*>(smem + oLl + offs[q]) = lo[q];
       // ---- X = w x, hi and lo (dt form; the reference form's X is x itself) ------
+      // thread pair per token row, four 8-channel chunks each
       if (MODE == kBwdDt) {
-#pragma unroll 2
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint4 a = *reinterpret_cast<const uint4*>(st + oSx + chunk_off(i, cc));
+        const int xr = tid >> 1, c0 = 4 * (tid & 1);
+        const float wx = s_w2[kb * Q + xr];
+#pragma unroll
+        for (int cc = c0; cc < c0 + 4; ++cc) {
+          const uint4 a = *reinterpret_cast<const uint4*>(st + oSx + chunk_off(xr, cc));
           const uint32_t xw[4] = {a.x, a.y, a.z, a.w};
           float v8[8];
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
             const float2 f = cvt_pair<bf16>(xw[m]);
-            v8[2 * m] = w * f.x;
-            v8[2 * m + 1] = w * f.y;
+            v8[2 * m] = wx * f.x;
+            v8[2 * m + 1] = wx * f.y;
           }
           uint4 hi, xlo;
           split8(v8, hi, xlo);
-          *reinterpret_cast<uint4*>(smem + oXh + chunk_off(i, cc)) = hi;
-          *reinterpret_cast<uint4*>(smem + oXl + chunk_off(i, cc)) = xlo;
+          *reinterpret_cast<uint4*>(smem + oXh + chunk_off(xr, cc)) = hi;
+          *reinterpret_cast<uint4*>(smem + oXl + chunk_off(xr, cc)) = xlo;
         }
       }
       fence_proxy_async_smem();
@@ -463,7 +470,7 @@ __global__ void __launch_bounds__(NT, 1)
   } else {
     // ------------------------------ epilogue ------------------------------
     const int et = tid - NBT;  // 0..127: token row of the tile = tensor-memory lane
-    const int ew = warp - 4;
+    const int ew = warp - 8;   // = warp % 4: the lane quarter this warp may read
     const int i = et;
     for (int k = 0;; ++k) {
       const int s = k % S, kb = k & 1;
