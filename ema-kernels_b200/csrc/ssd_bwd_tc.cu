@@ -358,13 +358,19 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t wide = *s_wide;
       // (a) masked products -> Mq, E, Ed tiles; row / column sums of T and R
       float rsum = 0.f;
-#pragma unroll 1
+      float cb2[2][16], dx2[2][16];  // both 16-column groups, loaded before one wait
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cCB + 32 * hw + 16 * g), cb2[g]);
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cDX + 32 * hw + 16 * g), dx2[g]);
+      }
+      tc::tmem_wait_ld();
+#pragma unroll
       for (int g = 0; g < 2; ++g) {
         const int j0 = 32 * hw + 16 * g;
-        float cb[16], dxm[16], mq[16], ev[16], ed[16], tv[16], rv[16];
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cCB + j0), cb);
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cDX + j0), dxm);
-        tc::tmem_wait_ld();
+        const float (&cb)[16] = cb2[g];
+        const float (&dxm)[16] = dx2[g];
+        float mq[16], ev[16], ed[16], tv[16], rv[16];
         const bool wg = (wide >> (j0 >> 4)) & 1u;  // warp-uniform
         const float rf = __expf(ci - s_cs[j0]);       // row factor of the group
 #pragma unroll
@@ -402,11 +408,16 @@ __global__ void __launch_bounds__(NT, 1)
         float ip = 0.f;
         float* dcrow = p.dC + ((static_cast<size_t>(b) * p.L + t0 + i) * p.G + grp) * N;
 #pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
-          const int n0 = 64 * hw + 16 * g;
-          float v[16], cv[16];
-          tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cG8 + n0), v);
+        for (int g2 = 0; g2 < 4; g2 += 2) {
+          float v2[2][16];
+          tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cG8 + 64 * hw + 16 * g2), v2[0]);
+          tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cG8 + 64 * hw + 16 * g2 + 16), v2[1]);
           tc::tmem_wait_ld();
+#pragma unroll
+          for (int gg = 0; gg < 2; ++gg) {
+          const int n0 = 64 * hw + 16 * (g2 + gg);
+          const float (&v)[16] = v2[gg];
+          float cv[16];
           if (act) {
             ld_sw16(smem + oC + (n0 >> 6) * R64, i, n0 & 63, cv);
 #pragma unroll
@@ -417,18 +428,22 @@ __global__ void __launch_bounds__(NT, 1)
                 atomicAdd(reinterpret_cast<float4*>(dcrow + n0 + k),
                           make_float4(e * v[k], e * v[k + 1], e * v[k + 2], e * v[k + 3]));
           }
+          }
         }
         if (act) s_inter[hw * 64 + i] = e * ip;
       }
       // (c) V_j = exp(cs_end - cs_j) x_j . (B_j dS^T)
       {
         float vp = 0.f;
-#pragma unroll 1
+        float vx2[2][16];
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXS + 32 * hw), vx2[0]);
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXS + 32 * hw + 16), vx2[1]);
+        tc::tmem_wait_ld();
+#pragma unroll
         for (int g = 0; g < 2; ++g) {
           const int p0 = 32 * hw + 16 * g;
-          float v[16], xv[16];
-          tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXS + p0), v);
-          tc::tmem_wait_ld();
+          const float (&v)[16] = vx2[g];
+          float xv[16];
           if (act) {
             ld_sw16(smem + oX, i, p0, xv);
 #pragma unroll
@@ -469,13 +484,19 @@ __global__ void __launch_bounds__(NT, 1)
       const float dtj = dtv[j], wj = dtj * __expf(cs_end - s_cs[j]);
       // dx = dXi + w dXs + D dy; dD += dy . x
       bf16* dxrow = p.dx + b * p.sdx_b + static_cast<long long>(t0 + j) * p.sdx_l + h * p.sdx_h;
-#pragma unroll 1
+      float xi2[2][16], xs2[2][16];  // both 16-column groups, loaded before one wait
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXI + 32 * hw + 16 * g), xi2[g]);
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXS + 32 * hw + 16 * g), xs2[g]);
+      }
+      tc::tmem_wait_ld();
+#pragma unroll
       for (int g = 0; g < 2; ++g) {
         const int p0 = 32 * hw + 16 * g;
-        float xi[16], xs[16], dv[16], xv[16];
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXI + p0), xi);
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cXS + p0), xs);
-        tc::tmem_wait_ld();
+        const float (&xi)[16] = xi2[g];
+        const float (&xs)[16] = xs2[g];
+        float dv[16], xv[16];
         if (act && j < nq) {
           ld_sw16(smem + oDY, j, p0, dv);
           ld_sw16(smem + oX, j, p0, xv);
@@ -493,15 +514,18 @@ __global__ void __launch_bounds__(NT, 1)
       // dB (both parts, summed over the group's heads by the atomics)
       float* dbrow = p.dB + ((static_cast<size_t>(b) * p.L + t0 + j) * p.G + grp) * N;
 #pragma unroll 1
-      for (int g = 0; g < 4; ++g) {
-        const int n0 = 64 * hw + 16 * g;
-        float v[16];
-        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cBI + n0), v);
+      for (int g2 = 0; g2 < 4; g2 += 2) {
+        float v2[2][16];
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cBI + 64 * hw + 16 * g2), v2[0]);
+        tc::tmem_ld16(tc::tmem_at(tb, 32 * q, cBI + 64 * hw + 16 * g2 + 16), v2[1]);
         tc::tmem_wait_ld();
         if (act && j < nq)
 #pragma unroll
-          for (int k = 0; k < 16; k += 4)
-            atomicAdd(reinterpret_cast<float4*>(dbrow + n0 + k), make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]));
+          for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+            for (int k = 0; k < 16; k += 4)
+              atomicAdd(reinterpret_cast<float4*>(dbrow + 64 * hw + 16 * (g2 + gg) + k),
+                        make_float4(v2[gg][k], v2[gg][k + 1], v2[gg][k + 2], v2[gg][k + 3]));
       }
     }
     tc::fence_before_sync();
