@@ -11,10 +11,11 @@ third-party and absent here).  Same argument names and layouts:
 
     s_t = exp(dt_t A_h) s_{t-1} + dt_t x_t B_t^T,   y_t = s_t C_t + D_h x_t
 
-``dt_bias`` / ``dt_softplus`` are applied before the scan (dt <- softplus(dt +
-dt_bias)) and differentiated by autograd.  Not supported yet: ``z`` gating,
-``seq_idx`` / ``cu_seqlens`` (packed sequences) and ``dt_limit`` other than the
-default.  headdim must be 64 and dstate 128 (the benchmark shapes).
+``dt_bias`` / ``dt_softplus`` / ``dt_limit`` are applied before the scan
+(dt <- clamp(softplus(dt + dt_bias), *dt_limit)) and ``z`` gating after it
+(out <- y * silu(z), in fp32, stored in y's dtype), all differentiated by
+autograd.  Not supported yet: ``seq_idx`` / ``cu_seqlens`` (packed sequences).
+headdim must be 64 and dstate 128 (the benchmark shapes).
 """
 
 from __future__ import annotations
@@ -161,15 +162,23 @@ def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bia
                               return_final_states=False, return_varlen_states=False):
     """mamba_ssm's ``mamba_chunk_scan_combined`` on the B200 SSD kernels (autograd).
 
-    Returns y, or (y, final_states) with ``return_final_states``.  ``chunk_size``
-    is accepted for signature compatibility; the result does not depend on it."""
-    assert z is None, "z gating is not supported yet"
+    Returns y, or (y, final_states) with ``return_final_states``; with ``z``
+    (batch, seqlen, nheads, headdim) y is gated by silu(z).  ``chunk_size`` is
+    accepted for signature compatibility; the result does not depend on it."""
     assert seq_idx is None and cu_seqlens is None and not return_varlen_states, \
         "packed sequences (seq_idx / cu_seqlens) are not supported yet"
-    assert tuple(dt_limit) == (0.0, float("inf")), "dt_limit is not supported yet"
     assert chunk_size > 0 and math.log2(chunk_size).is_integer(), "chunk_size must be a power of two"
+    assert z is None or z.shape == x.shape, "z must have the shape of x"
     if dt_bias is not None:
         dt = dt + dt_bias
     if dt_softplus:
         dt = F.softplus(dt)
-    return SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)
+    dt_min, dt_max = float(dt_limit[0]), float(dt_limit[1])
+    if dt_min > 0.0 or dt_max != float("inf"):
+        dt = dt.clamp(dt_min, dt_max)
+    out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)
+    if z is None:
+        return out
+    y, fin = out if return_final_states else (out, None)
+    y = (y.float() * F.silu(z.float())).to(y.dtype)
+    return (y, fin) if return_final_states else y

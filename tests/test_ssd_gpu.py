@@ -94,6 +94,40 @@ def test_mamba_call_form_autograd():
     torch.testing.assert_close(leaves[5].grad, dD, rtol=1e-3, atol=1e-3)
 
 
+def test_mamba_call_form_z_gating_and_dt_limit():
+    """mamba_chunk_scan_combined with z gating and a dt_limit that clamps on both
+    sides: equals the direct launchers on the clamped dt, gated by silu(z), with
+    the chain rule through the clamp, the softplus and the gate."""
+    from kernels.ssd_combined import mamba_chunk_scan_combined, ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
+    B, L, H, P, N, G = 1, 192, 4, 64, 128, 2
+    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=13)
+    x, dt_raw, A, Bm, Cm, D, dy = (t.to(DEV) for t in (tx, tdt, tA, tB, tC, tD, tdy))
+    z = torch.from_numpy(np.random.default_rng(14).standard_normal((B, L, H, P)).astype(np.float32))
+    z = z.to(torch.bfloat16).to(DEV)
+    bias = torch.full((H,), -1.0, device=DEV)
+    limit = (0.32, 0.33)  # softplus(dt_raw - 1) spans ~0.313-0.341 here: both bounds bite
+    leaves = [t.clone().requires_grad_() for t in (x, dt_raw, A, Bm, Cm, D, z)]
+    y = mamba_chunk_scan_combined(*leaves[:5], 256, D=leaves[5], z=leaves[6], dt_bias=bias, dt_softplus=True,
+                                  dt_limit=limit)
+    y.backward(dy)
+    pre = torch.nn.functional.softplus(dt_raw + bias)
+    inside = (pre >= limit[0]) & (pre <= limit[1])
+    assert 0 < int(inside.sum()) < inside.numel(), "the limit should clamp some but not all of dt"
+    dt = pre.clamp(*limit)
+    y2, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+    gate = torch.nn.functional.silu(z.float())
+    assert torch.equal(y, (y2.float() * gate).to(torch.bfloat16))
+    dys = (dy.float() * gate).to(torch.bfloat16)
+    dx, ddt, dA, dB, dC, dD, _ = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dys, D)
+    torch.testing.assert_close(leaves[0].grad, dx, rtol=0, atol=0)
+    torch.testing.assert_close(leaves[1].grad, ddt * inside * torch.sigmoid(dt_raw + bias), rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(leaves[2].grad, dA, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(leaves[5].grad, dD, rtol=1e-3, atol=1e-3)
+    sg = torch.sigmoid(z.float())
+    dz = (dy.float() * y2.float() * sg * (1 + z.float() * (1 - sg))).to(torch.bfloat16)
+    torch.testing.assert_close(leaves[6].grad, dz, rtol=1e-2, atol=1e-2)
+
+
 def test_ssd_forward_steep_decay_matches_oracle():
     """Large dt * A (cumsum spans over 60 within 16 tokens): the tcgen05 kernels'
     per-element decay path for such key groups, next to the factored one."""
