@@ -22,6 +22,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "ema_common.cuh"
 #include "ema_ssd_b200.h"
 
 namespace emab {
@@ -84,4 +85,37 @@ extern "C" EMA_API int ema_fwd_launch_noalloc(const EmaFwdArgs* args, void* stre
   a.workspace = scratch;
   a.workspace_bytes = EMA_NOALLOC_SCRATCH_BYTES;
   return ema_fwd_launch(&a, stream);
+}
+
+// The kernels report a give-up of a bounded wait (a look-back or load that
+// did not complete within its time limit) and a ticket count that shows two
+// launches shared the scratch at once in the scratch's header status word.
+// Callers of ema_fwd_launch read that word through their own workspace
+// pointer (ema_workspace_status); callers of the entry point above never see
+// the static array's address, so this reads (and optionally clears) the word
+// for them.  Before the first ema_fwd_launch_noalloc on the current device
+// there is nothing to report: *status is 0.
+extern "C" EMA_API int ema_noalloc_status(uint32_t* status, int32_t clear, void* stream) {
+  if (status == nullptr) return fail_msg(EMA_ERR_INVALID_ARGUMENT, "ema_noalloc_status: status is NULL");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail_msg(EMA_ERR_CUDA, "ema_noalloc_status: no usable current device");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    scratch = g_scratch_ptr[dev];
+  }
+  *status = 0u;
+  if (scratch == nullptr) return EMA_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* word = static_cast<uint32_t*>(scratch) + emab::kHdrStatus;
+  char msg[256];
+  cudaError_t e = cudaMemcpyAsync(status, word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) {
+    snprintf(msg, sizeof(msg), "ema_noalloc_status: %s", cudaGetErrorString(e));
+    return fail_msg(EMA_ERR_CUDA, msg);
+  }
+  return EMA_OK;
 }

@@ -168,6 +168,24 @@ EMA_API int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], flo
  */
 #define EMA_NOALLOC_SCRATCH_BYTES (4u << 20)
 EMA_API int ema_fwd_launch_noalloc(const EmaFwdArgs* args, void* stream);
+/* Status word of that static scratch on the current device (the counterpart of
+ * ema_workspace_status for callers that never see the array): copies it to
+ * *status, synchronising with `stream`, and clears it afterwards when `clear`
+ * is non-zero.  Non-zero bits (EMA_DEVSTATUS_*) mean a device-side wait gave
+ * up or two calls overlapped on the array, and the results are invalid.  0
+ * before the first ema_fwd_launch_noalloc on the device.  No counterpart in
+ * the reference.
+ */
+EMA_API int ema_noalloc_status(uint32_t* status, int32_t clear, void* stream);
+
+/* ---- dt rows ----------------------------------------------------------------
+ * No counterpart in the reference.  Copies dt (B,L,H) float32 into dt_rows
+ * transposed, (B,H,L): one contiguous row of seqlen values per (batch, head),
+ * the layout EmaFwdArgs.dt_rows / EmaBwdArgs.dt_rows hold.  The forward fills
+ * its dt_rows buffer itself; this is for a backward whose caller kept only dt.
+ */
+EMA_API int ema_dt_rows_launch(const float* dt, float* dt_rows, int64_t batch, int64_t seqlen, int64_t nheads,
+                               void* stream);
 
 /* ---- utilities ------------------------------------------------------------ */
 /* Copies the workspace status word to *status (synchronises with `stream`). */
