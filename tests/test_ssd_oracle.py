@@ -72,3 +72,15 @@ def test_adjoint_matches_finite_differences():
         m[idx] -= eps
         fd = (loss(**{name: p}) - loss(**{name: m})) / (2 * eps)
         np.testing.assert_allclose(g[gname][idx], fd, rtol=1e-6, atol=1e-8, err_msg=gname)
+
+
+@pytest.mark.parametrize("L,Q,G", [(50, 16, 1), (64, 32, 2), (40, 64, 1)])
+def test_chunked_adjoint_matches_sequential_adjoint(L, Q, G):
+    x, dt, A, B, C, D, dy = so.make_ssd_inputs(2, L, 4, 6, 5, ngroups=G, seed=L * Q, dt_range=(0.05, 0.5))
+    rng = np.random.default_rng(5)
+    s0 = rng.standard_normal((2, 4, 6, 5))
+    dfin = rng.standard_normal((2, 4, 6, 5))
+    r = so.ssd_bwd(x, dt, A, B, C, dy, D, initial_state=s0, d_final_state=dfin)
+    c = so.ssd_chunked_bwd(x, dt, A, B, C, dy, Q, D, initial_state=s0, d_final_state=dfin)
+    for name in ("dx", "ddt", "dA", "dB", "dC", "dD", "d_initial_state"):
+        np.testing.assert_allclose(c[name], r[name], rtol=1e-9, atol=1e-11, err_msg=name)
