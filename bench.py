@@ -426,10 +426,13 @@ def main():
 
     hx, hdt, hA, hdy = _inputs(rank, dev)
     x, dt, A, dy = (t.to(dev) for t in (hx, hdt, hA, hdy))
+    # dt transposed to (B, H, L) by the forward launch and read by the backward,
+    # as the autograd op does (ctx saves it)
+    dtr = torch.empty(x.shape[0], H, L, dtype=torch.float32, device=dev)
     if args.mode == "profile":
         for _ in range(max(1, args.steps)):
-            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
-            ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
+            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
+            ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
         torch.cuda.synchronize(dev)
         if dist is not None:
             dist.destroy_process_group()
@@ -439,15 +442,15 @@ def main():
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
-        ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
+        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
+        ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_fwd, stream=side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q)
+        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
     with torch.cuda.graph(g_bwd, pool=g_fwd.pool(), stream=side):
-        dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, states, dy, QB)
+        dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB, read to clean the L2
 
@@ -591,7 +594,7 @@ def main():
                     "api": "kernels.ema_chunk_scan.ema_chunk_scan_combined (autograd); inputs copied from "
                            "pinned host memory every step (next step's copy overlapped with this step's "
                            "compute), the loss and dA read back"},
-            "gpu_launches": 2 * K,  # ema_fwd_kernel + ema_bwd_kernel per step
+            "gpu_launches": 3 * K,  # dt_rows_kernel + ema_fwd_kernel + ema_bwd_kernel per step
             "clocks": clocks.summary(),
             "device_status": status,
         }

@@ -4,6 +4,7 @@
 
 #include <atomic>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -186,6 +187,43 @@ int check_shape(int64_t B, int64_t L, int64_t H, int64_t P, int64_t Q, int dtype
   return EMA_OK;
 }
 
+// dt (B, L, H) -> (B, H, L) through a 32 x 33 shared tile: each warp reads
+// 32 heads of one token (one 128-byte row) and writes 32 tokens of one head.
+// Grid (ceil(L/32), ceil(H/32), B), 256 threads.
+__global__ void __launch_bounds__(256) dt_rows_kernel(const float* __restrict__ dt, float* __restrict__ rows, int L,
+                                                      int H) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z, t0 = blockIdx.x * 32, h0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float* src = dt + static_cast<size_t>(b) * L * H;
+#pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int t = t0 + r, h = h0 + tx;
+    if (t < L && h < H) tile[r][tx] = src[static_cast<size_t>(t) * H + h];
+  }
+  __syncthreads();
+  float* dst = rows + static_cast<size_t>(b) * H * L;
+#pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int h = h0 + r, t = t0 + tx;
+    if (t < L && h < H) dst[static_cast<size_t>(h) * L + t] = tile[tx][r];
+  }
+}
+
+// dt (B, L, H) -> (B, H, L): one contiguous row per (batch, head), so each
+// scan tile loads its dt with one bulk copy.
+int launch_dt_rows(const float* dt, float* rows, int64_t B, int64_t L, int64_t H, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(rows) % 16 != 0)
+    return fail(EMA_ERR_INVALID_ARGUMENT, "dt_rows must be 16-byte aligned");
+  if (B > 65535 || (H + 31) / 32 > 65535)
+    return fail(EMA_ERR_UNSUPPORTED, "dt_rows: batch or nheads too large for the transpose grid");
+  dim3 grid(static_cast<unsigned>((L + 31) / 32), static_cast<unsigned>((H + 31) / 32), static_cast<unsigned>(B));
+  dt_rows_kernel<<<grid, 256, 0, s>>>(dt, rows, static_cast<int>(L), static_cast<int>(H));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "dt_rows: launch failed: %s", cudaGetErrorString(e));
+  return EMA_OK;
+}
+
 int map_dispatch_result(int r, const char* what) {
   if (r == 0) return EMA_OK;
   if (r == -1) return fail(EMA_ERR_UNSUPPORTED, "%s: no kernel for this combination", what);
@@ -301,6 +339,14 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   p.rows = a->dA;
   p.dt = a->dt;
   p.A = a->A;
+  p.dt_rows = 0;
+  if (a->dt_rows != nullptr) {
+    if (!dt_form) return fail(EMA_ERR_INVALID_ARGUMENT, "dt_rows: dt form only");
+    r = launch_dt_rows(a->dt, a->dt_rows, a->batch, a->seqlen, a->nheads, static_cast<cudaStream_t>(stream));
+    if (r) return r;
+    p.dt = a->dt_rows;
+    p.dt_rows = 1;
+  }
   p.seq_idx = a->seq_idx;
   p.seq_idx_type = a->seq_idx_type;
   p.init = a->initial_state;
@@ -393,6 +439,8 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
   p.rows = a->da_cs;
   p.dt = a->dt;
   p.A = a->A;
+  p.dt_rows = 0;  // the rows copy is switched in below, for the CUDA-core kernel only
+  if (a->dt_rows != nullptr && !dt_form) return fail(EMA_ERR_INVALID_ARGUMENT, "dt_rows: dt form only");
   p.states = a->states;
   p.st_b = a->states_stride[0];
   p.st_c = a->states_stride[1];
@@ -423,6 +471,10 @@ int ema_bwd_launch(const EmaBwdArgs* a, void* stream) {
     if (r == 0) return EMA_OK;
     if (r == -3) return EMA_ERR_CUDA;
     if (r != 1) return map_dispatch_result(r, "ema_bwd (tensor cores)");
+  }
+  if (a->dt_rows != nullptr) {
+    p.dt = a->dt_rows;
+    p.dt_rows = 1;
   }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = bwd_dispatch_bf16(l); break;
@@ -461,6 +513,14 @@ int chunk_cumsum_launch(const float* dA, const int64_t dA_stride[3], float* dA_c
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "chunk_cumsum: launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
+}
+
+int ema_dt_rows_launch(const float* dt, float* dt_rows, int64_t batch, int64_t seqlen, int64_t nheads, void* stream) {
+  if (dt == nullptr || dt_rows == nullptr) return fail(EMA_ERR_INVALID_ARGUMENT, "dt_rows: NULL argument");
+  if (batch < 0 || seqlen < 0 || nheads < 0) return fail(EMA_ERR_INVALID_ARGUMENT, "dt_rows: bad shape");
+  if (batch == 0 || seqlen == 0 || nheads == 0) return EMA_OK;
+  if (seqlen > INT32_MAX || nheads > INT32_MAX) return fail(EMA_ERR_UNSUPPORTED, "dt_rows: shape too large");
+  return launch_dt_rows(dt, dt_rows, batch, seqlen, nheads, static_cast<cudaStream_t>(stream));
 }
 
 int ema_workspace_status(const void* workspace, uint32_t* status, void* stream) {

@@ -14,10 +14,12 @@
 //   look-back warp  follows the ring and fetches each tile's incoming state
 //                   (forward) or arriving gradient (backward) from the tiles
 //                   before it while the compute warps run the tile's first pass;
-//   compute warps   scan the tile in the stage: warp w owns a token segment,
-//                   lane l owns BP/32 channels as packed fp32x2 pairs; the
-//                   segment's decay products come from warp shuffles, its
-//                   local scan (and, backward, its local gradient) runs
+//   compute warps   scan the tile in the stage: warp w owns a token segment
+//                   of it.  Forward: lane l owns a channel pair (BP / 32
+//                   channels) over the whole segment, so the local scan needs
+//                   no shuffles; backward: lane (run, group) owns a channel
+//                   group over a run of tokens, runs chained with shuffles.
+//                   The local scan (and, backward, the local gradient) runs
 //                   sequentially per thread and stays in registers; segments
 //                   are chained in shared memory (two block barriers per
 //                   tile), tiles through global memory; outputs go straight
@@ -57,13 +59,18 @@ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 // Stage count and CTAs per SM for a ring of `stage`-byte stages plus `priv`
 // bytes of per-CTA state: two CTAs per SM when each still gets >= 3 stages
 // (one computing, two loading), else one CTA with as many stages as fit.
-template <int STAGE, int PRIV>
+template <int STAGE, int PRIV, int MAXC = 2>
 struct Ring {
-  static constexpr int S2 = ((kSmemPerSM / 2 - kCtaReserve) - PRIV) / STAGE;
-  static constexpr int S1 = (kSmemPerCtaMax - PRIV) / STAGE;
-  static constexpr bool TWO = S2 >= 3;
-  static constexpr int S = TWO ? (S2 > kMaxStages ? kMaxStages : S2) : (S1 > kMaxStages ? kMaxStages : S1);
-  static constexpr int CTAS = TWO ? 2 : 1;
+  static constexpr int stages(int n) {
+    return n == 1 ? (kSmemPerCtaMax - PRIV) / STAGE : ((kSmemPerSM / n - kCtaReserve) - PRIV) / STAGE;
+  }
+  static constexpr int pick() {
+    for (int n = MAXC; n >= 2; --n)
+      if (stages(n) >= 3) return n;
+    return 1;
+  }
+  static constexpr int CTAS = pick();
+  static constexpr int S = stages(CTAS) > kMaxStages ? kMaxStages : stages(CTAS);
   static constexpr bool OK = S >= 1;
 };
 
@@ -107,6 +114,7 @@ struct FwdParams {
   const float* rows;  // (B,H,L) log2 decay dA (reference form)
   const float* dt;    // (B,L,H) dt (dt form)
   const float* A;     // (H,)
+  int dt_rows;        // dt laid out (B,H,L): one contiguous row per tile
   const void* seq_idx;
   int seq_idx_type;
   const float* init;  // (B,H,P)
@@ -128,6 +136,7 @@ struct BwdParams {
   const float* rows;  // (B,H,L) within-chunk log2 cumsum da_cs (reference form)
   const float* dt;    // (B,L,H) dt (dt form)
   const float* A;     // (H,)
+  int dt_rows;        // dt laid out (B,H,L): one contiguous row per tile
   const float* states;
   long long st_b, st_c, st_h, st_p;
   const float* d_final;  // (B,H,P)
@@ -574,35 +583,89 @@ __device__ __forceinline__ void chain_segments_rev(float* s_R, const float* s_D,
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
-// Tokens per compute-warp segment of the forward at block headdim BP.
+// Compute-warp layout of the forward ("channel-pair lanes"): warp w owns the
+// SEG consecutive tokens [w SEG, (w + 1) SEG) of the tile and all of its BP
+// channels; lane l owns channels [l CPL, (l + 1) CPL) (CPL = BP / 32: one
+// bf16x2 / f16x2 word or a float2 at headdim 64) and runs the recurrence
+// sequentially over the SEG tokens.  A warp reads one whole tile row per
+// shared-memory instruction (consecutive 4- or 8-byte words: conflict-free
+// without swizzle) and writes one whole row of y per store instruction (a
+// full 128-byte line at headdim 64, bf16); a segment's end state needs no
+// shuffles, only the per-token decay table (one exp per token).
+// Tokens per compute warp: 32 at headdim <= 64 (one token per lane in the
+// per-token table), 16 at headdim <= 128 (4 channels per lane: the local
+// results of 16 tokens fill the same 64 registers).
 constexpr int fwd_segment_tokens(int BP) { return BP == 64 ? 32 : 16; }
 
+// CPL consecutive elements of this lane as CPL / 2 float pairs (shared memory).
+template <typename T, int CPL>
+__device__ __forceinline__ void lane_load(const T* p, float2 (&v)[CPL / 2]) {
+  float f[CPL];
+  load_pack<T, CPL>(p, f);
+#pragma unroll
+  for (int q = 0; q < CPL / 2; ++q) v[q] = make_float2(f[2 * q], f[2 * q + 1]);
+}
+// Streaming store of CPL elements to global memory.
+template <typename T, int CPL>
+__device__ __forceinline__ void lane_store_cs(T* p, const float2 (&v)[CPL / 2]) {
+  float f[CPL];
+#pragma unroll
+  for (int q = 0; q < CPL / 2; ++q) {
+    f[2 * q] = v[q].x;
+    f[2 * q + 1] = v[q].y;
+  }
+  store_pack_global_cs<T, CPL>(p, f);
+}
+// v rounded to T and back (the value a store of T keeps).
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f32(from_f32<T>(v));
+}
+
+template <int CPL>
+__device__ __forceinline__ void lane_st_f32(float* p, const float2 (&v)[CPL / 2]) {
+  if constexpr (CPL == 2) {
+    *reinterpret_cast<float2*>(p) = v[0];
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+  }
+}
+template <int CPL>
+__device__ __forceinline__ void lane_ld_f32(const float* p, float2 (&v)[CPL / 2]) {
+  if constexpr (CPL == 2) {
+    v[0] = *reinterpret_cast<const float2*>(p);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
 template <typename T, int BP, int Q>
 struct FwdCfg {
-  static constexpr int CPL = 8;  // channels per compute lane
-  using Ln = Lanes<BP, CPL, 8>;
-  static constexpr int CG = Ln::CG, TS = Ln::TS, SEG = Ln::SEG, NPR = Ln::NPR, RUN = Ln::RUN;
+  static constexpr int CPL = BP / 32;  // channels per lane
+  static constexpr int NPL = CPL / 2;  // float pairs per lane
+  static constexpr int SEG = fwd_segment_tokens(BP);
   static constexpr int CPT = BP / 32;  // channels per lane of the look-back warp
   static constexpr int NW = Q / SEG;   // compute warps
   static constexpr int NC = NW * 32;   // compute threads
   static constexpr int NT = NC + 64;   // + producer warp + look-back warp
   static_assert((BP == 64 || BP == 128) && Q % SEG == 0 && NC >= BP && NC >= Q && NW <= 32, "geometry");
-  static_assert(SEG == fwd_segment_tokens(BP), "segment size known to the host");
   static constexpr int kX = Q * BP * static_cast<int>(sizeof(T));
   static constexpr int kStage = align_up(kX + (Q + 4) * 4, 128);  // x tile | decay row | A_h
-  // per-CTA state after the ring
-  static constexpr int oTok = 0;                              // float4[tix]  (a, a, w, w)
-  static constexpr int oG = oTok + tix_size<RUN>(Q) * 16;            // float2[tix]  decay from the run start through t
-  static constexpr int oL2 = oG + tix_size<RUN>(Q) * 8;              // float[Q]     log2 decay
-  static constexpr int oE = align_up(oL2 + Q * 4, 16);        // float[NW][BP + pad]
-  static constexpr int oD = oE + NW * (BP + kRowPad) * 4;     // float[NW]
-  static constexpr int oG0 = oD + NW * 4;                     // float[NW]
-  static constexpr int oSin = align_up(oG0 + NW * 4, 16);     // float[2][BP]  from the look-back warp
-  static constexpr int oEt = oSin + 2 * BP * 4;               // float[BP]
-  static constexpr int oMisc = oEt + BP * 4;                  // float[32]
-  static constexpr int oTile = oMisc + 32 * 4;                // int[kMaxStages]
+  static constexpr int oTok = 0;                               // float4[Q]  (a, w, g, log2 decay)
+  static constexpr int oE = align_up(oTok + Q * 16, 16);       // float[NW][BP + pad]
+  static constexpr int oD = oE + NW * (BP + kRowPad) * 4;      // float[NW]
+  static constexpr int oG0 = oD + NW * 4;                      // float[NW]
+  static constexpr int oSin = align_up(oG0 + NW * 4, 16);      // float[2][BP]  from the look-back warp
+  static constexpr int oEt = oSin + 2 * BP * 4;                // float[BP]
+  static constexpr int oMisc = oEt + BP * 4;                   // float[32]
+  static constexpr int oTile = oMisc + 32 * 4;                 // int[kMaxStages]
   static constexpr int oInfo = align_up(oTile + kMaxStages * 4, 16);  // TileInfo[kMaxStages]
-  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));  // full, empty, tid_full, vec_full/empty
+  static constexpr int oBar = oInfo + kMaxStages * static_cast<int>(sizeof(TileInfo));
   static constexpr int kPriv = oBar + (3 * kMaxStages + 4) * 8;
   using R = Ring<kStage, kPriv>;
   static constexpr int S = R::S;
@@ -615,13 +678,10 @@ template <typename T, int BP, int Q, int MODE, bool SEQ>
 __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     ema_fwd_kernel(const __grid_constant__ CUtensorMap tm_x, const FwdParams p) {
   using C = FwdCfg<T, BP, Q>;
-  constexpr int CPT = C::CPT, CG = C::CG, TS = C::TS, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S;
-  constexpr int CPL = C::CPL, NPR = C::NPR, RUN = C::RUN;
+  constexpr int CPT = C::CPT, SEG = C::SEG, NW = C::NW, NC = C::NC, S = C::S, CPL = C::CPL, NPL = C::NPL;
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* priv = smem + C::kPrivBase;
   float4* s_tok = reinterpret_cast<float4*>(priv + C::oTok);
-  float2* s_g = reinterpret_cast<float2*>(priv + C::oG);
-  float* s_l2 = reinterpret_cast<float*>(priv + C::oL2);
   float* s_E = reinterpret_cast<float*>(priv + C::oE);
   float* s_D = reinterpret_cast<float*>(priv + C::oD);
   float* s_G0 = reinterpret_cast<float*>(priv + C::oG0);
@@ -669,21 +729,23 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       unsigned char* st = smem + s * C::kStage;
       float* raw = reinterpret_cast<float*>(st + C::kX);
       const int n = min(Q, p.L - t0);
-      const float* src = (MODE == kFwdDt) ? p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h
-                                          : p.rows + static_cast<size_t>(bh) * p.L + t0;
-      const uint32_t bulk = (MODE == kFwdDt) ? 0u : row_bulk_bytes(src, n);
+      const bool rows = (MODE != kFwdDt) || p.dt_rows;
+      const float* src = (MODE != kFwdDt) ? p.rows + static_cast<size_t>(bh) * p.L + t0
+                         : rows ? p.dt + static_cast<size_t>(bh) * p.L + t0
+                                : p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h;
+      const uint32_t bulk = rows ? row_bulk_bytes(src, n) : 0u;
       if (lane == 0) {
         s_tile[s] = ticket;
         s_info[s] = TileInfo{c, b, h, t0, bh, 0, b * p.sy_b + static_cast<long long>(t0) * p.sy_l + h * p.sy_h};
         mbar_arrive_expect_tx(&full[s], C::kX + bulk);
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
       }
-      if (MODE == kFwdDt) {
-        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
-        if (lane == 0) cp_async_4(raw + Q, p.A + h);
-      } else {
+      if (rows) {
         load_row(raw, src, n, bulk, &full[s], lane);
+      } else {
+        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
       }
+      if (MODE == kFwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
     }, [&](int ticket) {
       const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
       const int b = fast_div(bh, p.div_h), h = bh - b * p.H;
@@ -716,16 +778,10 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   }
 
   // ------------------------------ compute warps ---------------------------
-  const int ts = lane / CG, cg = lane % CG;
-  const int s0 = warp * SEG;      // this warp's first token in the tile
-  const int r0 = s0 + ts * RUN;   // this lane's run
-  const int ch = cg * CPL;        // this lane's channel group
-  const int nch = min(CPL, p.P - ch);  // valid channels of the group (P is a multiple of 4)
+  const int s0 = warp * SEG;  // this warp's first token in the tile
+  const int ch = lane * CPL;  // this lane's first channel
   const unsigned FULL = 0xffffffffu;
-  // this run's per-token entries: r0 is a multiple of RUN, so tix(r0 + u) = tix(r0) + u
-  const float4* tok_r = s_tok + tix<RUN>(r0);
-  const float2* g_r = s_g + tix<RUN>(r0);
-  const long long lane_off = static_cast<long long>(r0) * p.sy_l + ch;  // within a tile's output
+  const float4* tok_w = s_tok + s0;
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!compute_wait(&full[s], (k / S) & 1, status, warp, NC, &s_fail)) break;
@@ -737,7 +793,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     const T* s_x = reinterpret_cast<const T*>(smem + s * C::kStage);
     const float* raw = reinterpret_cast<const float*>(smem + s * C::kStage + C::kX);
 
-    // ---- this warp's tokens: decay, weight, decay products within each run ----
+    // ---- this warp's tokens: decay, weight, decay products from the segment start
     {
       const int i = lane & (SEG - 1);
       const int t = t0 + s0 + i;
@@ -758,22 +814,18 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
             a = 0.f;
         }
       }
-      float g = a;  // product of the decays from the run start through t
+      float g = a;  // product of the decays from the segment start through t
 #pragma unroll
-      for (int o = 1; o < RUN; o <<= 1) {
-        const float n = __shfl_up_sync(FULL, g, o, RUN);
-        if ((i & (RUN - 1)) >= o) g *= n;
+      for (int o = 1; o < SEG; o <<= 1) {
+        const float n = __shfl_up_sync(FULL, g, o, SEG);
+        if (i >= o) g *= n;
       }
-      if (lane < SEG) {
-        s_tok[tix<RUN>(s0 + i)] = make_float4(a, a, w, w);
-        s_g[tix<RUN>(s0 + i)] = f2_bcast(g);
-        s_l2[s0 + i] = l2;
-      }
+      if (lane < SEG) s_tok[s0 + i] = make_float4(a, w, g, l2);
     }
     if (MODE == kFwdLog2 && (p.da_cs != nullptr || p.da_cs_sum != nullptr)) {
       // within-chunk cumsum of the log2 decay (reference outputs da_cs / da_cs_sum)
       named_sync(1, NC);
-      float v = (tid < Q) ? s_l2[tid] : 0.f;
+      float v = (tid < Q) ? s_tok[tid].w : 0.f;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float n = __shfl_up_sync(FULL, v, o);
@@ -789,34 +841,27 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     }
     __syncwarp();
 
-    // ---- pass 1: local scan of the run from zero, kept in registers -----------
-    const T* x_r = s_x + r0 * BP + ch;
-    float2 zl[RUN][NPR];
-    float Dexc;
-    float2 Eexc[NPR];
+    // ---- pass 1: the segment's scan from zero, kept in registers -------------
+    const T* x_l = s_x + s0 * BP + ch;
+    float2 zl[SEG][NPL];
     {
-      float2 z[NPR];
+      float2 z[NPL];
 #pragma unroll
-      for (int q = 0; q < NPR; ++q) z[q] = make_float2(0.f, 0.f);
+      for (int q = 0; q < NPL; ++q) z[q] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int u = 0; u < RUN; ++u) {
-        const float4 tk = tok_r[u];
-        const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
-        float2 xv[NPR];
-        load_grp<T, NPR>(x_r + u * BP, xv);
+      for (int u = 0; u < SEG; ++u) {
+        const float4 tk = tok_w[u];
+        float2 xv[NPL];
+        lane_load<T, CPL>(x_l + u * BP, xv);
 #pragma unroll
-        for (int q = 0; q < NPR; ++q) {
-          z[q] = (MODE == kFwdLog2) ? f2_fma(aa, z[q], xv[q]) : f2_fma(aa, z[q], f2_mul(ww, xv[q]));
+        for (int q = 0; q < NPL; ++q) {
+          z[q] = (MODE == kFwdLog2) ? f2_fma(f2_bcast(tk.x), z[q], xv[q])
+                                    : f2_fma(f2_bcast(tk.x), z[q], f2_mul(f2_bcast(tk.y), xv[q]));
           zl[u][q] = z[q];
         }
       }
-      float Dinc;
-      float2 Einc[NPR];
-      runs_scan_fwd<CG, TS, NPR>(g_r[RUN - 1].x, z, ts, Dinc, Einc, Dexc, Eexc);
-      if (ts == TS - 1) {
-        st_row<NPR>(s_E + warp * (BP + kRowPad) + ch, Einc);  // the segment's end state from zero
-        if (cg == 0) s_D[warp] = Dinc;
-      }
+      lane_st_f32<CPL>(s_E + warp * (BP + kRowPad) + ch, z);  // the segment's end state from zero
+      if (lane == 0) s_D[warp] = tok_w[SEG - 1].z;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the x stage
@@ -844,31 +889,29 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
             fmaf(s_G0[NW / 2], s_Sin[tid], s_E[(NW / 2) * (BP + kRowPad) + tid]);
     }
 
-    // ---- pass 2: y = local scan + (run decay so far) x (state entering the run)
-    float2 tin[NPR];
+    // ---- pass 2: y = local scan + (decay from the segment start) x (state entering it)
+    float2 tin[NPL];
     {
       const float2 g0 = f2_bcast(s_G0[warp]);
-      float2 sin[NPR], sw[NPR];
-      ld_row<NPR>(s_Sin + ch, sin);
-      ld_row<NPR>(s_E + warp * (BP + kRowPad) + ch, sw);
-      const float2 dx = f2_bcast(Dexc);
+      float2 sin[NPL], sw[NPL];
+      lane_ld_f32<CPL>(s_Sin + ch, sin);
+      lane_ld_f32<CPL>(s_E + warp * (BP + kRowPad) + ch, sw);
 #pragma unroll
-      for (int q = 0; q < NPR; ++q) tin[q] = f2_fma(dx, f2_fma(g0, sin[q], sw[q]), Eexc[q]);
+      for (int q = 0; q < NPL; ++q) tin[q] = f2_fma(g0, sin[q], sw[q]);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads the incoming state
-    if (p.y != nullptr) {  // (a state-only pass computes just the chunk and final states)
-      // running row pointer: one 64-bit add per token
-      T* yp = static_cast<T*>(p.y) + ti.out_off + lane_off;
+    if (p.y != nullptr && ch < p.P) {  // (a state-only pass computes just the chunk and final states)
+      T* yp = static_cast<T*>(p.y) + ti.out_off + static_cast<long long>(s0) * p.sy_l + ch;
       const long long ystep = p.sy_l;
-      const int nv = nch > 0 ? p.L - (t0 + r0) : 0;
+      const int nv = p.L - (t0 + s0);
 #pragma unroll
-      for (int u = 0; u < RUN; ++u) {
-        const float2 g = g_r[u];
-        float2 yv[NPR];
+      for (int u = 0; u < SEG; ++u) {
+        const float2 g = f2_bcast(tok_w[u].z);
+        float2 yv[NPL];
 #pragma unroll
-        for (int q = 0; q < NPR; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
-        if (u < nv) store_grp_cs<T, NPR>(yp, yv, nch);
+        for (int q = 0; q < NPL; ++q) yv[q] = f2_fma(g, tin[q], zl[u][q]);
+        if (u < nv) lane_store_cs<T, CPL>(yp, yv);
         yp += ystep;
       }
     }
@@ -1048,9 +1091,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       float* raw = reinterpret_cast<float*>(st + C::oRaw);
       float* sst = reinterpret_cast<float*>(st + C::oSt);
       const int n = min(Q, p.L - t0);
-      const float* src = (MODE == kBwdDt) ? p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h
-                                          : p.rows + static_cast<size_t>(bh) * p.L + t0;
-      const uint32_t bulk = (MODE == kBwdDt) ? 0u : row_bulk_bytes(src, n);
+      const bool rows = (MODE != kBwdDt) || p.dt_rows;
+      const float* src = (MODE != kBwdDt) ? p.rows + static_cast<size_t>(bh) * p.L + t0
+                         : rows ? p.dt + static_cast<size_t>(bh) * p.L + t0
+                                : p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h;
+      const uint32_t bulk = rows ? row_bulk_bytes(src, n) : 0u;
       const float* srow = p.states + b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h;
       const uint32_t sbulk = (p.st_p == 1) ? row_bulk_bytes(srow, p.P) : 0u;
       if (lane == 0) {
@@ -1060,12 +1105,12 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
         tma_load_4d(st + C::kX, &tm_dy, &full[s], 0, h, t0, b);
       }
-      if (MODE == kBwdDt) {
-        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
-        if (lane == 0) cp_async_4(raw + Q, p.A + h);
-      } else {
+      if (rows) {
         load_row(raw, src, n, bulk, &full[s], lane);
+      } else {
+        gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
       }
+      if (MODE == kBwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
       if (sbulk) {
         if (lane == 0) bulk_g2s(sst, srow, sbulk, &full[s]);
       } else {

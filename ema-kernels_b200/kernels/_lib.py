@@ -52,6 +52,7 @@ class EmaFwdArgs(ctypes.Structure):
         ("da_cs", _ptr), ("da_cs_sum", _ptr), ("final_state", _ptr),
         ("workspace", _ptr), ("workspace_bytes", ctypes.c_size_t),
         ("mid_states", _ptr), ("mid_states_stride", _i64 * 4),
+        ("dt_rows", _ptr),
     ]
 
 
@@ -67,6 +68,7 @@ class EmaBwdArgs(ctypes.Structure):
         ("d_final_state", _ptr), ("d_last_token", _ptr),
         ("dl", _ptr), ("ddt", _ptr), ("dA_out", _ptr), ("d_initial_state", _ptr),
         ("workspace", _ptr), ("workspace_bytes", ctypes.c_size_t),
+        ("dt_rows", _ptr),
     ]
 
 
@@ -109,6 +111,8 @@ lib.ema_bwd_launch.argtypes = [ctypes.POINTER(EmaBwdArgs), _ptr]
 lib.chunk_cumsum_launch.restype = ctypes.c_int
 lib.chunk_cumsum_launch.argtypes = [_ptr, ctypes.POINTER(_i64), _ptr, ctypes.POINTER(_i64), _ptr,
                                     ctypes.POINTER(_i64), _i64, _i64, _i64, _i64, _i32, _ptr]
+lib.ema_dt_rows_launch.restype = ctypes.c_int
+lib.ema_dt_rows_launch.argtypes = [_ptr, _ptr, _i64, _i64, _i64, _ptr]
 lib.ema_workspace_status.restype = ctypes.c_int
 lib.ema_workspace_status.argtypes = [_ptr, ctypes.POINTER(ctypes.c_uint32), _ptr]
 lib.ema_workspace_clear_status.restype = ctypes.c_int

@@ -44,7 +44,7 @@ def _check_inputs(x, dt, A, chunk_size):
 def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
                        initial_states: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                        return_final_states: bool = False, state_only: bool = False,
-                       half_chunk_states: bool = False):
+                       half_chunk_states: bool = False, dt_rows: Optional[torch.Tensor] = None):
     """Forward.  Returns (y, chunk_start_states (B, nchunks, H, P) fp32, final_states or None).
 
     ``state_only``: compute only the final state (y and the chunk states are not
@@ -83,6 +83,10 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
             final.copy_(init if init is not None else torch.zeros_like(final))
         return out, (fine[:, :-(-L // (chunk_size // 2))] if mid is not None else states), final
     ws = _lib.workspace(dev, _lib.lib.ema_scan_workspace_size(B, L, H, P, chunk_size))
+    if dt_rows is None:
+        dt_rows = torch.empty(B, H, L, dtype=torch.float32, device=dev)
+    assert dt_rows.shape == (B, H, L) and dt_rows.dtype == torch.float32 and dt_rows.is_contiguous(), \
+        "dt_rows must be a contiguous (batch, nheads, seqlen) float32 buffer"
     a = _lib.EmaFwdArgs()
     a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
     a.dtype = _lib.DTYPE_CODES[x.dtype]
@@ -99,6 +103,7 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
         a.mid_states, a.mid_states_stride = mid.data_ptr(), (_lib._i64 * 4)(s[0], s[1], s[2], s[3])
     a.final_state = _lib.ptr(final)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.dt_rows = dt_rows.data_ptr()
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.ema_fwd_launch(a, _lib.stream_ptr(dev)), "ema_chunk_scan_fwd")
     if mid is not None:  # the chunk-start states of chunk_size / 2 (a short last chunk has no mid)
@@ -109,12 +114,15 @@ def ema_chunk_scan_fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk
 def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, states: torch.Tensor,
                        dy: torch.Tensor, chunk_size: int = 256,
                        d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False,
-                       state_only: bool = False):
+                       state_only: bool = False, dt_rows: Optional[torch.Tensor] = None):
     """Backward.  Returns (dx, ddt fp32 (B,L,H), dA fp32 (H,), d_initial_states or None).
 
     ``state_only``: compute only the gradient w.r.t. the initial state (returns
     (None, None, None, d_initial)) -- the first pass of the sequence-parallel
-    backward; dx, ddt and dA are not written."""
+    backward; dx, ddt and dA are not written.
+
+    ``dt_rows``: dt transposed to (B, H, L), as the forward leaves it in its
+    ``dt_rows`` buffer; made here (one transpose launch) when not given."""
     B, L, H, P = _check_inputs(x, dt, A, chunk_size)
     dev = x.device
     nc = -(-L // chunk_size)
@@ -140,6 +148,13 @@ def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, state
             d_init.copy_(dfin if dfin is not None else torch.zeros_like(d_init))
         return dx, ddt, dA, d_init
     ws = _lib.workspace(dev, _lib.lib.ema_scan_workspace_size(B, L, H, P, chunk_size))
+    if dt_rows is None:
+        dt_rows = torch.empty(B, H, L, dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib.ema_dt_rows_launch(dt_k.data_ptr(), dt_rows.data_ptr(), B, L, H,
+                                                   _lib.stream_ptr(dev)), "ema_dt_rows")
+    assert dt_rows.shape == (B, H, L) and dt_rows.dtype == torch.float32 and dt_rows.is_contiguous(), \
+        "dt_rows must be a contiguous (batch, nheads, seqlen) float32 buffer"
     a = _lib.EmaBwdArgs()
     a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, chunk_size
     a.dtype = _lib.DTYPE_CODES[x.dtype]
@@ -154,6 +169,7 @@ def ema_chunk_scan_bwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, state
     a.ddt, a.dA_out = _lib.ptr(ddt), _lib.ptr(dA)
     a.d_initial_state = _lib.ptr(d_init)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    a.dt_rows = dt_rows.data_ptr()
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.ema_bwd_launch(a, _lib.stream_ptr(dev)), "ema_chunk_scan_bwd")
     return dx, ddt, dA, d_init
@@ -170,10 +186,12 @@ class EmaChunkScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, dt, A, chunk_size, initial_states, return_final_states):
         bq = backward_chunk(chunk_size)
+        B, L, H, _ = x.shape
+        dt_rows = torch.empty(B, H, L, dtype=torch.float32, device=x.device)
         y, states, final = ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states,
                                               return_final_states=return_final_states,
-                                              half_chunk_states=bq != chunk_size)
-        ctx.save_for_backward(x, dt, A, states)
+                                              half_chunk_states=bq != chunk_size, dt_rows=dt_rows)
+        ctx.save_for_backward(x, dt, A, states, dt_rows)
         ctx.chunk_size = bq
         ctx.has_init = initial_states is not None
         ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
@@ -183,12 +201,13 @@ class EmaChunkScanFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy, *rest):
-        x, dt, A, states = ctx.saved_tensors
+        x, dt, A, states, dt_rows = ctx.saved_tensors
         dfin = rest[0] if rest else None
         if dy is None:
             dy = torch.zeros_like(x)
         dx, ddt, dA, d_init = ema_chunk_scan_bwd(x, dt, A, states, dy, ctx.chunk_size,
-                                                 d_final_states=dfin, need_d_initial=ctx.has_init)
+                                                 d_final_states=dfin, need_d_initial=ctx.has_init,
+                                                 dt_rows=dt_rows)
         return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, d_init, None
 
 

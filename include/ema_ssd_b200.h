@@ -91,6 +91,12 @@ typedef struct EmaFwdArgs {
    * array of chunk_size / 2, so the backward can run on half-size chunks. */
   float* mid_states;
   int64_t mid_states_stride[4];
+  /* Not in the reference interface: dt form only, a (B,H,L) float32 buffer or
+   * NULL.  When given, the launcher first copies dt into it transposed (one
+   * contiguous row of seqlen values per (batch, head)), and the kernel loads
+   * each tile's dt as one row instead of gathering a column strided by nheads;
+   * the buffer then holds what EmaBwdArgs.dt_rows takes. */
+  float* dt_rows;
 } EmaFwdArgs;
 
 /* ---- EMA backward ---------------------------------------------------------
@@ -132,6 +138,10 @@ typedef struct EmaBwdArgs {
   float* d_initial_state; /* (B,H,P) contiguous or NULL */
   void* workspace;
   size_t workspace_bytes;
+  /* Not in the reference interface: dt form only, dt transposed to (B,H,L)
+   * (as EmaFwdArgs.dt_rows leaves it) or NULL; when given, each tile's dt is
+   * read from it as one contiguous row (`dt` is still required). */
+  const float* dt_rows;
 } EmaBwdArgs;
 
 /* Bytes of workspace the EMA launchers need for this shape. */
