@@ -55,21 +55,124 @@ def test_config1_fp32_forward():
     assert_fp32_close(dA, g["dA"], "dA")
 
 
+_ORACLE_CACHE = {}
+
+
+def _full_size_case(B, L, seed):
+    """Seeded bf16 inputs of a benchmark shape (H32 P64) and the float64 oracle's
+    outputs on the same bf16-rounded values, computed once per module."""
+    key = (B, L, seed)
+    if key not in _ORACLE_CACHE:
+        H, P = 32, 64
+        tx, tdt, tA, tdy = _inputs(B, L, H, P, seed, torch.bfloat16)
+        xf, dyf = tx.float().numpy(), tdy.float().numpy()
+        r = eo.ema_dt_fwd(xf, tdt.numpy(), tA.numpy())
+        g = eo.ema_dt_bwd(xf, tdt.numpy(), tA.numpy(), dyf)
+        _ORACLE_CACHE[key] = (tx, tdt, tA, tdy, r["y"], g)
+    return _ORACLE_CACHE[key]
+
+
+def _autograd_step(tx, tdt, tA, tdy, Q):
+    from kernels.ema_chunk_scan import ema_chunk_scan_combined
+    x, dt, A = (t.to(DEV).requires_grad_() for t in (tx, tdt, tA))
+    y = ema_chunk_scan_combined(x, dt, A, Q)
+    y.backward(tdy.to(DEV))
+    return y.detach(), x.grad, dt.grad, A.grad
+
+
 def test_config2_bf16_full_size():
     """BASELINE config 2 at full size: B8 L4096 H32 P64 chunk 256, bf16 I/O,
-    fp32 accumulation; y, dx, ddt and dA within 2e-2 rel / 1e-2 abs."""
-    B, L, H, P, Q = 8, 4096, 32, 64, 256
-    tx, tdt, tA, tdy = _inputs(B, L, H, P, 7, torch.bfloat16)
-    y, fin, dx, ddt, dA, _, _ = _run(tx, tdt, tA, tdy, Q)
-    xf = tx.float().numpy()
-    dyf = tdy.float().numpy()
-    r = eo.ema_dt_fwd(xf, tdt.numpy(), tA.numpy())
-    g = eo.ema_dt_bwd(xf, tdt.numpy(), tA.numpy(), dyf)
-    assert_lowp_close(y, r["y"], "y")
+    fp32 accumulation, through the autograd op the benchmark times (256-token
+    forward saving the state entering every 128 tokens, 128-token backward,
+    dt transposed once and shared); y, dx, ddt and dA within 2e-2 rel / 1e-2 abs."""
+    tx, tdt, tA, tdy, y_ref, g = _full_size_case(8, 4096, 7)
+    y, dx, ddt, dA = _autograd_step(tx, tdt, tA, tdy, 256)
+    assert_lowp_close(y, y_ref, "y")
     assert_lowp_close(dx, g["dx"], "dx")
     assert_lowp_close(ddt, g["ddt"], "ddt")
     assert_lowp_close(dA, g["dA"], "dA")
     assert_fp32_close(ddt, g["ddt"], "ddt (fp32 accumulation)")
+
+
+def test_config2_bf16_full_size_direct_launchers():
+    """The same inputs through the direct launchers at 256-token tiles in both
+    directions (the pair a caller without the autograd op gets)."""
+    tx, tdt, tA, tdy, y_ref, g = _full_size_case(8, 4096, 7)
+    y, fin, dx, ddt, dA, _, _ = _run(tx, tdt, tA, tdy, 256)
+    assert_lowp_close(y, y_ref, "y")
+    assert_lowp_close(dx, g["dx"], "dx")
+    assert_lowp_close(ddt, g["ddt"], "ddt")
+    assert_lowp_close(dA, g["dA"], "dA")
+
+
+def test_config4_bf16_full_size_one_gpu():
+    """BASELINE config 4's sequence on one GPU: B1 L65536 H32 P64 chunk 256, bf16,
+    through the autograd op (32 chains of 256 tiles: the longest look-back
+    chains of the benchmark shapes)."""
+    tx, tdt, tA, tdy, y_ref, g = _full_size_case(1, 65536, 21)
+    y, dx, ddt, dA = _autograd_step(tx, tdt, tA, tdy, 256)
+    assert_lowp_close(y, y_ref, "y")
+    assert_lowp_close(dx, g["dx"], "dx")
+    assert_lowp_close(ddt, g["ddt"], "ddt")
+    assert_lowp_close(dA, g["dA"], "dA")
+
+
+@pytest.mark.parametrize("L", [1000, 999])
+def test_dt_rows_and_strided_dt_agree(L):
+    """The launchers read each tile's dt either as one row of the (B, H, L) copy
+    the forward makes (the Python API's path) or as a column of dt (B, L, H)
+    strided by nheads (a C caller that passes no dt_rows buffer).  Both agree
+    with each other and with the oracle; L = 999 leaves the rows unaligned for
+    bulk copies (element-wise fallback)."""
+    import ctypes
+
+    from kernels import _lib
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    B, H, P, Q = 2, 3, 64, 256
+    tx, tdt, tA, tdy = _inputs(B, L, H, P, L, torch.bfloat16)
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    y, st, _ = ema_chunk_scan_fwd(x, dt, A, Q)
+    dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, st, dy, Q)
+
+    nc = -(-L // Q)
+    stream = _lib.stream_ptr(torch.device(DEV))
+    ws = torch.zeros(_lib.lib.ema_scan_workspace_size(B, L, H, P, Q), dtype=torch.uint8, device=DEV)
+    y2 = torch.empty_like(x)
+    st2 = torch.empty(B, nc, H, P, dtype=torch.float32, device=DEV)
+    a = _lib.EmaFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, Q
+    a.dtype = _lib.DTYPE_CODES[x.dtype]
+    a.x, a.x_stride = x.data_ptr(), _lib.strides3(x)
+    a.out, a.out_stride = y2.data_ptr(), _lib.strides3(y2)
+    a.dt, a.A = dt.data_ptr(), A.data_ptr()
+    s = st2.stride()
+    a.states, a.states_stride = st2.data_ptr(), (_lib._i64 * 4)(*s)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(_lib.lib.ema_fwd_launch(ctypes.byref(a), stream), "forward, strided dt")
+    dx2 = torch.empty_like(x)
+    ddt2 = torch.empty(B, L, H, dtype=torch.float32, device=DEV)
+    dA2 = torch.empty(H, dtype=torch.float32, device=DEV)
+    b = _lib.EmaBwdArgs()
+    b.batch, b.seqlen, b.nheads, b.headdim, b.chunk_size = B, L, H, P, Q
+    b.dtype = a.dtype
+    b.x, b.x_stride = x.data_ptr(), _lib.strides3(x)
+    b.dout, b.dout_stride = dy.data_ptr(), _lib.strides3(dy)
+    b.dx, b.dx_stride = dx2.data_ptr(), _lib.strides3(dx2)
+    b.dt, b.A = dt.data_ptr(), A.data_ptr()
+    b.states, b.states_stride = st2.data_ptr(), (_lib._i64 * 4)(*s)
+    b.ddt, b.dA_out = ddt2.data_ptr(), dA2.data_ptr()
+    b.workspace, b.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(_lib.lib.ema_bwd_launch(ctypes.byref(b), stream), "backward, strided dt")
+    torch.cuda.synchronize()
+    close = dict(rtol=1e-2, atol=1e-3)  # one bf16 ulp: tiles may combine aggregate or inclusive records
+    torch.testing.assert_close(y2, y, **close)
+    torch.testing.assert_close(st2, st, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(dx2, dx, **close)
+    torch.testing.assert_close(ddt2, ddt, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dA2, dA, rtol=1e-4, atol=1e-4)
+    g = eo.ema_dt_bwd(tx.float().numpy(), tdt.numpy(), tA.numpy(), tdy.float().numpy())
+    assert_lowp_close(dx2, g["dx"], "dx (strided dt)")
+    assert_lowp_close(ddt2, g["ddt"], "ddt (strided dt)")
 
 
 @pytest.mark.parametrize("Q", [64, 128, 256])
