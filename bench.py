@@ -1,4 +1,4 @@
-"""Benchmark: EMA fwd+bwd Mtokens/s at B8 L4096 H32 P64 bf16 (chunk 256), one B200 per rank.
+"""Benchmark: EMA fwd+bwd Mtokens/s at B8 L4096 H32 P64 bf16 (chunk 256).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -6,24 +6,31 @@ Workload (config 2 of the benchmark spec): the dt-parameterised EMA
 ``h_t = exp(dt_t A_h) h_{t-1} + dt_t x_t`` forward + backward (dx, ddt, dA) on
 seeded synthetic inputs -- x, dy ~ N(0,1) bf16; dt = softplus(N(0,1) + b_h) in
 [1e-3, 1e-1]; A = -exp(U(0, log 16)).  A "step" is one forward and one
-backward through the public API (kernels.ema_chunk_scan).
+backward of the whole B8 L4096 batch through kernels.ema_chunk_scan.
 
-Multi-GPU: one process per GPU (torchrun), each rank processes its own
-B8 L4096 H32 P64 batch (weak scaling: batch x heads shard with no data-path
-collective; the per-head dA partials would join the model's gradient
-all-reduce, which this op does not own).
+Multi-GPU (one process per GPU under torchrun): ``value`` is STRONG scaling --
+the global B8 batch is split by batch rows over the ranks (by heads where the
+rows do not divide), no collective on the data path (the per-head dA partials
+would join the model's gradient all-reduce, which this op does not own).
+Extra keys on the same line: ``weak`` (every rank a whole B8 batch),
+``sp_config4`` (config 4, one B1 L65536 sequence split over the ranks with
+the NCCL state chain, and its error against the single-GPU op) and
+``ssd_config5`` (config 5, the Mamba-2 SSD at B32 L8192 H80 split by batch
+rows).
 
-Timing: ``value`` replays the step as two CUDA graphs (forward, backward) with
-inputs resident in HBM; before every step, outside the timed intervals, the L2
-is flushed by a 256 MiB write followed by a 256 MiB read of another buffer (so
-the timed step neither hits its own data in L2 nor pays for writing back the
-flush's dirty lines); CUDA events on the launching stream, summed over exactly
-K steps; max over ranks.  Each step launches exactly two kernels of this
-library (ema_fwd_kernel, ema_bwd_kernel).  ``e2e`` calls the public
-API eagerly: every step copies its inputs from pinned host memory (the next
-step's copy overlapped with this step's compute) and reads back the loss and
-dA, all inside the timed region.  ``cpu_baseline`` times the reference's PyTorch CPU path
-(oracle/ema_torch_path.py) on a bounded sample on rank 0 at N=1.
+Timing: ``value`` replays the step as ONE CUDA graph (dt transpose, forward,
+backward) with inputs resident in HBM; before every step, outside the timed
+interval, the L2 is flushed by a 256 MiB write followed by a 256 MiB read of
+another buffer; CUDA events around each replay on the launching stream, summed
+over exactly K steps; max over ranks.  Events captured inside the graph split
+each step into the forward (transpose + ema_fwd_kernel) and the backward
+(ema_bwd_kernel) for the per-kernel roofline.  ``e2e`` calls the public
+autograd API eagerly: every step copies its inputs from pinned host memory
+(the next step's copy overlapped with this step's compute) and reads back the
+loss and dA, all inside the timed region.  ``cpu_baseline`` times the
+reference's PyTorch CPU path (oracle/ema_torch_path.py) on one fixed sample
+(one batch row at full length) on rank 0 at N=1; ``--impl reference`` times
+the same sample per step.
 """
 
 from __future__ import annotations
@@ -147,9 +154,20 @@ def _inputs(rank, device, dtype=torch.bfloat16):
             torch.from_numpy(dy).to(dtype))
 
 
-def _cpu_baseline():
-    """The reference's CPU path (ema_torch_ref + autograd) on one batch row of the
-    workload at full length: L4096 H32 P64 bf16 = 4096 tokens."""
+CPU_SAMPLE = f"1 of the {B} batch rows at full length (L{L} H{H} P{P} bf16 = {L} tokens)"
+
+
+def _ema_config(world, shard=None):
+    """The workload description both arms print (the reference arm's is identical)."""
+    return {"workload": WORKLOAD, "global_batch": B, "seq_len": L, "nheads": H, "headdim": P, "chunk_size": Q,
+            "parallelism": f"batch x heads split over {world} GPU(s) (strong scaling), no collective",
+            "l2": "flushed before every step outside the timed interval: 256 MiB write, then 256 MiB read "
+                  "of another buffer; step inputs 272 MB > 126 MB L2"}
+
+
+def _cpu_sample_seconds(reps, warm):
+    """Seconds per fwd + autograd bwd of the reference's CPU path on the fixed sample:
+    one batch row of the workload at full length, on all host threads."""
     from oracle import ema_torch_path as tp
     from oracle.ema_oracle import make_dt_inputs
     cores = len(os.sched_getaffinity(0))
@@ -157,43 +175,33 @@ def _cpu_baseline():
     x, dt, A, dy = make_dt_inputs(1, L, H, P, seed=99)
     tx = torch.from_numpy(x).to(torch.bfloat16)
     tdy = torch.from_numpy(dy).to(torch.bfloat16)
-    secs = tp.time_sample(tx, torch.from_numpy(dt), torch.from_numpy(A), tdy)
+    tdt, tA = torch.from_numpy(dt), torch.from_numpy(A)
+    for _ in range(warm):
+        tp.dt_form_fwd_bwd(tx, tdt, tA, tdy)
+    return tp.time_sample(tx, tdt, tA, tdy, reps=reps) / reps, cores
+
+
+def _cpu_baseline():
+    secs, cores = _cpu_sample_seconds(reps=3, warm=1)
     return {"value": L / secs / 1e6, "unit": "Mtokens/s", "cores": cores, "kind": "port",
-            "sample": f"1 of the {B} batch rows at full length (L{L} H{H} P{P} bf16 = {L} tokens), "
-                      f"fwd + autograd bwd of ema_torch_ref in torch on {cores} threads, {secs:.1f} s"}
+            "sample": f"{CPU_SAMPLE}, fwd + autograd bwd of ema_torch_ref in torch on {cores} threads, "
+                      f"1 warm-up + 3 timed passes, {secs:.2f} s per pass"}
 
 
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
     steps = max(1, args.steps)
-    warm = 3  # the contract's minimum; each step is a bounded sample
-    from oracle import ema_torch_path as tp
-    from oracle.ema_oracle import make_dt_inputs
-    cores = len(os.sched_getaffinity(0))
-    torch.set_num_threads(cores)
-    # each step: fwd+bwd of a bounded sample of the workload -- one batch row
-    # (all heads) over Ls tokens, Ls sized so warm-up + K steps take ~2 minutes
-    def sample(n):
-        x, dt, A, dy = make_dt_inputs(1, n, H, P, seed=7)
-        return (torch.from_numpy(x).to(torch.bfloat16), torch.from_numpy(dt), torch.from_numpy(A),
-                torch.from_numpy(dy).to(torch.bfloat16))
-
-    t_probe = tp.time_sample(*sample(256))
-    budget = 120.0 / (steps + warm)
-    Ls = int(min(L, max(64, 256 * budget / max(t_probe, 1e-6))) // 64 * 64)
-    tx, tdt, tA, tdy = sample(Ls)
-    for _ in range(warm):
-        tp.dt_form_fwd_bwd(tx, tdt, tA, tdy)
-    secs = tp.time_sample(tx, tdt, tA, tdy, reps=steps)
-    value = steps * Ls / secs / 1e6
-    sample = (f"per step 1 batch row x L{Ls} (H{H} P{P} bf16, {Ls} tokens) of the workload: fwd + "
-              f"autograd bwd of ema_torch_ref in torch on {cores} threads")
+    warm = max(3, args.warmup)
+    secs, cores = _cpu_sample_seconds(reps=steps, warm=warm)
+    value = L / secs / 1e6
+    sample = (f"per step {CPU_SAMPLE}: fwd + autograd bwd of ema_torch_ref in torch on {cores} threads "
+              f"({warm} warm-up passes)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "Mtokens/s", "n_gpus": world,
-        "steps": steps, "warmup": warm, "ms_per_step": secs / steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_tokens_per_step": Ls},
+        "steps": steps, "warmup": warm, "ms_per_step": secs * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _ema_config(world),
         "cpu_baseline": {"value": value, "unit": "Mtokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "Mtokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -375,44 +383,195 @@ def _tc_peak():
         return 1590.0
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["bench", "profile"], default="bench",
-                    help="profile: run --steps eager fwd+bwd steps and exit (for ncu captures)")
-    ap.add_argument("--profile-batch", type=int, default=0,
-                    help="with --mode profile --workload ssd: batch of the capture (default: the config's)")
-    ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
-                    help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
-                         "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
 
-    rank = int(os.environ.get("RANK", 0))
-    world = int(os.environ.get("WORLD_SIZE", 1))
-    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+def _shard(world, rank):
+    """Rows (or, where the rows do not divide, heads) of the global batch for this rank."""
+    if B % world == 0:
+        n = B // world
+        return slice(rank * n, (rank + 1) * n), slice(0, H)
+    if H % world == 0:
+        n = H // world
+        return slice(0, B), slice(rank * n, (rank + 1) * n)
+    raise SystemExit(f"--gpus {world} divides neither the batch ({B}) nor the heads ({H})")
 
-    if args.impl == "reference":
-        if args.workload != "ema":
-            if rank == 0:
-                print(json.dumps({"impl": "reference", "workload": args.workload,
-                                  "unavailable": "the reference has no CPU path for this workload "
-                                                 "(SSD is the absent mamba_ssm package; SP is not in the reference)"}))
-            return
-        run_reference_arm(args, rank, world)
-        return
-    if args.workload == "ssd":
-        run_ssd(args, rank, world, local_rank)
-        return
-    if args.workload == "sp":
-        run_sp(args, rank, world, local_rank)
-        return
 
+class StepGraph:
+    """One CUDA graph per step: dt transpose + forward, then the backward, with
+    timing events captured between them (the per-kernel split of each replay)."""
+
+    def __init__(self, x, dt, A, dy, dev):
+        from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
+        b_, l_, h_, _ = x.shape
+        self.qb = backward_chunk(Q)  # what the autograd op runs: 128-token backward tiles on half-chunk states
+        self.dtr = torch.empty(b_, h_, l_, dtype=torch.float32, device=dev)
+
+        def fwd():
+            return ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=self.qb != Q, dt_rows=self.dtr)
+
+        def bwd(states):
+            return ema_chunk_scan_bwd(x, dt, A, states, dy, self.qb, dt_rows=self.dtr)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # eager warm-up: allocates this stream's workspace
+            _, st, _ = fwd()
+            bwd(st)
+        side.synchronize()
+        self.ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+        self.g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g, stream=side):
+            self.ev[0].record()
+            self.y, st, _ = fwd()
+            self.ev[1].record()
+            self.grads = bwd(st)
+            self.ev[2].record()
+        torch.cuda.current_stream(dev).wait_stream(side)
+
+    def run(self, K, W, flush, stream):
+        """W untimed then K timed replays, each after an L2 flush; returns summed
+        (step, forward, backward) milliseconds."""
+        for _ in range(W):
+            flush()
+            self.g.replay()
+        torch.cuda.synchronize()
+        tot = [0.0, 0.0, 0.0]
+        for _ in range(K):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            self.g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            tot[0] += e0.elapsed_time(e1)
+            tot[1] += self.ev[0].elapsed_time(self.ev[1])
+            tot[2] += self.ev[1].elapsed_time(self.ev[2])
+        return tot
+
+
+def _max_over_ranks(vals, dev, dist):
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def _sp_leg(args, rank, world, dev, dist):
+    """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong
+    scaling) through kernels.ema_sp -- state-only pass, NCCL send/recv state
+    chain, local pass, dA all-reduce -- and its largest error against the
+    single-GPU op on the whole sequence (normwise, max over ranks)."""
+    import torch.distributed as tdist
+    from kernels import ema_sp
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    from oracle.ema_oracle import make_dt_inputs
+    c = SP_CFG
+    own_group = not tdist.is_initialized()
+    if own_group:  # one rank: a local group so the span code runs unchanged
+        tdist.init_process_group("gloo", store=tdist.HashStore(), rank=0, world_size=1)
+    span = c["L"] // world
+    x, dt, A, dy = make_dt_inputs(c["B"], c["L"], c["H"], c["P"], seed=21)
+    fx = torch.from_numpy(x).to(torch.bfloat16).to(dev)
+    fdy = torch.from_numpy(dy).to(torch.bfloat16).to(dev)
+    fdt = torch.from_numpy(dt).to(dev)
+    A = torch.from_numpy(A).to(dev)
+    sl = slice(rank * span, (rank + 1) * span)
+    xs, dys, dts = (t[:, sl].contiguous() for t in (fx, fdy, fdt))
+
+    def step():
+        y, states, _, _ = ema_sp.sp_forward(xs, dts, A, c["Q"])
+        return (y,) + tuple(ema_sp.sp_backward(xs, dts, A, states, dys, c["Q"])[:3])
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize()
+    K = max(1, min(args.steps, 50))
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        out = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    # the single-GPU op on the whole sequence, this rank's span compared
+    yr, st, _ = ema_chunk_scan_fwd(fx, fdt, A, c["Q"])
+    dxr, ddtr, dAr, _ = ema_chunk_scan_bwd(fx, fdt, A, st, fdy, c["Q"])
+    refs = (yr[:, sl], dxr[:, sl], ddtr[:, sl], dAr)
+    errs = [float((o.float() - r.float()).abs().max() / r.float().abs().max().clamp_min(1e-30))
+            for o, r in zip(out, refs)]
+    ms, *errs = _max_over_ranks([ms] + errs, dev, dist if world > 1 else None)
+    if own_group:
+        tdist.destroy_process_group()
+    tokens = c["B"] * c["L"]
+    peak, _ = _peaks()
+    gbs = BYTES_PER_TOKEN * tokens / (ms * 1e-3) / 1e9 / world
+    return {"metric": "EMA fwd+bwd Mtokens/s, sequence parallel (config 4: B1 L65536 H32 P64 bf16)",
+            "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "ms_per_step": ms, "steps": K,
+            "scaling": "strong", "span_per_rank": span,
+            "parallelism": f"sequence parallel over {world} GPU(s): NCCL send/recv state chain + dA all-reduce"
+                           if world > 1 else "one GPU: the whole sequence, no chain",
+            "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
+            "max_rel_err_vs_single_gpu": dict(zip(("y", "dx", "ddt", "dA"), errs)),
+            "timing": "eager calls, CUDA events around K steps, max over ranks"}
+
+
+SSD5_CFG = dict(B=32, L=8192, H=80, P=64, N=128, G=1)
+SSD5_BYTES_PER_TOKEN = 10 * 80 * 64 + 12 * 1 * 128 + 12 * 80  # 53,696 B
+
+
+def _ssd5_leg(args, rank, world, dev, dist):
+    """Config 5: the Mamba-2 SSD fwd+bwd at B32 L8192 H80 P64 N128 (Mamba-2-2.7B
+    layer shape), the global batch split by rows over the ranks (strong
+    scaling), one CUDA graph per step, inputs larger than L2."""
+    import math
+    from kernels.ssd_combined import ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
+    c = SSD5_CFG
+    if c["B"] % world:
+        return {"unavailable": f"{world} ranks do not divide the batch of {c['B']}"}
+    nb = c["B"] // world
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    shp = (nb, c["L"], c["H"])
+    x = torch.randn(*shp, c["P"], generator=g, device=dev).to(bf)
+    dy = torch.randn(*shp, c["P"], generator=g, device=dev).to(bf)
+    bias = torch.log(torch.expm1(torch.exp(torch.rand(c["H"], generator=g, device=dev)
+                                           * math.log(100.0) + math.log(1e-3))))
+    dt = torch.clamp(torch.nn.functional.softplus(torch.randn(*shp, generator=g, device=dev) + bias), 1e-3, 1e-1)
+    A = -torch.exp(torch.rand(c["H"], generator=g, device=dev) * math.log(16.0))
+    Bm = (torch.randn(nb, c["L"], c["G"], c["N"], generator=g, device=dev) / math.sqrt(c["N"])).to(bf)
+    Cm = (torch.randn(nb, c["L"], c["G"], c["N"], generator=g, device=dev) / math.sqrt(c["N"])).to(bf)
+    D = torch.randn(c["H"], generator=g, device=dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        y, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+        ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
+        side.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            y, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
+            ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
+        K = max(1, min(args.steps, 10))
+        if dist is not None:
+            dist.barrier()
+        ms = _event_ms(gr.replay, K, 3, side)
+    (ms,) = _max_over_ranks([ms / K], dev, dist)
+    del gr
+    tokens = c["B"] * c["L"]
+    peak, _ = _peaks()
+    gbs = SSD5_BYTES_PER_TOKEN * tokens / (ms * 1e-3) / 1e9 / world
+    return {"metric": "SSD fwd+bwd Mtokens/s (config 5: B32 L8192 H80 P64 N128 G1 bf16)",
+            "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "ms_per_step": ms, "steps": K,
+            "scaling": "strong", "batch_per_gpu": nb,
+            "parallelism": f"batch rows split over {world} GPU(s), no collective",
+            "roofline": {"bound": "ridge (HBM figure)", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak},
+            "timing": "one CUDA graph per step (forward + backward), CUDA events, inputs > L2, max over ranks"}
+
+
+def run_ema(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist = None
@@ -422,14 +581,15 @@ def main():
 
     from kernels import _lib
     from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
-    QB = backward_chunk(Q)  # what the autograd op runs: 128-token backward tiles on half-chunk states
-
-    hx, hdt, hA, hdy = _inputs(rank, dev)
+    QB = backward_chunk(Q)
+    rows, heads = _shard(world, rank)
+    hx, hdt, hA, hdy = _inputs(0, dev)  # the global batch (same seed on every rank), then this rank's part
+    hx, hdy = hx[rows, :, heads].contiguous(), hdy[rows, :, heads].contiguous()
+    hdt, hA = hdt[rows, :, heads].contiguous(), hA[heads].contiguous()
     x, dt, A, dy = (t.to(dev) for t in (hx, hdt, hA, hdy))
-    # dt transposed to (B, H, L) by the forward launch and read by the backward,
-    # as the autograd op does (ctx saves it)
-    dtr = torch.empty(x.shape[0], H, L, dtype=torch.float32, device=dev)
+    tokens_rank = x.shape[0] * L * x.shape[2] / H  # token rows of this rank, in whole-head units
     if args.mode == "profile":
+        dtr = torch.empty(x.shape[0], x.shape[2], L, dtype=torch.float32, device=dev)
         for _ in range(max(1, args.steps)):
             y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
             ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
@@ -438,19 +598,6 @@ def main():
             dist.destroy_process_group()
         return
 
-    # eager warm-up (allocates the workspace of this stream), then two graphs
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
-        ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
-    torch.cuda.current_stream(dev).wait_stream(side)
-    torch.cuda.synchronize(dev)
-    g_fwd, g_bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_fwd, stream=side):
-        y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
-    with torch.cuda.graph(g_bwd, pool=g_fwd.pool(), stream=side):
-        dx, ddt, dA, _ = ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB, read to clean the L2
 
@@ -458,47 +605,40 @@ def main():
         flush.zero_()
         flush_rd.sum()
 
+    stream = torch.cuda.current_stream(dev)
+    sg = StepGraph(x, dt, A, dy, dev)
     clocks = ClockSampler(local_rank)
     clocks.start()
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        flush_l2()
-        g_fwd.replay()
-        g_bwd.replay()
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
     t_wall0 = time.time()
-    for k in range(K):
-        flush_l2()
-        ev[k][0].record(stream)
-        g_fwd.replay()
-        ev[k][1].record(stream)
-        g_bwd.replay()
-        ev[k][2].record(stream)
-    torch.cuda.synchronize(dev)
+    step_ms, fwd_ms, bwd_ms = sg.run(K, args.warmup, flush_l2, stream)
     t_wall1 = time.time()
-    if dist is not None:
-        dist.barrier()
     clocks.window = (t_wall0, t_wall1)
-    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
-    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
-    step_ms = sum(e[0].elapsed_time(e[2]) for e in ev)
-    tm = torch.tensor([step_ms, fwd_ms, bwd_ms], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-    step_ms, fwd_ms, bwd_ms = (float(v) for v in tm.tolist())
+    step_ms, fwd_ms, bwd_ms = _max_over_ranks([step_ms, fwd_ms, bwd_ms], dev, dist)
     clocks.stop()
     status = _lib.device_status()
+    del sg
+
+    weak = None
+    if world > 1:  # every rank a whole B8 batch of its own
+        wx, wdt, wA, wdy = (t.to(dev) for t in _inputs(rank, dev))
+        wg = StepGraph(wx, wdt, wA, wdy, dev)
+        if dist is not None:
+            dist.barrier()
+        (wms, _, _) = _max_over_ranks(wg.run(K, args.warmup, flush_l2, stream), dev, dist)
+        weak = {"value": world * TOKENS / (wms / K * 1e-3) / 1e6, "unit": "Mtokens/s",
+                "ms_per_step": wms / K, "batch_per_gpu": B, "scaling": "weak"}
+        del wg, wx, wdt, wA, wdy
 
     # ---- end to end through the public API with host buffers --------------
-    # Every step copies its inputs (x, dt, A, dy: 272 MB) from pinned host memory,
-    # runs forward + backward through the autograd op, and reads back the step's
-    # result: the loss sum(y * dy) and the parameter gradient dA.  The copy of
-    # step k+1's inputs runs on a copy stream while step k computes (two device
-    # input buffers), as a training loop's data loader would.
+    # Every step copies this rank's inputs (x, dt, A, dy) from pinned host
+    # memory, runs forward + backward through the autograd op, and reads back
+    # the step's result: the loss sum(y * dy) and the parameter gradient dA.
+    # The copy of step k+1's inputs runs on a copy stream while step k computes
+    # (two device input buffers), as a training loop's data loader would.
     from kernels.ema_chunk_scan import ema_chunk_scan_combined
     px, pdt, pA, pdy = (t.pin_memory() for t in (hx, hdt, hA, hdy))
     out_loss = torch.empty(1, dtype=torch.float32).pin_memory()
@@ -553,57 +693,117 @@ def main():
         e2e_step(k)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / E], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    e2e_ms = float(e2e_ms.item())
+    (e2e_ms,) = _max_over_ranks([e0.elapsed_time(e1) / E], dev, dist)
+    del bufs
+
+    sp = ssd5 = None
+    if not args.no_extra_legs:
+        try:
+            sp = _sp_leg(args, rank, world, dev, dist)
+        except Exception as e:  # a leg's failure is reported, the headline line still prints
+            sp = {"unavailable": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+        try:
+            ssd5 = _ssd5_leg(args, rank, world, dev, dist)
+        except Exception as e:
+            ssd5 = {"unavailable": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
 
     if rank == 0:
         peak, peak_kind = _peaks()
         ms = step_ms / K
-        value = world * TOKENS / (ms * 1e-3) / 1e6
+        value = TOKENS / (ms * 1e-3) / 1e6  # the whole global batch per step
+        toks = tokens_rank  # algorithmic bytes of one launch on one rank
         bwd_launch_s = bwd_ms / K * 1e-3
         fwd_launch_s = fwd_ms / K * 1e-3
-        bwd_gbs = BWD_BYTES_PER_TOKEN * TOKENS / bwd_launch_s / 1e9
-        fwd_gbs = FWD_BYTES_PER_TOKEN * TOKENS / fwd_launch_s / 1e9
-        step_gbs = BYTES_PER_TOKEN * TOKENS / (ms * 1e-3) / 1e9
+        bwd_gbs = BWD_BYTES_PER_TOKEN * toks / bwd_launch_s / 1e9
+        fwd_gbs = FWD_BYTES_PER_TOKEN * toks / fwd_launch_s / 1e9
+        step_gbs = BYTES_PER_TOKEN * toks / (ms * 1e-3) / 1e9
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = _cpu_baseline()
+        cfg = _ema_config(world)
+        cfg.update({"rows_per_gpu": hx.shape[0], "heads_per_gpu": hx.shape[2], "backward_chunk": QB,
+                    "timing": "one CUDA graph per step (dt transpose, forward, backward); events around each "
+                              "replay on the launching stream; events captured in the graph split forward "
+                              "and backward"})
         line = {
             "metric": METRIC, "value": value, "unit": "Mtokens/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world, "seq_len": L,
-                       "nheads": H, "headdim": P, "chunk_size": Q, "backward_chunk": QB,
-                       "parallelism": f"batch x heads sharded over {world} GPU(s), no collective",
-                       "l2": "flushed before every step outside the timed intervals: 256 MiB write, then "
-                             "256 MiB read of another buffer; step inputs 272 MB > 126 MB L2",
-                       "timing": "two CUDA graphs per step (fwd, bwd), events on the launching stream"},
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "kernel": "ema_bwd_kernel", "achieved": bwd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": bwd_gbs / peak, "traffic": _profile_traffic(),
-                         "algorithmic_bytes_per_launch": BWD_BYTES_PER_TOKEN * TOKENS,
+                         "algorithmic_bytes_per_launch": BWD_BYTES_PER_TOKEN * toks,
                          "launch_ms": bwd_launch_s * 1e3, "peak_source": f"{peak_kind} (hbm_gbs)"},
-            "kernels": {"ema_fwd_kernel": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs, "frac": fwd_gbs / peak},
+            "kernels": {"forward (dt_rows_kernel + ema_fwd_kernel)": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs,
+                                                                      "frac": fwd_gbs / peak},
                         "ema_bwd_kernel": {"ms": bwd_launch_s * 1e3, "gbs": bwd_gbs, "frac": bwd_gbs / peak}},
-            "step_roofline": {"algorithmic_bytes_per_step": BYTES_PER_TOKEN * TOKENS, "achieved_gbs": step_gbs,
+            "step_roofline": {"algorithmic_bytes_per_step_per_gpu": BYTES_PER_TOKEN * toks, "achieved_gbs": step_gbs,
                               "frac": step_gbs / peak, "peak_source": peak_kind},
-            "e2e": {"value": world * TOKENS / (e2e_ms * 1e-3) / 1e6, "unit": "Mtokens/s",
+            "e2e": {"value": TOKENS / (e2e_ms * 1e-3) / 1e6, "unit": "Mtokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": E,
-                    "api": "kernels.ema_chunk_scan.ema_chunk_scan_combined (autograd); inputs copied from "
-                           "pinned host memory every step (next step's copy overlapped with this step's "
+                    "api": "kernels.ema_chunk_scan.ema_chunk_scan_combined (autograd); each rank's inputs copied "
+                           "from pinned host memory every step (next step's copy overlapped with this step's "
                            "compute), the loss and dA read back"},
             "gpu_launches": 3 * K,  # dt_rows_kernel + ema_fwd_kernel + ema_bwd_kernel per step
             "clocks": clocks.summary(),
             "device_status": status,
         }
+        if weak is not None:
+            line["weak"] = weak
+        if sp is not None:
+            line["sp_config4"] = sp
+        if ssd5 is not None:
+            line["ssd_config5"] = ssd5
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    del g_fwd, g_bwd
     if dist is not None:
+        dist.barrier()
         dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-legs", action="store_true",
+                    help="skip the sequence-parallel config-4 and SSD config-5 legs of the line")
+    ap.add_argument("--mode", choices=["bench", "profile"], default="bench",
+                    help="profile: run --steps eager fwd+bwd steps and exit (for ncu captures)")
+    ap.add_argument("--profile-batch", type=int, default=0,
+                    help="with --mode profile --workload ssd: batch of the capture (default: the config's)")
+    ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
+                    help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
+                         "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if args.workload != "ema":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "workload": args.workload,
+                                  "unavailable": "the reference has no CPU path for this workload "
+                                                 "(SSD is the absent mamba_ssm package; SP is not in the reference)"}))
+            return
+        run_reference_arm(args, rank, world)
+        return
+    if args.workload == "ssd":
+        run_ssd(args, rank, world, local_rank)
+        return
+    if args.workload == "sp":
+        run_sp(args, rank, world, local_rank)
+        return
+
+    run_ema(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

@@ -924,8 +924,8 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
 // ---------------------------------------------------------------------------
 // Per-token table of one backward tile, built by a single warp (the
 // look-back warp, off the compute warps' path): for token t of the tile,
-// tok[tix(t)] = (a_t, a_t, w_t, w_t) and g[tix(t)] = the product of the
-// decays after t through the end of its RUN-token run (1 at the run end).
+// tok[tix(t)] = (a_t, w_t, A_h a_t, w_t a_t) and g[tix(t)] = the product of
+// the decays after t through the end of its RUN-token run (1 at the run end).
 // dt form: a_t = exp(dt_t A_h), w_t = dt_t; reference form: a_t =
 // 2^(cs_t - cs_{t-1}), w_t = 1 (ema_fwd_triton's decay between rows,
 // kernels/ema_kernels/ema_fused.py).  Tokens at or past `n` get a = 1, w = 0.
@@ -974,7 +974,7 @@ __device__ __forceinline__ void bwd_token_table(const float* raw, float Ah, int 
   if (lane % LPR == LPR - 1) after = 1.f;
 #pragma unroll
   for (int j = 0; j < TPL; ++j) {
-    tok[tix<RUN>(j0 + j)] = make_float4(a[j], a[j], w[j], w[j]);
+    tok[tix<RUN>(j0 + j)] = make_float4(a[j], w[j], Ah * a[j], w[j] * a[j]);
     g[tix<RUN>(j0 + j)] = f2_bcast(suf[j] * after);
   }
 }
@@ -1208,8 +1208,8 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         load_grp<T, NPR>(x_r + i * BP, xv);
 #pragma unroll
         for (int q = 0; q < NPR; ++q)
-          z[q] = (MODE == kBwdCumsum) ? f2_fma(make_float2(tk.x, tk.y), z[q], xv[q])
-                                      : f2_fma(make_float2(tk.x, tk.y), z[q], f2_mul(make_float2(tk.z, tk.w), xv[q]));
+          z[q] = (MODE == kBwdCumsum) ? f2_fma(f2_bcast(tk.x), z[q], xv[q])
+                                      : f2_fma(f2_bcast(tk.x), z[q], f2_mul(f2_bcast(tk.y), xv[q]));
         const int u = RUN - 1 - i;
         float2 dv[NPR];
         load_grp<T, NPR>(dy_r + u * BP, dv);
@@ -1219,7 +1219,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
           gl[u][q] = gc[q];
         }
         const float4 tu = tok_r[u];
-        an = make_float2(tu.x, tu.y);
+        an = f2_bcast(tu.x);
       }
       // an = a at the run start: the run's dy reaches the state before it as a_r0 gc
       float2 Rr[NPR];
@@ -1274,20 +1274,19 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         gend[q] = f2_fma(ds, f2_fma(hs, gn[q], rw[q]), Gexc[q]);
       }
     }
-    float2 dacc = make_float2(0.f, 0.f);  // dt form: sum over this lane's tokens of dt a G z_{t-1}
+    float dsum = 0.f;  // dt form: sum over this lane's tokens of dt a sum_p G z_{t-1}
     if (p.dx != nullptr) {  // (a state-only pass computes just the gradient at the span start)
       {
         // dx goes over this run's rows of the dy tile (dy is no longer read:
         // gl holds it), then one TMA store per warp segment (it clips the
         // rows past seqlen and the channels past headdim)
         T* const dx_s = const_cast<T*>(s_dy) + r0 * BP + ch;
-        const float2 A2 = f2_bcast(Ah);
         float pr[RUN];
 #pragma unroll
         for (int u = 0; u < RUN; ++u) {
           const float4 tk = tok_r[u];
           const float2 gr = g_r[u];
-          const float2 aa = make_float2(tk.x, tk.y), ww = make_float2(tk.z, tk.w);
+          const float2 aa = f2_bcast(tk.x), ww = f2_bcast(tk.y);
           float2 G[NPR], dxv[NPR], xv[NPR];
 #pragma unroll
           for (int q = 0; q < NPR; ++q) {
@@ -1305,16 +1304,19 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
 #pragma unroll
             for (int q = 0; q < NPR; ++q) zp[q] = f2_fma(aa, zp[q], xv[q]);
           } else {
-            // ddt_t = sum_p G_t (x_t + A a_t z_{t-1});  dA += dt_t a_t sum_p G_t z_{t-1}
-            const float2 Aa = f2_mul(A2, aa), wa = f2_mul(ww, aa);
-            float2 m = make_float2(0.f, 0.f);
+            // with S1 = sum_p G_t x_t and S2 = sum_p G_t z_{t-1} (this lane's channels):
+            // ddt_t = S1 + A a_t S2;  dA += dt_t a_t S2
+            float2 s1 = f2_mul(G[0], xv[0]), s2 = f2_mul(G[0], zp[0]);
 #pragma unroll
-            for (int q = 0; q < NPR; ++q) {
-              m = f2_fma(G[q], f2_fma(Aa, zp[q], xv[q]), m);
-              dacc = f2_fma(wa, f2_mul(G[q], zp[q]), dacc);
-              zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
+            for (int q = 1; q < NPR; ++q) {
+              s1 = f2_fma(G[q], xv[q], s1);
+              s2 = f2_fma(G[q], zp[q], s2);
             }
-            pr[u] = m.x + m.y;
+#pragma unroll
+            for (int q = 0; q < NPR; ++q) zp[q] = f2_fma(aa, zp[q], f2_mul(ww, xv[q]));
+            const float S2 = s2.x + s2.y;
+            pr[u] = fmaf(tk.z, S2, s1.x + s1.y);
+            dsum = fmaf(tk.w, S2, dsum);
           }
         }
         // the last token's extra gradient is added to the rounded dx, as the
@@ -1361,7 +1363,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     if (MODE == kBwdDt && p.dx != nullptr) {
       // per-(tile, warp) partial of dA, head-major so that the last CTA sums
       // each head's partials as one contiguous run, in a fixed order
-      float dap = dacc.x + dacc.y;
+      float dap = dsum;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(FULL, dap, o);
       if (lane == 0) ws.partial[((static_cast<size_t>(h) * p.nc + c) * p.B + b) * NW + warp] = dap;
