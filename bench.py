@@ -16,7 +16,9 @@ Extra keys on the same line: ``weak`` (every rank a whole B8 batch),
 ``sp_config4`` (config 4, one B1 L65536 sequence split over the ranks with
 the NCCL state chain, and its error against the single-GPU op) and
 ``ssd_config5`` (config 5, the Mamba-2 SSD at B32 L8192 H80 split by batch
-rows).
+rows); rank 0 adds ``bench_ema_total``, the reference's own benchmark
+(ema_combined against its d_state-1 mamba_chunk_scan_combined call) on the
+drop-ins at that benchmark's default shape.
 
 Timing: ``value`` replays the step as ONE CUDA graph (dt transpose, forward,
 backward) with inputs resident in HBM; before every step, outside the timed
@@ -571,6 +573,65 @@ def _ssd5_leg(args, rank, world, dev, dist):
             "timing": "one CUDA graph per step (forward + backward), CUDA events, inputs > L2, max over ranks"}
 
 
+TOTAL_CFG = dict(B=16, L=2048, H=32, P=64, Q=64)  # bench_ema_total.py's argparse defaults (:94-103)
+
+
+def _ema_total_leg(dev, reps=20, warm=3):
+    """The reference's own benchmark (kernels/benchmarks/bench_ema_total.py:38-91)
+    on this repository's drop-ins, at its default shape (B16 L2048 H32 P64,
+    chunk 64, bf16): ``run_combined`` = ema_combined fwd + bwd with A (B, L)
+    shared over heads; ``run_mamba`` = mamba_chunk_scan_combined fwd + bwd
+    called as it calls it (x / dt fp32, B = p, C = 1 of shape (B, L, 1, 1),
+    A = -1: d_state 1).  Each rep is the eager call sequence the reference
+    times (input clones, forward, loss, backward), CUDA events, median of reps."""
+    from kernels.backward.ema_ssd_combined import ema_combined
+    from kernels.ssd_combined import mamba_chunk_scan_combined
+    c = TOTAL_CFG
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = -torch.rand(c["B"], c["L"], generator=g, device=dev, dtype=torch.bfloat16)
+    X = torch.randn(c["B"], c["L"], c["H"], c["P"], generator=g, device=dev, dtype=torch.bfloat16)
+    dout = torch.randn(X.shape, generator=g, device=dev, dtype=torch.bfloat16)
+
+    def run_combined():
+        A_c = A.detach().clone().requires_grad_()
+        X_c = X.detach().clone().requires_grad_()
+        out = ema_combined(X_c, A_c, chunk_size=c["Q"])
+        (out * dout).sum().backward()
+
+    def run_mamba():
+        p = torch.sigmoid(torch.randn((c["B"], c["L"], 1), generator=g, dtype=torch.bfloat16, device=dev))
+        dt = -torch.log(1 - p).to(torch.float32).squeeze(-1).requires_grad_()
+        X_beta = (X.reshape(c["B"], c["L"], c["H"] * c["P"]) / dt[..., None]).requires_grad_()
+        X_m = X_beta.reshape(c["B"], c["L"], c["H"], c["P"])
+        dt_m = dt[:, :, None].expand(c["B"], c["L"], c["H"])
+        A_m = -1 * torch.ones(c["H"], dtype=torch.float32, device=dev, requires_grad=True)
+        B_m = p.to(torch.float32)[..., None]
+        C_m = torch.ones_like(B_m)
+        out_m = mamba_chunk_scan_combined(X_m, dt_m, A_m, B_m, C_m, chunk_size=c["Q"], seq_idx=None)
+        dout_m = torch.randn(out_m.shape, generator=g, dtype=out_m.dtype, device=dev)
+        (out_m * dout_m).sum().backward()
+
+    res = {}
+    for name, fn in (("ema_combined_fwd_bwd_ms", run_combined), ("mamba_chunk_scan_combined_fwd_bwd_ms", run_mamba)):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res[name] = float(np.median(ts))
+    tokens = c["B"] * c["L"]
+    return {"config": {**c, "dtype": "bf16", "source": "kernels/benchmarks/bench_ema_total.py defaults"},
+            **res, "ema_combined_mtok_s": tokens / res["ema_combined_fwd_bwd_ms"] / 1e3,
+            "mamba_chunk_scan_combined_mtok_s": tokens / res["mamba_chunk_scan_combined_fwd_bwd_ms"] / 1e3,
+            "timing": "eager calls as the reference times them (clones, forward, loss, backward), CUDA events, "
+                      f"median of {reps} after {warm} warm-up; L2 not flushed (inputs 268 MB)"}
+
+
 def run_ema(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -696,7 +757,7 @@ def run_ema(args, rank, world, local_rank):
     (e2e_ms,) = _max_over_ranks([e0.elapsed_time(e1) / E], dev, dist)
     del bufs
 
-    sp = ssd5 = None
+    sp = ssd5 = total = None
     if not args.no_extra_legs:
         try:
             sp = _sp_leg(args, rank, world, dev, dist)
@@ -708,6 +769,11 @@ def run_ema(args, rank, world, local_rank):
         except Exception as e:
             ssd5 = {"unavailable": f"{type(e).__name__}: {e}"}
         torch.cuda.empty_cache()
+        if rank == 0:
+            try:
+                total = _ema_total_leg(dev)
+            except Exception as e:
+                total = {"unavailable": f"{type(e).__name__}: {e}"}
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -755,6 +821,8 @@ def run_ema(args, rank, world, local_rank):
             line["sp_config4"] = sp
         if ssd5 is not None:
             line["ssd_config5"] = ssd5
+        if total is not None:
+            line["bench_ema_total"] = total
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -15,7 +15,17 @@ third-party and absent here).  Same argument names and layouts:
 (dt <- clamp(softplus(dt + dt_bias), *dt_limit)) and ``z`` gating after it
 (out <- y * silu(z), in fp32, stored in y's dtype), all differentiated by
 autograd.  Not supported yet: ``seq_idx`` / ``cu_seqlens`` (packed sequences).
-headdim must be 64 and dstate 128 (the benchmark shapes).
+
+Two kernel families serve the call, by d_state:
+
+* dstate 128, headdim 64, bf16 x (the Mamba-2 layer shapes of configs 3 and
+  5): the SSD kernels (tcgen05 forward and backward).
+* dstate 1 -- the reference's own benchmark call (bench_ema_total.py:62-76:
+  x / dt in fp32, B = p and C = 1 of shape (batch, seqlen, 1, 1), A = -1): the
+  state is a headdim vector, h_t = exp(dt_t A_h) h_{t-1} + dt_t B_t x_t,
+  y_t = C_t h_t + D_h x_t, i.e. the dt-form EMA of B x scaled by C.  It runs
+  on the EMA scan kernels (kernels.ema_chunk_scan) with the B and C scalings
+  as autograd ops around them; any headdim <= 128, x in fp32 / bf16 / fp16.
 """
 
 from __future__ import annotations
@@ -157,6 +167,34 @@ class SsdChunkScanFn(torch.autograd.Function):
         return (dx, ddt.to(tdt), dA.to(tA), dB.to(tB), dC.to(tC), None if dD is None else dD.to(tD), d_init, None)
 
 
+def _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size):
+    """d_state = 1: y = C * EMA_dt(B x) + D x on the EMA kernels (autograd throughout).
+
+    B and C (batch, seqlen, ngroups, 1) are per-token scalars of each head's
+    group; the products with them run in fp32 around the scan, which takes
+    B x in fp32 whatever x's dtype, so no extra rounding enters."""
+    from .ema_chunk_scan import ema_chunk_scan_combined
+    b_, L, H, P = x.shape
+    G = B.shape[2]
+    assert B.shape == (b_, L, G, 1) and C.shape == B.shape, "B and C must be (batch, seqlen, ngroups, 1)"
+    assert H % G == 0, "nheads must be a multiple of ngroups"
+    assert dt.shape == (b_, L, H) and A.shape == (H,), "dt (batch, seqlen, nheads), A (nheads,)"
+    grp = torch.arange(H, device=x.device) // (H // G)
+    Bh = B[..., 0].float()[:, :, grp]  # (b, l, H)
+    Ch = C[..., 0].float()[:, :, grp]
+    xf = x.float()  # one conversion: both gradient paths into x sum in fp32 before its single rounding
+    xb = xf * Bh[..., None]
+    q = min(max(chunk_size, 64), 256)  # the scan's tile length; the result does not depend on it
+    init = None if initial_states is None else initial_states[..., 0]
+    out = ema_chunk_scan_combined(xb, dt, A, q, initial_states=init, return_final_states=return_final_states)
+    z, fin = out if return_final_states else (out, None)
+    y = z * Ch[..., None]
+    if D is not None:
+        y = y + D.float()[None, None, :, None] * xf
+    y = y.to(x.dtype)
+    return (y, fin[..., None]) if return_final_states else y
+
+
 def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bias=None, initial_states=None,
                               seq_idx=None, cu_seqlens=None, dt_softplus=False, dt_limit=(0.0, float("inf")),
                               return_final_states=False, return_varlen_states=False):
@@ -176,7 +214,10 @@ def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bia
     dt_min, dt_max = float(dt_limit[0]), float(dt_limit[1])
     if dt_min > 0.0 or dt_max != float("inf"):
         dt = dt.clamp(dt_min, dt_max)
-    out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)
+    if B.shape[-1] == 1:
+        out = _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size)
+    else:
+        out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)
     if z is None:
         return out
     y, fin = out if return_final_states else (out, None)

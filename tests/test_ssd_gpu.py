@@ -182,3 +182,75 @@ def test_ssd_backward_mma_sync_kernel_on_strided_dx():
         for name, k in (("dx", dx), ("ddt", ddt), ("dB", dB), ("dC", dC)):
             assert_lowp_close(k, g[name], name)
     assert float(pad[..., P:].abs().max()) == 0.0  # nothing written outside the view
+
+
+def _reference_bench_call(batch, seqlen, nheads, headdim, seed, dtype):
+    """The inputs kernels/benchmarks/bench_ema_total.py:62-76 builds for its SSD
+    call: p = sigmoid(randn) per (batch, token); dt = -log(1 - p) repeated
+    over heads; X_m = X / dt (fp32 by promotion); A_m = -1; B_m = p and
+    C_m = ones of shape (batch, seqlen, 1, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(batch, seqlen, nheads, headdim, generator=g).to(dtype)
+    p = torch.sigmoid(torch.randn(batch, seqlen, 1, generator=g).to(dtype))
+    dt1 = -torch.log(1 - p).to(torch.float32).squeeze(-1)
+    Xm = (X.reshape(batch, seqlen, nheads * headdim) / dt1[..., None]).reshape(batch, seqlen, nheads, headdim)
+    dt = dt1[:, :, None].expand(batch, seqlen, nheads).contiguous()
+    A = -torch.ones(nheads)
+    Bm = p.to(torch.float32)[..., None]
+    Cm = torch.ones_like(Bm)
+    dy = torch.randn(Xm.shape, generator=g)
+    return Xm, dt, A, Bm, Cm, dy
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_reference_benchmark_call_form_dstate1(dtype):
+    """mamba_chunk_scan_combined exactly as the reference's benchmark calls it
+    (fp32 x, d_state 1, B = p, C = 1, A = -1, chunk 64) through autograd,
+    against the float64 SSD oracle: y, dx, ddt, dA and dB."""
+    from kernels.ssd_combined import mamba_chunk_scan_combined
+    Xm, dt, A, Bm, Cm, dy = _reference_bench_call(2, 512, 4, 64, seed=5, dtype=dtype)
+    assert Xm.dtype == torch.float32
+    leaves = [t.to(DEV).requires_grad_() for t in (Xm, dt, A, Bm)]
+    y = mamba_chunk_scan_combined(leaves[0], leaves[1], leaves[2], leaves[3], Cm.to(DEV), chunk_size=64,
+                                  seq_idx=None)
+    y.backward(dy.to(DEV))
+    args = [t.double().numpy() for t in (Xm, dt, A, Bm, Cm)]
+    r = so.ssd_fwd(*args)
+    g = so.ssd_bwd(*args, dy.double().numpy())
+    from _tol import assert_fp32_close
+    assert_fp32_close(y, r["y"], "y")
+    for name, t in (("dx", leaves[0]), ("ddt", leaves[1]), ("dA", leaves[2]), ("dB", leaves[3])):
+        assert_fp32_close(t.grad, g[name], name)
+
+
+def test_dstate1_groups_D_gates_and_states():
+    """d_state 1 with two groups, bf16 x, D skip, non-trivial C, an initial state
+    and the final state's gradient, z gating: every gradient against the oracle
+    (z through torch autograd on the oracle's y)."""
+    from kernels.ssd_combined import mamba_chunk_scan_combined
+    rng = np.random.default_rng(9)
+    b_, L, H, P, G = 2, 300, 4, 32, 2
+    x = torch.from_numpy(rng.standard_normal((b_, L, H, P)).astype(np.float32)).to(torch.bfloat16)
+    dt = torch.from_numpy(rng.uniform(0.01, 0.3, (b_, L, H)).astype(np.float32))
+    A = torch.from_numpy(-rng.uniform(0.5, 4.0, H).astype(np.float32))
+    Bm = torch.from_numpy(rng.standard_normal((b_, L, G, 1)).astype(np.float32))
+    Cm = torch.from_numpy(rng.standard_normal((b_, L, G, 1)).astype(np.float32))
+    D = torch.from_numpy(rng.standard_normal(H).astype(np.float32))
+    s0 = torch.from_numpy(rng.standard_normal((b_, H, P, 1)).astype(np.float32))
+    # y is bf16 like x, so the gradient reaching the scan is bf16: draw dy in bf16
+    dy = torch.from_numpy(rng.standard_normal((b_, L, H, P)).astype(np.float32)).to(torch.bfloat16).float()
+    dfin = torch.from_numpy(rng.standard_normal((b_, H, P, 1)).astype(np.float32))
+    leaves = [t.to(DEV).requires_grad_() for t in (x, dt, A, Bm, Cm, D, s0)]
+    y, fin = mamba_chunk_scan_combined(*leaves[:5], 128, D=leaves[5], initial_states=leaves[6],
+                                       return_final_states=True)
+    ((y.float() * dy.to(DEV)).sum() + (fin * dfin.to(DEV)).sum()).backward()
+    args = [t.double().numpy() for t in (x.float(), dt, A, Bm, Cm)]
+    r = so.ssd_fwd(*args, D=D.double().numpy(), initial_state=s0.double().numpy())
+    g = so.ssd_bwd(*args, dy.double().numpy(), D=D.double().numpy(), initial_state=s0.double().numpy(),
+                   d_final_state=dfin.double().numpy())
+    assert_lowp_close(y, r["y"], "y")
+    from _tol import assert_fp32_close
+    assert_fp32_close(fin, r["final_state"], "final state")
+    assert_lowp_close(leaves[0].grad, g["dx"], "dx")
+    for name, i in (("ddt", 1), ("dA", 2), ("dB", 3), ("dC", 4), ("dD", 5), ("d_initial_state", 6)):
+        assert_fp32_close(leaves[i].grad, g[name], name)
