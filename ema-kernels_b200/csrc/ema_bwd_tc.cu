@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
         named_sync(kBarEpi, NET);
       }
-      if (et == 0) reset_counters(ws, epoch, total);
+      finish_launch(ws, epoch, total, et, NET, kBarEpi);
     }
   }
   // builders and epilogue meet before the tensor memory is released

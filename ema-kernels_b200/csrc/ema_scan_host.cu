@@ -150,6 +150,7 @@ int carve_workspace(void* ws, size_t bytes, int64_t tiles, int BP, ScanWorkspace
   out->partial = reinterpret_cast<float*>(base + l.partial);
   out->agg = reinterpret_cast<uint64_t*>(base + l.agg);
   out->incl = reinterpret_cast<uint64_t*>(base + l.incl);
+  out->rec_end = reinterpret_cast<uint64_t*>(base + (bytes & ~static_cast<size_t>(7)));
   return EMA_OK;
 }
 

@@ -99,6 +99,7 @@ struct ScanWorkspace {
   float* partial;  // per-(tile, warp) dA partial sums, head-major (dt-form backward; room for 32 per tile)
   uint64_t* agg;   // [tiles][BP + 1] aggregate words (index BP: decay)
   uint64_t* incl;  // [tiles][BP] inclusive words
+  uint64_t* rec_end;  // one past the workspace's last whole word: records live in [agg, rec_end)
 };
 
 // A ring stage's tile, decoded once by the producer for the compute warps.
@@ -236,6 +237,24 @@ __device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t
   ws.hdr[kHdrDone] = 0u;
   __threadfence();
   ws.hdr[kHdrEpoch] = (epoch + 1u) & kEpochMask;
+}
+
+// End of a launch, in the last CTA only, by `nthreads` threads that share named
+// barrier `bar`: resets the counters and advances the epoch.  Tags are the
+// epoch + 1 and the epoch wraps to 0 after 2^30 launches, so a record slot
+// that no launch since rewrote (a larger shape's slot, say) could carry the
+// tag the next launch takes for current; the launch whose reset wraps the
+// epoch therefore clears every record word of the workspace first (a few
+// microseconds, once per 2^30 launches).
+__device__ __forceinline__ void finish_launch(const ScanWorkspace& ws, uint32_t epoch, int total, int tid,
+                                              int nthreads, int bar) {
+  if (((epoch + 1u) & kEpochMask) == 0u) {
+    const size_t n = static_cast<size_t>(ws.rec_end - ws.agg);
+    for (size_t i = tid; i < n; i += nthreads) ws.agg[i] = 0ull;
+    __threadfence();
+    named_sync(bar, nthreads);
+  }
+  if (tid == 0) reset_counters(ws, epoch, total);
 }
 
 // Producer-side end of stream: mark the stage as "no more tiles" with the
@@ -916,7 +935,11 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
       }
     }
   }
-  if (tid == 0 && count_cta_done(ws)) reset_counters(ws, epoch, total);
+  __shared__ uint32_t s_last;
+  named_sync(1, NC);  // every compute thread is past its last store
+  if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
+  named_sync(1, NC);
+  if (s_last) finish_launch(ws, epoch, total, tid, NC, 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -1400,7 +1423,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       }
       named_sync(1, NC);
     }
-    if (tid == 0) reset_counters(ws, epoch, total);
+    finish_launch(ws, epoch, total, tid, NC, 1);
   }
 }
 

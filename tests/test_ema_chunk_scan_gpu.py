@@ -117,6 +117,102 @@ def test_config4_bf16_full_size_one_gpu():
     assert_lowp_close(dA, g["dA"], "dA")
 
 
+def _abi_fwd(x, dt, A, Q, ws, y, states):
+    """ema_fwd_launch through the C ABI (strided dt, no dt_rows) on a caller workspace."""
+    import ctypes
+
+    from kernels import _lib
+    B, L, H, P = x.shape
+    a = _lib.EmaFwdArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim, a.chunk_size = B, L, H, P, Q
+    a.dtype = _lib.DTYPE_CODES[x.dtype]
+    a.x, a.x_stride = x.data_ptr(), _lib.strides3(x)
+    a.out, a.out_stride = y.data_ptr(), _lib.strides3(y)
+    a.dt, a.A = dt.data_ptr(), A.data_ptr()
+    a.states, a.states_stride = states.data_ptr(), (_lib._i64 * 4)(*states.stride())
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(_lib.lib.ema_fwd_launch(ctypes.byref(a), _lib.stream_ptr(x.device)), "ema_fwd_launch")
+
+
+def _abi_bwd(x, dt, A, states, dy, Q, ws, dx, ddt, dA):
+    import ctypes
+
+    from kernels import _lib
+    B, L, H, P = x.shape
+    b = _lib.EmaBwdArgs()
+    b.batch, b.seqlen, b.nheads, b.headdim, b.chunk_size = B, L, H, P, Q
+    b.dtype = _lib.DTYPE_CODES[x.dtype]
+    b.x, b.x_stride = x.data_ptr(), _lib.strides3(x)
+    b.dout, b.dout_stride = dy.data_ptr(), _lib.strides3(dy)
+    b.dx, b.dx_stride = dx.data_ptr(), _lib.strides3(dx)
+    b.dt, b.A = dt.data_ptr(), A.data_ptr()
+    b.states, b.states_stride = states.data_ptr(), (_lib._i64 * 4)(*states.stride())
+    b.ddt, b.dA_out = ddt.data_ptr(), dA.data_ptr()
+    b.workspace, b.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(_lib.lib.ema_bwd_launch(ctypes.byref(b), _lib.stream_ptr(x.device)), "ema_bwd_launch")
+
+
+def test_epoch_wrap_clears_stale_records():
+    """Look-back records are tagged with the launch epoch + 1, and the epoch wraps
+    to 0 after 2^30 launches.  A workspace is set up as it could be found then:
+    epoch 2^30 - 1 and every record word holding a stale value under tag 1, the
+    tag of the first launch after the wrap.  A small launch (which wraps the
+    epoch) and then a larger one, which reads slots the small one never wrote,
+    must both match the same launches on a fresh workspace, forward and
+    backward; the status word stays clear."""
+    from kernels import _lib
+    Q = 256
+    small = _inputs(1, 512, 2, 64, 31, torch.bfloat16)
+    big = _inputs(2, 2048, 8, 64, 32, torch.bfloat16)
+    need = _lib.lib.ema_scan_workspace_size(2, 2048, 8, 64, Q)
+
+    def stale_workspace():
+        ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+        words = ws[256:].view(torch.int64)
+        stale = (1 << 32) | int(np.array(1e30, dtype=np.float32).view(np.uint32))
+        words.fill_(stale)
+        ws[:4].view(torch.int32).fill_(0x3FFFFFFF)
+        return ws
+
+    def run(case, ws):
+        x, dt, A, dy = (t.to(DEV) for t in case)
+        B, L, H, P = x.shape
+        nc = -(-L // Q)
+        y = torch.empty_like(x)
+        st = torch.empty(B, nc, H, P, dtype=torch.float32, device=DEV)
+        _abi_fwd(x, dt, A, Q, ws, y, st)
+        dx = torch.empty_like(x)
+        ddt = torch.empty(B, L, H, dtype=torch.float32, device=DEV)
+        dA = torch.empty(H, dtype=torch.float32, device=DEV)
+        return y, st, dx, ddt, dA, (x, dt, A, dy)
+
+    def run_bwd(out, ws):
+        y, st, dx, ddt, dA, (x, dt, A, dy) = out
+        _abi_bwd(x, dt, A, st, dy, Q, ws, dx, ddt, dA)
+        return y, dx, ddt, dA
+
+    fresh = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    ref = run_bwd(run(big, fresh), fresh)
+    # forward: the small launch wraps the epoch, the big one runs at tag 1
+    ws = stale_workspace()
+    fs = run(small, ws)
+    fb = run(big, ws)
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 1, "two launches after 2^30 - 1 leave epoch 1"
+    # backward, the same way
+    ws2 = stale_workspace()
+    run_bwd(fs, ws2)
+    got = run_bwd(fb, ws2)
+    torch.cuda.synchronize()
+    for w in (ws, ws2):
+        assert int(w[12:16].view(torch.int32).item()) == 0, "device status word set"
+    close = dict(rtol=1e-2, atol=1e-3)
+    torch.testing.assert_close(got[0], ref[0], **close)
+    torch.testing.assert_close(got[1], ref[1], **close)
+    torch.testing.assert_close(got[2], ref[2], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(got[3], ref[3], rtol=1e-4, atol=1e-4)
+
+
 @pytest.mark.parametrize("L", [1000, 999])
 def test_dt_rows_and_strided_dt_agree(L):
     """The launchers read each tile's dt either as one row of the (B, H, L) copy
