@@ -22,6 +22,9 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "kernels", "libema_ssd_b200.so")
+# test-only library (tcgen05 operand self-test), kept out of the product library
+SELFTEST_SRC = os.path.join(ROOT, "tests", "native", "tc_selftest.cu")
+SELFTEST_LIB = os.path.join(ROOT, "tests", "native", "libema_selftest_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -73,7 +76,21 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_selftest(force)
     return LIB
+
+
+def build_selftest(force: bool = False) -> str:
+    """tests/native/libema_selftest_b200.so: the tcgen05 operand self-test the GPU
+    tests run (not part of the product library)."""
+    deps = _deps() + [SELFTEST_SRC, os.path.join(os.path.dirname(SELFTEST_SRC), "ema_selftest_b200.h")]
+    if force or _stale(SELFTEST_LIB, deps):
+        cmd = [_nvcc(), *ARCH, *CFLAGS, "-I", os.path.dirname(SELFTEST_SRC), "-shared", "-o", SELFTEST_LIB,
+               SELFTEST_SRC, "-lcuda"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {SELFTEST_SRC}:\n{r.stdout}\n{r.stderr}")
+    return SELFTEST_LIB
 
 
 if __name__ == "__main__":

@@ -127,8 +127,6 @@ lib.ssd_bwd_launch.restype = ctypes.c_int
 lib.ssd_bwd_launch.argtypes = [ctypes.POINTER(SsdBwdArgs), _ptr]
 lib.ssd_device_status.restype = ctypes.c_int
 lib.ssd_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _ptr]
-lib.tc_selftest_gemm.restype = ctypes.c_int
-lib.tc_selftest_gemm.argtypes = [ctypes.c_int, _ptr, _ptr, _ptr, _ptr, _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p
 lib.ema_version.restype = ctypes.c_char_p
 

@@ -76,8 +76,11 @@ def _np(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMA_REFERENCE_DIR"),
+                    help="root of a checkout of the reference repository (or set EMA_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or EMA_REFERENCE_DIR: the reference checkout to generate fixtures from")
     os.environ["TRITON_INTERPRET"] = "1"
     tmp = _stage_reference(args.reference)
     sys.path.insert(0, tmp)

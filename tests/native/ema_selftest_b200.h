@@ -1,10 +1,10 @@
 /*
- * ema_selftest_b200.h -- internal self-test entry points of libema_ssd_b200.so.
+ * ema_selftest_b200.h -- test-only library libema_selftest_b200.so.
  *
- * Not part of the reference interface: these check, on the GPU, the tcgen05
- * operand conventions (128-byte-swizzled shared-memory tiles, K-major and
- * MN-major descriptors, tensor-memory accumulators) that the SSD kernels are
- * built on.  Used by the GPU test suite.
+ * Not part of the product or of the reference interface: these check, on the
+ * GPU, the tcgen05 operand conventions (128-byte-swizzled shared-memory tiles,
+ * K-major and MN-major descriptors, tensor-memory accumulators) that the SSD
+ * kernels are built on.  Used by the GPU test suite only.
  */
 #ifndef EMA_SELFTEST_B200_H_
 #define EMA_SELFTEST_B200_H_
@@ -22,6 +22,8 @@ extern "C" {
  *   mode 2: d (128x128) = a (128x128)^T * b (128x128)
  *   mode 3: as mode 0, with `a` staged into shared memory by the threads. */
 EMA_API int tc_selftest_gemm(int mode, const void* a, const void* b, float* d, uint32_t* status, void* stream);
+/* Detail of the last error returned on the calling thread. */
+EMA_API const char* tc_selftest_last_error(void);
 
 #ifdef __cplusplus
 }

@@ -11,18 +11,60 @@
 //   mode 4: an M = 64 MMA, D[64x64] = A B^T (A, B 64 x 128, K-major), written
 //           into zeroed tensor memory; all 128 lanes x 64 columns are read
 //           back, which shows where the 64 rows of D live
+//
+// Test infrastructure: built by ema-kernels_b200/build.py into
+// tests/native/libema_selftest_b200.so, apart from the product library, and
+// loaded only by tests/test_tcgen05_gpu.py.
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
-#include "ema_scan_dispatch.h"
+#include <string>
+
+#include "ema_common.cuh"
 #include "ema_selftest_b200.h"
 #include "tc_common.cuh"
 
 namespace emab {
-void set_last_error(const char* msg);
-
 namespace {
+
+thread_local std::string g_error;
+
+void set_last_error(const char* msg) { g_error = msg; }
+
+// Tiled 2-D bf16 tensor map with 128-byte swizzle (this library's own copy of
+// the product library's encoder).
+int encode_map(CUtensorMap* m, const void* ptr, const uint64_t* dims, const uint64_t* stride_bytes,
+               const uint32_t* box) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  if (enc == nullptr) {
+    set_last_error("cuTensorMapEncodeTiled is not available from the driver");
+    return EMA_ERR_CUDA;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) {  // bind the context
+    set_last_error("no current device");
+    return EMA_ERR_CUDA;
+  }
+  cuuint64_t d[2] = {dims[0], dims[1]};
+  cuuint64_t st[1] = {stride_bytes[0]};
+  cuuint32_t b[2] = {box[0], box[1]}, e[2] = {1u, 1u};
+  if (enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed");
+    return EMA_ERR_CUDA;
+  }
+  return EMA_OK;
+}
 
 constexpr int kRegion = 128 * 128;  // one 128-row x 64-column bf16 region, bytes
 
@@ -126,8 +168,6 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
-unsigned long long g_smem_mask = 0;
-
 }  // namespace
 }  // namespace emab
 
@@ -143,25 +183,27 @@ extern "C" EMA_API int tc_selftest_gemm(int mode, const void* a, const void* b, 
   const uint64_t dims128[2] = {128, 128};
   const uint64_t st256[1] = {256};
   const uint32_t box[2] = {64, 128};
-  int r = encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, dims128, st256, box, true);
+  int r = encode_map(&ma, a, dims128, st256, box);
   if (r) return r;
   if (mode == 4) {
     const uint64_t d64[2] = {128, 64};
     const uint32_t box64[2] = {64, 64};
-    r = encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, d64, st256, box64, true);
+    r = encode_map(&ma, a, d64, st256, box64);
     if (r) return r;
-    r = encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, d64, st256, box64, true);
+    r = encode_map(&mb, b, d64, st256, box64);
   } else if (mode == 1) {
     const uint64_t dims64[2] = {64, 128};
     const uint64_t st128[1] = {128};
-    r = encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, dims64, st128, box, true);
+    r = encode_map(&mb, b, dims64, st128, box);
   } else {
-    r = encode_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, dims128, st256, box, true);
+    r = encode_map(&mb, b, dims128, st256, box);
   }
   if (r) return r;
   const int smem = 4 * 128 * 128 + 1024;
-  r = ensure_smem_attr(reinterpret_cast<const void*>(tc_selftest_kernel), smem, &g_smem_mask);
-  if (r) return EMA_ERR_CUDA;
+  if (cudaFuncSetAttribute(tc_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    set_last_error("cudaFuncSetAttribute failed");
+    return EMA_ERR_CUDA;
+  }
   tc_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(
       ma, mb, mode, static_cast<const __nv_bfloat16*>(a), d, status);
   const cudaError_t e = cudaGetLastError();
@@ -171,3 +213,5 @@ extern "C" EMA_API int tc_selftest_gemm(int mode, const void* a, const void* b, 
   }
   return EMA_OK;
 }
+
+extern "C" EMA_API const char* tc_selftest_last_error(void) { return g_error.c_str(); }

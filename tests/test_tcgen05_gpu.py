@@ -4,18 +4,34 @@ K-major and MN-major MMA operands, a thread-written swizzled tile, fp32
 accumulation in tensor memory.  Each mode is one 128-row bf16 GEMM compared
 with a float64 product of the same bf16 inputs."""
 
+import ctypes
+import os
+
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
+# test-only library built by ema-kernels_b200/build.py next to its source
+_SELFTEST = os.path.join(os.path.dirname(os.path.abspath(__file__)), "native", "libema_selftest_b200.so")
+
+
+def _selftest_lib():
+    lib = ctypes.CDLL(_SELFTEST)
+    lib.tc_selftest_gemm.restype = ctypes.c_int
+    lib.tc_selftest_gemm.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 5
+    lib.tc_selftest_last_error.restype = ctypes.c_char_p
+    return lib
+
 
 def _run(mode, a, b, n):
     from kernels import _lib
+    st = _selftest_lib()
     d = torch.full((128, n), float("nan"), device="cuda", dtype=torch.float32)
     status = torch.zeros(1, device="cuda", dtype=torch.int32)
-    _lib.check(_lib.lib.tc_selftest_gemm(mode, a.data_ptr(), b.data_ptr(), d.data_ptr(), status.data_ptr(),
-                                         _lib.stream_ptr(a.device)), "tc_selftest_gemm")
+    rc = st.tc_selftest_gemm(mode, a.data_ptr(), b.data_ptr(), d.data_ptr(), status.data_ptr(),
+                             _lib.stream_ptr(a.device))
+    assert rc == 0, st.tc_selftest_last_error().decode()
     torch.cuda.synchronize()
     assert int(status.item()) == 0, "device-side wait timed out"
     return d
