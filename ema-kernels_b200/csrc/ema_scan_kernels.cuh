@@ -213,7 +213,7 @@ __device__ __forceinline__ bool lookback_warp(const ScanWorkspace& ws, uint32_t 
         return false;
       }
       __nanosleep(backoff);
-      backoff = backoff < 2048 ? backoff * 2 : 2048;
+      backoff = backoff < 128 ? backoff * 2 : 128;
     }
   }
   return true;
@@ -1119,13 +1119,16 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
                          : rows ? p.dt + static_cast<size_t>(bh) * p.L + t0
                                 : p.dt + (static_cast<size_t>(b) * p.L + t0) * p.H + h;
       const uint32_t bulk = rows ? row_bulk_bytes(src, n) : 0u;
+      // a state-only pass (no dx) needs only the reverse chain: dy and the decays,
+      // not x or the chunk start state (pass 1 then scans stale x; nothing uses it)
+      const bool full_pass = p.dx != nullptr;
       const float* srow = p.states + b * p.st_b + static_cast<long long>(c) * p.st_c + h * p.st_h;
-      const uint32_t sbulk = (p.st_p == 1) ? row_bulk_bytes(srow, p.P) : 0u;
+      const uint32_t sbulk = (full_pass && p.st_p == 1) ? row_bulk_bytes(srow, p.P) : 0u;
       if (lane == 0) {
         s_tile[s] = c * BH + bh;
         s_info[s] = TileInfo{c, b, h, t0, bh, 0, b * p.sdx_b + static_cast<long long>(t0) * p.sdx_l + h * p.sdx_h};
-        mbar_arrive_expect_tx(&full[s], 2 * C::kX + bulk + sbulk);
-        tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
+        mbar_arrive_expect_tx(&full[s], (full_pass ? 2 : 1) * C::kX + bulk + sbulk);
+        if (full_pass) tma_load_4d(st, &tm_x, &full[s], 0, h, t0, b);
         tma_load_4d(st + C::kX, &tm_dy, &full[s], 0, h, t0, b);
       }
       if (rows) {
@@ -1136,14 +1139,14 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       if (MODE == kBwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
       if (sbulk) {
         if (lane == 0) bulk_g2s(sst, srow, sbulk, &full[s]);
-      } else {
+      } else if (full_pass) {
         for (int i = lane; i < p.P; i += 32) cp_async_4(sst + i, srow + static_cast<long long>(i) * p.st_p);
       }
     }, [&](int ticket) {
       const int cr = fast_div(ticket, p.div_bh), bh = ticket - cr * BH;
       const int c = p.nc - 1 - cr;
       const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
-      tma_prefetch_l2_4d(&tm_x, 0, h, t0, b);
+      if (p.dx != nullptr) tma_prefetch_l2_4d(&tm_x, 0, h, t0, b);
       tma_prefetch_l2_4d(&tm_dy, 0, h, t0, b);
     });
     return;

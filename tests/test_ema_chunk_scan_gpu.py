@@ -490,3 +490,45 @@ def test_half_chunk_states_feed_the_half_chunk_backward(P, L):
     (yy * dy).sum().backward()
     g0 = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy())
     assert_fp32_close(xg.grad, g0["dx"], "autograd dx")
+
+
+@pytest.mark.parametrize("Q", [128, 256])
+def test_few_long_chains_match_oracle(Q):
+    """Two (batch, head) sequences of 16-32 tiles each (every tile's look-back
+    walks a chain with many tiles in flight): forward with an initial state,
+    backward with a final-state gradient, both state-only passes (the backward
+    one reads no x) and the autograd pair, all in fp32 against the float64
+    oracle."""
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    B, L, H, P = 1, 4096, 2, 64
+    tx, tdt, tA, tdy = _inputs(B, L, H, P, 40 + Q, torch.float32, dt_range=(1e-3, 0.2))
+    rng = np.random.default_rng(5)
+    init = rng.standard_normal((B, H, P)).astype(np.float32)
+    dfin = rng.standard_normal((B, H, P)).astype(np.float32)
+    x, dt, A, dy = (t.to(DEV) for t in (tx, tdt, tA, tdy))
+    ti, tf = torch.from_numpy(init).to(DEV), torch.from_numpy(dfin).to(DEV)
+    y, st, fin = ema_chunk_scan_fwd(x, dt, A, Q, initial_states=ti, return_final_states=True)
+    _, _, fin_only = ema_chunk_scan_fwd(x, dt, A, Q, initial_states=ti, state_only=True)
+    dx, ddt, dA, dinit = ema_chunk_scan_bwd(x, dt, A, st, dy, Q, d_final_states=tf, need_d_initial=True)
+    _, _, _, dinit_only = ema_chunk_scan_bwd(x, dt, A, st, dy, Q, d_final_states=tf, state_only=True)
+    r = eo.ema_dt_fwd(tx.numpy(), tdt.numpy(), tA.numpy(), initial_state=init)
+    g = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy(), initial_state=init, d_final_state=dfin)
+    assert_fp32_close(y, r["y"], "y")
+    assert_fp32_close(fin, r["final_state"], "final")
+    assert_fp32_close(fin_only, r["final_state"], "final (state-only)")
+    assert_fp32_close(st[:, 1:], r["y"][:, Q - 1::Q][:, :st.shape[1] - 1], "chunk start states")
+    assert_fp32_close(dx, g["dx"], "dx")
+    assert_fp32_close(ddt, g["ddt"], "ddt")
+    assert_fp32_close(dA, g["dA"], "dA")
+    assert_fp32_close(dinit, g["d_initial_state"], "d_initial")
+    assert_fp32_close(dinit_only, g["d_initial_state"], "d_initial (state-only)")
+    # the autograd pair: a 256-token forward with half-chunk states and the 128-token backward
+    if Q == 256:
+        from kernels.ema_chunk_scan import ema_chunk_scan_combined
+        xg, dtg, Ag = (t.clone().requires_grad_() for t in (x, dt, A))
+        yg = ema_chunk_scan_combined(xg, dtg, Ag, 256)
+        yg.backward(dy)
+        g0 = eo.ema_dt_bwd(tx.numpy(), tdt.numpy(), tA.numpy(), tdy.numpy())
+        assert_fp32_close(xg.grad, g0["dx"], "autograd dx")
+        assert_fp32_close(dtg.grad, g0["ddt"], "autograd ddt")
+        assert_fp32_close(Ag.grad, g0["dA"], "autograd dA")
