@@ -96,7 +96,7 @@ inline FastDiv make_fast_div(uint32_t d) {
 
 struct ScanWorkspace {
   uint32_t* hdr;   // kHdrWords header words
-  float* partial;  // per-(tile, warp) dA partial sums, head-major (dt-form backward; room for 32 per tile)
+  float* partial;  // dA partial sums, head-major: one per tile (dt-form backward), 4 per tile (tensor-core backward); room for 32
   uint64_t* agg;   // [tiles][BP + 1] aggregate words (index BP: decay)
   uint64_t* incl;  // [tiles][BP] inclusive words
   uint64_t* rec_end;  // one past the workspace's last whole word: records live in [agg, rec_end)
@@ -1002,6 +1002,58 @@ __device__ __forceinline__ void bwd_token_table(const float* raw, float Ah, int 
   }
 }
 
+// dA[h] = the sum of the n per-tile partials of head h (`part`, head-major,
+// contiguous), by the NT threads of the last CTA.  Each head gets G
+// consecutive lanes (the largest power of two <= 32 with G * H <= NT, else 1);
+// lane g of a head sums elements g, g + G, ... in that order with 16 loads in
+// flight (float4 loads when the head's run is 16-byte aligned), and the G lanes
+// combine in a fixed shuffle tree: the result does not depend on timing, and
+// the whole tail costs one or two L2 round trips instead of one per head.
+template <int NT>
+__device__ __forceinline__ void sum_head_partials(const float* part, int H, int n, float* out, int tid) {
+  static_assert(NT % 32 == 0, "whole warps");
+  const unsigned FULL = 0xffffffffu;
+  int G = 32;
+  while (G > 1 && G * H > NT) G >>= 1;
+  const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(part) & 15u) == 0;
+  for (int base = 0; base < H * G; base += NT) {  // warp-uniform trip count
+    const int slot = base + tid;
+    const int hh = slot / G, g = slot % G;
+    float acc = 0.f;
+    if (slot < H * G) {
+      const float* src = part + static_cast<size_t>(hh) * n;
+      if (vec) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        const int nq = n >> 2;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = g; j < nq; j += 16 * G) {
+          float4 v[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) v[u] = (j + u * G < nq) ? __ldcg(s4 + j + u * G) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            a.x += v[u].x;
+            a.y += v[u].y;
+            a.z += v[u].z;
+            a.w += v[u].w;
+          }
+        }
+        acc = (a.x + a.y) + (a.z + a.w);
+      } else {
+        for (int j = g; j < n; j += 16 * G) {
+          float v[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) v[u] = (j + u * G < n) ? __ldcg(src + j + u * G) : 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) acc += v[u];
+        }
+      }
+    }
+    for (int o = G >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+    if (slot < H * G && g == 0) out[hh] = acc;
+  }
+}
+
 // Tokens per compute-warp segment of the backward at block headdim BP: the
 // height of the box the host's dx tensor map stores per warp.
 constexpr int bwd_segment_tokens(int BP) { return BP == 64 ? 32 : 16; }
@@ -1075,6 +1127,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   uint64_t* vec_empty = vec_full + 2;
   uint64_t* tok_full = vec_empty + 2;
   __shared__ uint32_t s_epoch, s_last, s_fail;
+  __shared__ float s_dap[2][NW];  // dt form: each compute warp's dA partial of tile k, slot k % 2
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const ScanWorkspace& ws = p.ws;
@@ -1192,9 +1245,27 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   const int ch = cg * CPL;
   const int nch = min(CPL, p.P - ch);
   const unsigned FULL = 0xffffffffu;
+  // stage whose dx store (issued at the end of the previous tile) may still be
+  // reading it: released once this tile's first pass is done, so the store's
+  // read of shared memory overlaps that pass instead of stalling the warp.  A
+  // one-stage ring cannot defer (the next tile's data needs that stage).
+  constexpr bool kDefer = S >= 2;
+  int pend = -1;
+  // dt form: the previous tile's dA partial slot, written by thread 0 once the
+  // block barrier below has seen every warp's share (the sum over warps is
+  // taken in warp order, so it does not depend on timing)
+  size_t pslot = ~size_t{0};
   for (int k = 0;; ++k) {
     const int s = k % S;
     if (!compute_wait(&full[s], (k / S) & 1, status, warp, NC, &s_fail)) break;
+    if (MODE == kBwdDt && tid == 0 && pslot != ~size_t{0}) {
+      const float* d = s_dap[(k - 1) & 1];
+      float t = d[0];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) t += d[w];
+      ws.partial[pslot] = t;
+      pslot = ~size_t{0};
+    }
     const int tile = s_tile[s];
     if (tile < 0) break;
     const TileInfo ti = s_info[s];
@@ -1263,6 +1334,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       if (ts == 0) st_row<NPR>(s_R + warp * (BP + kRowPad) + ch, Rinc);
     }
     named_sync(1, NC);  // every segment's aggregates
+    if (pend >= 0 && lane == 0) {
+      bulk_wait_read<0>();
+      mbar_arrive(&empty[pend]);
+    }
+    pend = -1;
 
     // ---- chain segments: Zin (forward, true states) and Rloc (reverse); publish
     const bool has_succ = (c > 0);  // the reverse chain continues towards chunk 0
@@ -1308,19 +1384,32 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
         // rows past seqlen and the channels past headdim)
         T* const dx_s = const_cast<T*>(s_dy) + r0 * BP + ch;
         float pr[RUN];
+        // token u + 1's shared-memory operands are read before token u's dx is
+        // stored: the store may alias them as far as the compiler knows, so
+        // loads written after it would wait for it, one latency per token
+        float4 tk_n = tok_r[0];
+        float2 gr_n = g_r[0];
+        float2 xv_n[NPR];
+        load_grp<T, NPR>(x_r, xv_n);
 #pragma unroll
         for (int u = 0; u < RUN; ++u) {
-          const float4 tk = tok_r[u];
-          const float2 gr = g_r[u];
-          const float2 aa = f2_bcast(tk.x), ww = f2_bcast(tk.y);
+          const float4 tk = tk_n;
+          const float2 gr = gr_n;
           float2 G[NPR], dxv[NPR], xv[NPR];
+#pragma unroll
+          for (int q = 0; q < NPR; ++q) xv[q] = xv_n[q];
+          if (u + 1 < RUN) {
+            tk_n = tok_r[u + 1];
+            gr_n = g_r[u + 1];
+            load_grp<T, NPR>(x_r + (u + 1) * BP, xv_n);
+          }
+          const float2 aa = f2_bcast(tk.x), ww = f2_bcast(tk.y);
 #pragma unroll
           for (int q = 0; q < NPR; ++q) {
             G[q] = f2_fma(gr, gend[q], gl[u][q]);
             dxv[q] = (MODE == kBwdCumsum) ? G[q] : f2_mul(ww, G[q]);
           }
           store_grp<T, NPR>(dx_s + u * BP, dxv);
-          load_grp<T, NPR>(x_r + u * BP, xv);
           if (MODE == kBwdCumsum) {
             // dl_t = a_t sum_p G_t z_{t-1}
             float2 m = f2_mul(G[0], zp[0]);
@@ -1381,49 +1470,37 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       if (p.dx != nullptr) {
         tma_store_4d(&tm_dx, s_dy + s0 * BP, 0, h, t0 + s0, b);
         bulk_commit();
-        bulk_wait_read<0>();  // the stage may be refilled once the store has read it
       }
-      mbar_arrive(&empty[s]);         // this warp no longer reads the stage
-      mbar_arrive(&vec_empty[k & 1]);  // nor slot k % 2 (arriving gradient, token table)
+      mbar_arrive(&vec_empty[k & 1]);  // this warp no longer reads slot k % 2 (arriving gradient, token table)
+    }
+    // the stage is released once the dx store has read it (next tile, or below)
+    if (kDefer && p.dx != nullptr) {
+      pend = s;
+    } else if (lane == 0) {
+      if (p.dx != nullptr) bulk_wait_read<0>();
+      mbar_arrive(&empty[s]);
     }
     if (MODE == kBwdDt && p.dx != nullptr) {
-      // per-(tile, warp) partial of dA, head-major so that the last CTA sums
-      // each head's partials as one contiguous run, in a fixed order
+      // this tile's dA partial: per warp here, summed over the warps by thread
+      // 0 at the next tile's first barrier into slot (h, c, b) -- head-major,
+      // so that the last CTA reads each head's partials as one contiguous run
       float dap = dsum;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dap += __shfl_xor_sync(FULL, dap, o);
-      if (lane == 0) ws.partial[((static_cast<size_t>(h) * p.nc + c) * p.B + b) * NW + warp] = dap;
+      if (lane == 0) s_dap[k & 1][warp] = dap;
+      if (tid == 0) pslot = (static_cast<size_t>(h) * p.nc + c) * p.B + b;
     }
   }
   if (lane == 0 && p.dx != nullptr) bulk_wait_all();  // this warp's dx stores have landed
+  if (pend >= 0 && lane == 0) mbar_arrive(&empty[pend]);
   named_sync(1, NC);
   if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
   named_sync(1, NC);
   if (s_last) {
     if (MODE == kBwdDt && p.dx != nullptr) {
-      // dA[h] = sum of head h's nc * B * NW partials (contiguous): warp per
-      // head, a fixed split over lanes and a fixed shuffle tree, so the sum is
-      // deterministic.  Loads are issued eight at a time before any is used:
-      // the tail costs a few L2 round trips, not one per partial.
+      // dA[h] = sum of head h's nc * B per-tile partials
       __threadfence();
-      const int n2 = p.nc * p.B * NW / 2;
-      for (int hh = warp; hh < p.H; hh += NW) {
-        const float2* part = reinterpret_cast<const float2*>(ws.partial + static_cast<size_t>(hh) * p.nc * p.B * NW);
-        float2 acc = make_float2(0.f, 0.f);
-        int i = lane;
-        for (; i + 7 * 32 < n2; i += 8 * 32) {
-          float2 v[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = __ldcg(part + i + u * 32);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) acc = f2_add(acc, v[u]);
-        }
-        for (; i < n2; i += 32) acc = f2_add(acc, __ldcg(part + i));
-        float a = acc.x + acc.y;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(FULL, a, o);
-        if (lane == 0) p.dA_out[hh] = a;
-      }
+      sum_head_partials<NC>(ws.partial, p.H, p.nc * p.B, p.dA_out, tid);
       named_sync(1, NC);
     }
     finish_launch(ws, epoch, total, tid, NC, 1);
