@@ -44,6 +44,16 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
   return t;
 }
 
+// Programmatic dependent launch.  The scan kernels are launched with
+// programmatic stream serialisation, so a kernel's CTAs may start while the
+// previous kernel on the stream is still finishing.  grid_dep_wait() blocks
+// until that kernel has completed and its writes are visible: nothing before
+// it may read global memory that an earlier kernel writes (inputs, outputs,
+// the shared look-back workspace).  grid_dep_release() lets the next kernel's
+// CTAs be scheduled as SMs free up.  Both are no-ops for a plain launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

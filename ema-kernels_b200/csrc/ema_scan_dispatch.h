@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include "ema_scan_kernels.cuh"
 
 namespace emab {
@@ -55,6 +57,26 @@ constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
 
 // Set the dynamic shared-memory opt-in of `fn` once per device.
 int ensure_smem_attr(const void* fn, int bytes, unsigned long long* device_mask);
+
+// Launch with programmatic stream serialisation: the kernel's CTAs may be
+// scheduled while the previous kernel on the stream is still finishing, and
+// run their prologue up to grid_dep_wait() (ema_common.cuh) meanwhile -- the
+// launch latency and the prologue overlap the previous kernel's tail.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_programmatic(void (*fn)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                       Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, std::forward<Args>(args)...);
+}
 // Tiled tensor map of `rank` dims (dims[0] innermost), byte strides of dims
 // 1..rank-1, box extents; 128-byte swizzle or none.  EMA_OK or an error code
 // with the message set.

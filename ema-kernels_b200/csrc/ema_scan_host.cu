@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(256) dt_rows_kernel(const float* __restrict__ 
   const int b = blockIdx.z, t0 = blockIdx.x * 32, h0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const float* src = dt + static_cast<size_t>(b) * L * H;
+  grid_dep_wait();
 #pragma unroll
   for (int r = ty; r < 32; r += 8) {
     const int t = t0 + r, h = h0 + tx;
@@ -209,6 +210,7 @@ __global__ void __launch_bounds__(256) dt_rows_kernel(const float* __restrict__ 
     const int h = h0 + r, t = t0 + tx;
     if (t < L && h < H) dst[static_cast<size_t>(h) * L + t] = tile[tx][r];
   }
+  grid_dep_release();
 }
 
 // dt (B, L, H) -> (B, H, L): one contiguous row per (batch, head), so each
@@ -219,8 +221,9 @@ int launch_dt_rows(const float* dt, float* rows, int64_t B, int64_t L, int64_t H
   if (B > 65535 || (H + 31) / 32 > 65535)
     return fail(EMA_ERR_UNSUPPORTED, "dt_rows: batch or nheads too large for the transpose grid");
   dim3 grid(static_cast<unsigned>((L + 31) / 32), static_cast<unsigned>((H + 31) / 32), static_cast<unsigned>(B));
-  dt_rows_kernel<<<grid, 256, 0, s>>>(dt, rows, static_cast<int>(L), static_cast<int>(H));
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_programmatic(dt_rows_kernel, grid, dim3(256), 0, s, dt, rows, static_cast<int>(L),
+                                      static_cast<int>(H));
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "dt_rows: launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
 }

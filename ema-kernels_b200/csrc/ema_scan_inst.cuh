@@ -24,8 +24,9 @@ int launch_fwd(const FwdLaunch& l) {
     auto fn = ema_fwd_kernel<T, BP, Q, MODE, SEQ>;
     int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), C::kBytes, &mask);
     if (e) return e;
-    fn<<<persistent_grid(l.tiles, l.num_sms, C::CTAS), C::NT, C::kBytes, l.stream>>>(*l.map_x, l.params);
-    return static_cast<int>(cudaGetLastError());
+    const cudaError_t le = launch_programmatic(fn, dim3(persistent_grid(l.tiles, l.num_sms, C::CTAS)), dim3(C::NT),
+                                               C::kBytes, l.stream, *l.map_x, l.params);
+    return static_cast<int>(le != cudaSuccess ? le : cudaGetLastError());
   }
 }
 
@@ -39,9 +40,9 @@ int launch_bwd(const BwdLaunch& l) {
     auto fn = ema_bwd_kernel<T, BP, Q, MODE>;
     int e = ensure_smem_attr(reinterpret_cast<const void*>(fn), C::kBytes, &mask);
     if (e) return e;
-    fn<<<persistent_grid(l.tiles, l.num_sms, C::CTAS), C::NT, C::kBytes, l.stream>>>(*l.map_x, *l.map_dy,
-                                                                                     *l.map_dx, l.params);
-    return static_cast<int>(cudaGetLastError());
+    const cudaError_t le = launch_programmatic(fn, dim3(persistent_grid(l.tiles, l.num_sms, C::CTAS)), dim3(C::NT),
+                                               C::kBytes, l.stream, *l.map_x, *l.map_dy, *l.map_dx, l.params);
+    return static_cast<int>(le != cudaSuccess ? le : cudaGetLastError());
   }
 }
 

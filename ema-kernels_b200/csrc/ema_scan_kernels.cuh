@@ -721,7 +721,6 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
   uint32_t* status = &ws.hdr[kHdrStatus];
   if (tid == 0) {
     s_fail = 0u;
-    s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 33);       // producer lane 0 (expect_tx) + 32 cp.async arrivals
       mbar_init(&empty[s], NW + 1);  // every compute warp + the look-back warp
@@ -733,6 +732,9 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     }
     fence_mbar_init();
   }
+  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
+  grid_dep_release();
+  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const uint32_t tag = epoch + 1u;
@@ -1134,7 +1136,6 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   uint32_t* status = &ws.hdr[kHdrStatus];
   if (tid == 0) {
     s_fail = 0u;
-    s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 33);
       mbar_init(&empty[s], NW + 1);
@@ -1147,6 +1148,9 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     }
     fence_mbar_init();
   }
+  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
+  grid_dep_release();
+  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const uint32_t tag = epoch + 1u;
