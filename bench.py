@@ -660,6 +660,10 @@ def run_ema(args, rank, world, local_rank):
     from kernels import _lib
     from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
     QB = backward_chunk(Q)
+    bwd_kernel = "ema_bwd_kernel"
+    if args.ema_backward == "tc":  # the tcgen05 backward (bf16, headdim 64, 128-token tiles)
+        _lib.check(_lib.lib.ema_set_tensor_core_path(1), "ema_set_tensor_core_path")
+        bwd_kernel = "ema_bwd_tc_kernel"
     rows, heads = _shard(world, rank)
     hx, hdt, hA, hdy = _inputs(0, dev)  # the global batch (same seed on every rank), then this rank's part
     hx, hdy = hx[rows, :, heads].contiguous(), hdy[rows, :, heads].contiguous()
@@ -807,6 +811,7 @@ def run_ema(args, rank, world, local_rank):
             cpu = _cpu_baseline()
         cfg = _ema_config(world)
         cfg.update({"rows_per_gpu": hx.shape[0], "heads_per_gpu": hx.shape[2], "backward_chunk": QB,
+                    "backward_kernel": bwd_kernel,
                     "timing": "one CUDA graph per step (dt transpose, forward, backward; programmatic "
                               "dependent launch between them); events around each replay on the launching "
                               "stream; the per-kernel split from a second graph of the same step with events "
@@ -815,13 +820,14 @@ def run_ema(args, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": "Mtokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
-            "roofline": {"bound": "hbm", "kernel": "ema_bwd_kernel", "achieved": bwd_gbs, "peak": peak,
-                         "unit": "GB/s", "frac": bwd_gbs / peak, "traffic": _profile_traffic(),
+            "roofline": {"bound": "hbm", "kernel": bwd_kernel, "achieved": bwd_gbs, "peak": peak,
+                         "unit": "GB/s", "frac": bwd_gbs / peak,
+                         "traffic": _profile_traffic() if bwd_kernel == "ema_bwd_kernel" else None,
                          "algorithmic_bytes_per_launch": BWD_BYTES_PER_TOKEN * toks,
                          "launch_ms": bwd_launch_s * 1e3, "peak_source": f"{peak_kind} (hbm_gbs)"},
             "kernels": {"forward (dt_rows_kernel + ema_fwd_kernel)": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs,
                                                                       "frac": fwd_gbs / peak},
-                        "ema_bwd_kernel": {"ms": bwd_launch_s * 1e3, "gbs": bwd_gbs, "frac": bwd_gbs / peak}},
+                        bwd_kernel: {"ms": bwd_launch_s * 1e3, "gbs": bwd_gbs, "frac": bwd_gbs / peak}},
             "step_roofline": {"algorithmic_bytes_per_step_per_gpu": BYTES_PER_TOKEN * toks, "achieved_gbs": step_gbs,
                               "frac": step_gbs / peak, "peak_source": peak_kind},
             "e2e": {"value": TOKENS / (e2e_ms * 1e-3) / 1e6, "unit": "Mtokens/s",
@@ -863,6 +869,9 @@ def main():
                     help="profile: run --steps eager fwd+bwd steps and exit (for ncu captures)")
     ap.add_argument("--profile-batch", type=int, default=0,
                     help="with --mode profile --workload ssd: batch of the capture (default: the config's)")
+    ap.add_argument("--ema-backward", choices=["scan", "tc"], default="scan",
+                    help="EMA backward kernel: scan (CUDA-core scan, the default the autograd op runs) or tc "
+                         "(the tcgen05 backward, ema_bwd_tc_kernel; for comparison)")
     ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
                     help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
                          "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")
