@@ -212,6 +212,42 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
 }
 
+// ---- the SSD's dt map ---------------------------------------------------------
+// dt <- clamp(softplus(dt + bias[h]), lo, hi), each step optional (Mamba-2's
+// dt_bias / dt_softplus / dt_limit).  softplus(v) = log1p(exp(v)), v itself
+// above 20 (torch's default threshold).  *deriv (if given) receives d dt / d
+// (dt given): sigmoid(v) for the softplus, times 0 where the clamp is active.
+struct DtMap {
+  const float* bias;  // (H,) or null
+  int softplus;
+  int clamp;
+  float lo, hi;
+};
+__device__ __forceinline__ bool dt_map_active(const DtMap& m) {
+  return m.bias != nullptr || m.softplus != 0 || m.clamp != 0;
+}
+__device__ __forceinline__ float dt_map(const DtMap& m, int h, float raw, float* deriv) {
+  float v = (m.bias != nullptr) ? raw + m.bias[h] : raw;
+  float d = 1.f;
+  if (m.softplus) {
+    if (v <= 20.f) {
+      d = 1.f / (1.f + expf(-v));
+      v = log1pf(expf(v));
+    }
+  }
+  if (m.clamp) {
+    if (v < m.lo || v > m.hi) d = 0.f;
+    v = fminf(fmaxf(v, m.lo), m.hi);
+  }
+  if (deriv != nullptr) *deriv = d;
+  return v;
+}
+// The map an SsdFwdArgs / SsdBwdArgs asks for.
+template <class Args>
+inline DtMap dt_map_of(const Args* a) {
+  return DtMap{a->dt_bias, a->dt_softplus, a->dt_clamp, a->dt_min, a->dt_max};
+}
+
 // ---- element packs --------------------------------------------------------
 template <int BYTES>
 struct RawVec;

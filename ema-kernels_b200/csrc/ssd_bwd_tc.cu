@@ -72,7 +72,8 @@ constexpr int oF = oYL + R64;       // floats below
 // float offsets within oF
 constexpr int fCs = 0, fDt = 64, fRow = 192, fColT = 320, fColR = 384, fInter = 448, fV = 576, fMisc = 704;
 constexpr int fEcol = 712;  // exp(cs_g - cs_j) per key j (g: first key of its 16-key group), and a wide-group mask
-constexpr int kFloats = 780;
+constexpr int fDer = 780;   // d dt / d (dt given) per token, where a dt map is active
+constexpr int kFloats = 844;
 // exp(cs_i - cs_j) is factored per 16-key group unless the cumsum spans more than this inside it
 constexpr float kWideSpan = 60.f;
 constexpr int kTP = 65;                     // padded row of the staged T / R tiles
@@ -106,6 +107,8 @@ struct Params {
   float* dD;
   float* ds0;  // (B,H,P,N) or null
   uint32_t* status;
+  DtMap dtm;        // dt <- clamp(softplus(dt + bias)), applied as dt lands in shared memory
+  float* ddt_bias;  // (H,) or null: the gradient of the bias, accumulated
 };
 
 __device__ __forceinline__ void split_bf16(float v, float& hi, float& lo) {
@@ -145,6 +148,8 @@ __global__ void __launch_bounds__(NT, 1)
   float* s_V = F + fV;          // [2][64]
   float* s_misc = F + fMisc;
   float* s_ecol = F + fEcol;
+  float* s_der = F + fDer;
+  const bool mapped = dt_map_active(p.dtm);
   uint32_t* s_wide = reinterpret_cast<uint32_t*>(F + fEcol + 64);
   uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + oBar);
   uint64_t* bar_mma = bar_full + 1;
@@ -274,7 +279,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (tid >= 128) stage_state(p.nc - 1, tid - 128);
 
-  float dA_acc = 0.f, dD_acc = 0.f;
+  float dA_acc = 0.f, dD_acc = 0.f, dbias_acc = 0.f;
   const uint32_t id64 = tc::idesc_bf16(64, 64, false, false);
 
   for (int c = p.nc - 1; c >= 0; --c) {
@@ -286,6 +291,17 @@ __global__ void __launch_bounds__(NT, 1)
     if (warp == 0) {
       cp_async_wait_all();
       __syncwarp();
+      if (mapped) {  // the map in place (padding tokens stay 0), its derivative for ddt
+        float* dtw = s_dt + (c & 1) * Q;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = lane + 32 * e;
+          float der = 0.f;
+          if (t0 + j < p.L) dtw[j] = dt_map(p.dtm, h, dtw[j], &der);
+          s_der[j] = der;
+        }
+        __syncwarp();
+      }
       float a0 = dtv[lane] * Ah, a1 = dtv[32 + lane] * Ah;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -612,16 +628,27 @@ __global__ void __launch_bounds__(NT, 1)
       }
       r0 += __shfl_sync(0xffffffffu, r1, 0);
       const float R[2] = {r0, r1};
-      float da = 0.f;
+      float da = 0.f, db = 0.f;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int i = lane + 32 * e;
-        if (i < nq) p.ddt[(static_cast<size_t>(b) * p.L + t0 + i) * p.H + h] = dir[e] + Ah * R[e];
+        if (i < nq) {
+          float g = dir[e] + Ah * R[e];
+          if (mapped) {
+            g *= s_der[i];
+            db += g;
+          }
+          p.ddt[(static_cast<size_t>(b) * p.L + t0 + i) * p.H + h] = g;
+        }
         da = fmaf(dtk[e], R[e], da);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) da += __shfl_xor_sync(0xffffffffu, da, o);
+      for (int o = 16; o > 0; o >>= 1) {
+        da += __shfl_xor_sync(0xffffffffu, da, o);
+        db += __shfl_xor_sync(0xffffffffu, db, o);
+      }
       dA_acc += da;
+      dbias_acc += db;
     } else if (warp >= 4 && c > 0) {
       stage_state(c - 1, tid - 128);  // the next chunk's state tiles, off its critical path
     }
@@ -632,6 +659,7 @@ __global__ void __launch_bounds__(NT, 1)
   for (int o = 16; o > 0; o >>= 1) dD_acc += __shfl_xor_sync(0xffffffffu, dD_acc, o);
   if (lane == 0 && p.dD != nullptr) atomicAdd(&p.dD[h], dD_acc);
   if (tid == 0) atomicAdd(&p.dA[h], dA_acc);
+  if (tid == 0 && p.ddt_bias != nullptr) atomicAdd(&p.ddt_bias[h], dbias_acc);
   if (warp == 0) cp_async_wait_all();
   tc::fence_before_sync();
   __syncthreads();
@@ -714,6 +742,8 @@ int ssd_bwd_tc_launch(const SsdBwdArgs* a, cudaStream_t stream) {
   p.dC = a->dC;
   p.dD = a->dD;
   p.ds0 = a->d_initial_state;
+  p.dtm = dt_map_of(a);
+  p.ddt_bias = a->ddt_bias;
   p.status = ssd_tc_status_device_ptr();
   if (p.status == nullptr) return fail(EMA_ERR_CUDA, "ssd_bwd: status word");
   r = ensure_smem_attr(reinterpret_cast<const void*>(ssd_bwd_tc_kernel), kSmem, &g_mask);

@@ -91,6 +91,7 @@ struct Params {
   float* chunk_states;  // (B, nc64, H, P, N) or null
   float* s_final;       // (B, H, P, N) or null
   uint32_t* status;
+  DtMap dtm;            // dt <- clamp(softplus(dt + bias)), applied as dt lands in shared memory
 };
 
 __device__ uint32_t g_status;
@@ -242,9 +243,11 @@ __global__ void __launch_bounds__(NT, 1)
       float run = 0.f;
       cp_async_wait_all();
       __syncwarp();
+      const bool mapped = dt_map_active(p.dtm);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         d[k] = s_dt[warp * Q + 4 * lane + k];
+        if (mapped && t0 + 4 * lane + k < p.L) d[k] = dt_map(p.dtm, h0 + warp, d[k], nullptr);  // padding stays 0
         run += d[k];
         c[k] = run;
       }
@@ -570,6 +573,7 @@ int ssd_fwd_tc_launch(const SsdFwdArgs* a, cudaStream_t stream) {
   p.sy_h = a->out_stride[2];
   p.chunk_states = a->chunk_states;
   p.s_final = a->final_state;
+  p.dtm = dt_map_of(a);
   void* st = nullptr;
   if (cudaGetSymbolAddress(&st, g_status) != cudaSuccess) return fail(EMA_ERR_CUDA, "ssd_fwd: status word");
   p.status = static_cast<uint32_t*>(st);

@@ -75,6 +75,8 @@ struct Params {
   float* dC;
   float* dD;
   float* ds0;
+  DtMap dtm;        // dt <- clamp(softplus(dt + bias)), applied as dt is staged
+  float* ddt_bias;  // (H,) or null: the gradient of the bias, accumulated
 };
 
 __device__ __forceinline__ uint32_t ld32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
@@ -294,7 +296,9 @@ __global__ void __launch_bounds__(NTHR, 2) ssd_fwd_kernel(const Params p) {
               LN, sm.BT, LQ);
     load_tile(p.Cm + b * p.sc_b + static_cast<long long>(t0) * p.sc_l + grp * p.sc_g, p.sc_l, Q, N, nq, sm.Cm,
               LN, nullptr, 0);
-    if (tid < Q) sm.dtv[tid] = (tid < nq) ? p.dt[(static_cast<size_t>(b) * p.L + t0 + tid) * p.H + h] : 0.f;
+    if (tid < Q)
+      sm.dtv[tid] = (tid < nq) ? dt_map(p.dtm, h, p.dt[(static_cast<size_t>(b) * p.L + t0 + tid) * p.H + h], nullptr)
+                               : 0.f;
     // chunk start state, saved for the backward
     if (p.chunk_states != nullptr) {
       float* cs_out = p.chunk_states + ((static_cast<size_t>(b) * p.nc + c) * p.H + h) * P * N;
@@ -420,6 +424,7 @@ struct BwdSmem {
   bf16 Ed[Q * LQ];     // a DX dt
   float cs[Q];
   float dtv[Q];
+  float der[Q];        // d dt / d (dt given) per token
   float rowT[Q], colT[Q], colR[Q], inter[Q], V[Q];
   float misc[4];       // [0] sum dS_out . Sin, [1] sum dy . x
 };
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
       const int pp = p0 + gq + 8 * (r >> 1), nn = n0 + nt * 8 + 2 * q4 + (r & 1);
       ds[nt][r] = (p.ds_final != nullptr) ? p.ds_final[(bh * P + pp) * N + nn] : 0.f;
     }
-  float dA_acc = 0.f, dD_acc = 0.f;
+  float dA_acc = 0.f, dD_acc = 0.f, dbias_acc = 0.f;
 
   for (int c = p.nc - 1; c >= 0; --c) {
     const int t0 = c * Q;
@@ -463,7 +468,10 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
     load_tile_batched<Q, N>(p.Cm + b * p.sc_b + static_cast<long long>(t0) * p.sc_l + grp * p.sc_g, p.sc_l, nq,
                             sm.Cm, LN, sm.CT, LQ);
     if (tid < Q) {
-      sm.dtv[tid] = (tid < nq) ? p.dt[(static_cast<size_t>(b) * p.L + t0 + tid) * p.H + h] : 0.f;
+      float der = 0.f;
+      sm.dtv[tid] = (tid < nq) ? dt_map(p.dtm, h, p.dt[(static_cast<size_t>(b) * p.L + t0 + tid) * p.H + h], &der)
+                               : 0.f;
+      sm.der[tid] = der;
       sm.rowT[tid] = sm.colT[tid] = sm.colR[tid] = sm.inter[tid] = sm.V[tid] = 0.f;
     }
     if (tid < 4) sm.misc[tid] = 0.f;
@@ -719,16 +727,24 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
       }
       r0v += __shfl_sync(FULL, r1, 0);
       const float R[2] = {r0v, r1};
-      float da = 0.f;
+      float da = 0.f, db = 0.f;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int i = lane + 32 * e;
-        if (i < nq) p.ddt[(static_cast<size_t>(b) * p.L + t0 + i) * p.H + h] = dir[e] + Ah * R[e];
+        if (i < nq) {
+          const float g = (dir[e] + Ah * R[e]) * sm.der[i];
+          p.ddt[(static_cast<size_t>(b) * p.L + t0 + i) * p.H + h] = g;
+          db += g;
+        }
         da = fmaf(dtk[e], R[e], da);
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) da += __shfl_xor_sync(FULL, da, o);
+      for (int o = 16; o > 0; o >>= 1) {
+        da += __shfl_xor_sync(FULL, da, o);
+        db += __shfl_xor_sync(FULL, db, o);
+      }
       dA_acc += da;
+      dbias_acc += db;
     }
     __syncthreads();  // before the next chunk overwrites the staged operands
   }
@@ -737,6 +753,7 @@ __global__ void __launch_bounds__(NTHR, 1) ssd_bwd_kernel(const Params p) {
   for (int o = 16; o > 0; o >>= 1) dD_acc += __shfl_xor_sync(FULL, dD_acc, o);
   if (lane == 0 && p.dD != nullptr) atomicAdd(&p.dD[h], dD_acc);
   if (tid == 0) atomicAdd(&p.dA[h], dA_acc);
+  if (tid == 0 && p.ddt_bias != nullptr) atomicAdd(&p.ddt_bias[h], dbias_acc);
   if (p.ds0 != nullptr) {
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
@@ -842,6 +859,7 @@ extern "C" EMA_API int ssd_fwd_launch(const SsdFwdArgs* a, void* stream) {
   p.sy_h = a->out_stride[2];
   p.chunk_states = a->chunk_states;
   p.s_final = a->final_state;
+  p.dtm = emab::dt_map_of(a);
   static unsigned long long attr_mask = 0;
   r = emab::ensure_smem_attr(reinterpret_cast<const void*>(ssd_fwd_kernel), static_cast<int>(sizeof(FwdSmem)),
                              &attr_mask);
@@ -877,6 +895,7 @@ extern "C" EMA_API int ssd_bwd_launch(const SsdBwdArgs* a, void* stream) {
   if (e == cudaSuccess) e = cudaMemsetAsync(a->dB, 0, bl * a->ngroups * N * sizeof(float), s);
   if (e == cudaSuccess) e = cudaMemsetAsync(a->dC, 0, bl * a->ngroups * N * sizeof(float), s);
   if (e == cudaSuccess && a->dD != nullptr) e = cudaMemsetAsync(a->dD, 0, a->nheads * sizeof(float), s);
+  if (e == cudaSuccess && a->ddt_bias != nullptr) e = cudaMemsetAsync(a->ddt_bias, 0, a->nheads * sizeof(float), s);
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "ssd_bwd: %s", cudaGetErrorString(e));
   if (a->batch == 0 || a->seqlen == 0) return EMA_OK;
   // the tensor-core kernel, wherever its TMA and vector-store alignment holds
@@ -919,6 +938,8 @@ extern "C" EMA_API int ssd_bwd_launch(const SsdBwdArgs* a, void* stream) {
   p.dC = a->dC;
   p.dD = a->dD;
   p.ds0 = a->d_initial_state;
+  p.dtm = emab::dt_map_of(a);
+  p.ddt_bias = a->ddt_bias;
   static unsigned long long attr_mask = 0;
   r = emab::ensure_smem_attr(reinterpret_cast<const void*>(ssd_bwd_kernel), static_cast<int>(sizeof(BwdSmem)),
                              &attr_mask);

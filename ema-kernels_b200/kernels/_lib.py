@@ -83,6 +83,8 @@ class SsdFwdArgs(ctypes.Structure):
         ("D", _ptr), ("initial_state", _ptr),
         ("out", _ptr), ("out_stride", _i64 * 3),
         ("chunk_states", _ptr), ("final_state", _ptr),
+        ("dt_bias", _ptr), ("dt_softplus", _i32), ("dt_clamp", _i32), ("dt_min", ctypes.c_float),
+        ("dt_max", ctypes.c_float),
     ]
 
 
@@ -99,6 +101,20 @@ class SsdBwdArgs(ctypes.Structure):
         ("d_final_state", _ptr),
         ("dx", _ptr), ("dx_stride", _i64 * 3),
         ("ddt", _ptr), ("dA", _ptr), ("dB", _ptr), ("dC", _ptr), ("dD", _ptr), ("d_initial_state", _ptr),
+        ("dt_bias", _ptr), ("dt_softplus", _i32), ("dt_clamp", _i32), ("dt_min", ctypes.c_float),
+        ("dt_max", ctypes.c_float), ("ddt_bias", _ptr),
+    ]
+
+
+class SsdGateArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64),
+        ("dtype", _i32), ("reserved", _i32),
+        ("y", _ptr), ("y_stride", _i64 * 3),
+        ("z", _ptr), ("z_stride", _i64 * 3),
+        ("out", _ptr), ("out_stride", _i64 * 3),
+        ("dout", _ptr), ("dout_stride", _i64 * 3),
+        ("dz", _ptr), ("dz_stride", _i64 * 3),
     ]
 
 
@@ -125,6 +141,10 @@ lib.ssd_fwd_launch.restype = ctypes.c_int
 lib.ssd_fwd_launch.argtypes = [ctypes.POINTER(SsdFwdArgs), _ptr]
 lib.ssd_bwd_launch.restype = ctypes.c_int
 lib.ssd_bwd_launch.argtypes = [ctypes.POINTER(SsdBwdArgs), _ptr]
+lib.ssd_gate_fwd_launch.restype = ctypes.c_int
+lib.ssd_gate_fwd_launch.argtypes = [ctypes.POINTER(SsdGateArgs), _ptr]
+lib.ssd_gate_bwd_launch.restype = ctypes.c_int
+lib.ssd_gate_bwd_launch.argtypes = [ctypes.POINTER(SsdGateArgs), _ptr]
 lib.ssd_device_status.restype = ctypes.c_int
 lib.ssd_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p

@@ -11,10 +11,12 @@ third-party and absent here).  Same argument names and layouts:
 
     s_t = exp(dt_t A_h) s_{t-1} + dt_t x_t B_t^T,   y_t = s_t C_t + D_h x_t
 
-``dt_bias`` / ``dt_softplus`` / ``dt_limit`` are applied before the scan
-(dt <- clamp(softplus(dt + dt_bias), *dt_limit)) and ``z`` gating after it
-(out <- y * silu(z), in fp32, stored in y's dtype), all differentiated by
-autograd.  Not supported yet: ``seq_idx`` / ``cu_seqlens`` (packed sequences).
+``dt_bias`` / ``dt_softplus`` / ``dt_limit`` map dt inside the SSD kernels
+(dt <- clamp(softplus(dt + dt_bias), *dt_limit), the map's gradient folded into
+the backward's ddt, plus the gradient of dt_bias), and ``z`` gates the output
+(out <- y * silu(z), fp32 arithmetic, stored in y's dtype) on the native gate
+kernels, one pass each way.  Not supported yet: ``seq_idx`` / ``cu_seqlens``
+(packed sequences).
 
 Two kernel families serve the call, by d_state:
 
@@ -72,9 +74,27 @@ def _prep(x, dt, A, B, C, D):
     return b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk
 
 
+def _set_dt_map(a, H, dev, dt_bias, dt_softplus, dt_limit):
+    """The kernels' dt map in SsdFwdArgs / SsdBwdArgs: dt <- clamp(softplus(dt + dt_bias),
+    *dt_limit), each step optional (the clamp only for a limit other than (0, inf), as
+    the torch form of the map applies it).  Returns the bias tensor the launch reads."""
+    bias = None
+    if dt_bias is not None:
+        assert dt_bias.shape == (H,), "dt_bias must be (nheads,)"
+        bias = dt_bias.detach().to(device=dev, dtype=torch.float32).contiguous()
+    lo, hi = float(dt_limit[0]), float(dt_limit[1])
+    a.dt_bias = _lib.ptr(bias)
+    a.dt_softplus = int(bool(dt_softplus))
+    a.dt_clamp = int(lo > 0.0 or hi != float("inf"))
+    a.dt_min, a.dt_max = lo, hi
+    return bias
+
+
 def ssd_chunk_scan_fwd(x, dt, A, B, C, D=None, initial_states=None, return_final_states=False,
-                       save_states=True):
-    """Forward.  Returns (y, chunk_states or None, final_states or None)."""
+                       save_states=True, dt_bias=None, dt_softplus=False, dt_limit=(0.0, float("inf"))):
+    """Forward.  Returns (y, chunk_states or None, final_states or None).  ``dt`` is
+    mapped inside the kernels: clamp(softplus(dt + dt_bias), *dt_limit), each step
+    optional (mamba_chunk_scan_combined's dt options)."""
     b_, L, H, P, G, N, xk, dtk, Ak, Bk, Ck, Dk = _prep(x, dt, A, B, C, D)
     dev = x.device
     y = torch.empty(b_, L, H, P, dtype=x.dtype, device=dev)
@@ -97,15 +117,20 @@ def ssd_chunk_scan_fwd(x, dt, A, B, C, D=None, initial_states=None, return_final
     a.out, a.out_stride = y.data_ptr(), _s3(y)
     a.chunk_states = _lib.ptr(cst)
     a.final_state = _lib.ptr(fin)
+    bias = _set_dt_map(a, H, dev, dt_bias, dt_softplus, dt_limit)  # noqa: F841 (alive across the launch)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.ssd_fwd_launch(a, _lib.stream_ptr(dev)), "ssd_chunk_scan_fwd")
     return y, cst, fin
 
 
 def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=None, need_d_initial=False,
-                       dx_out=None):
+                       dx_out=None, dt_bias=None, dt_softplus=False, dt_limit=(0.0, float("inf")),
+                       ddt_bias_out=None):
     """Backward.  Returns (dx, ddt, dA, dB, dC, dD or None, d_initial_states or None);
     dB / dC are fp32 (batch, seqlen, ngroups, dstate), summed over each group's heads.
+    With the forward's dt map (``dt_bias`` / ``dt_softplus`` / ``dt_limit``), ddt is
+    the gradient of the dt given, and ``ddt_bias_out`` ((nheads,) fp32, optional)
+    receives the gradient of dt_bias.
     ``dx_out``: a (batch, seqlen, nheads, headdim) bf16 buffer to write dx into
     (headdim stride 1, other strides even); the tensor-core kernel needs them to
     be multiples of 8 and 16-byte alignment, else the mma.sync kernel runs."""
@@ -142,6 +167,10 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=
     a.ddt, a.dA, a.dB, a.dC = ddt.data_ptr(), dA.data_ptr(), dB.data_ptr(), dC.data_ptr()
     a.dD = _lib.ptr(dD)
     a.d_initial_state = _lib.ptr(d_init)
+    bias = _set_dt_map(a, H, dev, dt_bias, dt_softplus, dt_limit)  # noqa: F841 (alive across the launch)
+    if ddt_bias_out is not None:
+        assert ddt_bias_out.shape == (H,) and ddt_bias_out.dtype == torch.float32 and ddt_bias_out.is_contiguous()
+    a.ddt_bias = _lib.ptr(ddt_bias_out)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.ssd_bwd_launch(a, _lib.stream_ptr(dev)), "ssd_chunk_scan_bwd")
     return dx, ddt, dA, dB, dC, dD, d_init
@@ -149,22 +178,74 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=
 
 class SsdChunkScanFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, dt, A, B, C, D, initial_states, return_final_states):
-        y, cst, fin = ssd_chunk_scan_fwd(x, dt, A, B, C, D, initial_states, return_final_states)
-        ctx.save_for_backward(x, dt, A, B, C, D, cst)
+    def forward(ctx, x, dt, A, B, C, D, initial_states, return_final_states, dt_bias, dt_softplus, dt_limit):
+        y, cst, fin = ssd_chunk_scan_fwd(x, dt, A, B, C, D, initial_states, return_final_states,
+                                         dt_bias=dt_bias, dt_softplus=dt_softplus, dt_limit=dt_limit)
+        ctx.save_for_backward(x, dt, A, B, C, D, cst, dt_bias)
         ctx.has_init = initial_states is not None
-        ctx.dtypes = (dt.dtype, A.dtype, B.dtype, C.dtype, None if D is None else D.dtype)
+        ctx.dt_opts = (dt_softplus, dt_limit)
+        ctx.dtypes = (dt.dtype, A.dtype, B.dtype, C.dtype, None if D is None else D.dtype,
+                      None if dt_bias is None else dt_bias.dtype)
         return (y, fin) if return_final_states else y
 
     @staticmethod
     def backward(ctx, dy, *rest):
-        x, dt, A, B, C, D, cst = ctx.saved_tensors
+        x, dt, A, B, C, D, cst, dt_bias = ctx.saved_tensors
         dfin = rest[0] if rest else None
         if dy is None:
             dy = torch.zeros_like(x)
-        dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(x, dt, A, B, C, cst, dy, D, dfin, ctx.has_init)
-        tdt, tA, tB, tC, tD = ctx.dtypes
-        return (dx, ddt.to(tdt), dA.to(tA), dB.to(tB), dC.to(tC), None if dD is None else dD.to(tD), d_init, None)
+        dbias = None if dt_bias is None else torch.empty(dt_bias.shape, dtype=torch.float32, device=x.device)
+        dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(
+            x, dt, A, B, C, cst, dy, D, dfin, ctx.has_init, dt_bias=dt_bias, dt_softplus=ctx.dt_opts[0],
+            dt_limit=ctx.dt_opts[1], ddt_bias_out=dbias)
+        tdt, tA, tB, tC, tD, tbias = ctx.dtypes
+        return (dx, ddt.to(tdt), dA.to(tA), dB.to(tB), dC.to(tC), None if dD is None else dD.to(tD), d_init, None,
+                None if dbias is None else dbias.to(tbias), None, None)
+
+
+def _gate_args(y, z, out):
+    a = _lib.SsdGateArgs()
+    a.batch, a.seqlen, a.nheads, a.headdim = y.shape
+    a.dtype = _lib.DTYPE_CODES[y.dtype]
+    a.y, a.y_stride = y.data_ptr(), _s3(y)
+    a.z, a.z_stride = z.data_ptr(), _s3(z)
+    a.out, a.out_stride = out.data_ptr(), _s3(out)
+    return a
+
+
+def _last_dim_unit(t):
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+class SsdGateFn(torch.autograd.Function):
+    """out = y * silu(z) on the native gate kernels (one pass each way, fp32
+    arithmetic, one rounding to y's dtype); z is taken in y's dtype."""
+
+    @staticmethod
+    def forward(ctx, y, z):
+        assert y.is_cuda and z.shape == y.shape and y.ndim == 4, "y and z: (batch, seqlen, nheads, headdim)"
+        y = _last_dim_unit(y)
+        zk = _last_dim_unit(z.to(y.dtype))
+        out = torch.empty_like(y, memory_format=torch.contiguous_format)
+        a = _gate_args(y, zk, out)
+        with torch.cuda.device(y.device):
+            _lib.check(_lib.lib.ssd_gate_fwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_fwd")
+        ctx.save_for_backward(y, zk)
+        ctx.z_dtype = z.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, zk = ctx.saved_tensors
+        dout = _last_dim_unit(dout.to(y.dtype))
+        dy = torch.empty_like(y, memory_format=torch.contiguous_format)
+        dz = torch.empty_like(zk, memory_format=torch.contiguous_format)
+        a = _gate_args(y, zk, dy)
+        a.dout, a.dout_stride = dout.data_ptr(), _s3(dout)
+        a.dz, a.dz_stride = dz.data_ptr(), _s3(dz)
+        with torch.cuda.device(y.device):
+            _lib.check(_lib.lib.ssd_gate_bwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_bwd")
+        return dy, dz.to(ctx.z_dtype)
 
 
 def _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size):
@@ -207,19 +288,21 @@ def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bia
         "packed sequences (seq_idx / cu_seqlens) are not supported yet"
     assert chunk_size > 0 and math.log2(chunk_size).is_integer(), "chunk_size must be a power of two"
     assert z is None or z.shape == x.shape, "z must have the shape of x"
-    if dt_bias is not None:
-        dt = dt + dt_bias
-    if dt_softplus:
-        dt = F.softplus(dt)
-    dt_min, dt_max = float(dt_limit[0]), float(dt_limit[1])
-    if dt_min > 0.0 or dt_max != float("inf"):
-        dt = dt.clamp(dt_min, dt_max)
     if B.shape[-1] == 1:
+        # the EMA kernels take dt as given: the map runs as torch ops here
+        if dt_bias is not None:
+            dt = dt + dt_bias
+        if dt_softplus:
+            dt = F.softplus(dt)
+        dt_min, dt_max = float(dt_limit[0]), float(dt_limit[1])
+        if dt_min > 0.0 or dt_max != float("inf"):
+            dt = dt.clamp(dt_min, dt_max)
         out = _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size)
-    else:
-        out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states)
+    else:  # the SSD kernels apply the dt map themselves
+        out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states, dt_bias,
+                                   bool(dt_softplus), (float(dt_limit[0]), float(dt_limit[1])))
     if z is None:
         return out
     y, fin = out if return_final_states else (out, None)
-    y = (y.float() * F.silu(z.float())).to(y.dtype)
+    y = SsdGateFn.apply(y, z)
     return (y, fin) if return_final_states else y

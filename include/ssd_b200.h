@@ -10,7 +10,8 @@
  * _mamba_chunk_scan_combined_bwd), with the same layouts:
  *
  *   x, y, dx        (batch, seqlen, nheads, headdim)      bf16, headdim stride 1
- *   dt, ddt         (batch, seqlen, nheads)               fp32 contiguous, dt > 0 (after any softplus)
+ *   dt, ddt         (batch, seqlen, nheads)               fp32 contiguous (dt > 0 after the optional
+ *                                                          bias / softplus / clamp map in the args)
  *   A, dA, D, dD    (nheads,)                             fp32
  *   B, C            (batch, seqlen, ngroups, dstate)      bf16, dstate stride 1
  *   dB, dC          (batch, seqlen, ngroups, dstate)      fp32 contiguous (summed over the heads of a group)
@@ -54,6 +55,14 @@ typedef struct SsdFwdArgs {
   int64_t out_stride[3];
   float* chunk_states;           /* (B, ssd_internal_chunks(L), H, P, N) or NULL (no backward) */
   float* final_state;            /* (B,H,P,N) or NULL */
+  /* dt pre-processing inside the kernels (mamba_chunk_scan_combined's dt_bias,
+   * dt_softplus and dt_limit): dt <- clamp(softplus(dt + dt_bias), dt_min, dt_max),
+   * each step optional; all zero (the default of a zero-filled struct): dt as given.
+   * softplus(v) = log(1 + exp(v)), and v itself above 20 (torch's threshold). */
+  const float* dt_bias;          /* (H,) or NULL */
+  int32_t dt_softplus;           /* non-zero: apply the softplus */
+  int32_t dt_clamp;              /* non-zero: clamp to [dt_min, dt_max] */
+  float dt_min, dt_max;
 } SsdFwdArgs;
 
 typedef struct SsdBwdArgs {
@@ -81,7 +90,40 @@ typedef struct SsdBwdArgs {
   float* dC;                     /* (B,L,G,N) fp32 */
   float* dD;                     /* (H,) or NULL (required when D is given) */
   float* d_initial_state;        /* (B,H,P,N) or NULL */
+  /* dt pre-processing inside the kernels (mamba_chunk_scan_combined's dt_bias,
+   * dt_softplus and dt_limit): dt <- clamp(softplus(dt + dt_bias), dt_min, dt_max),
+   * each step optional; all zero (the default of a zero-filled struct): dt as given.
+   * softplus(v) = log(1 + exp(v)), and v itself above 20 (torch's threshold). */
+  const float* dt_bias;          /* (H,) or NULL */
+  int32_t dt_softplus;           /* non-zero: apply the softplus */
+  int32_t dt_clamp;              /* non-zero: clamp to [dt_min, dt_max] */
+  float dt_min, dt_max;
+  /* With a dt map, ddt is the gradient of the dt given (before the bias), and
+   * ddt_bias (H,) -- zero-filled by the launcher, then accumulated -- the
+   * gradient of dt_bias; NULL to skip it. */
+  float* ddt_bias;
 } SsdBwdArgs;
+
+/* The output gate of mamba_chunk_scan_combined's `z` argument, out = y * silu(z),
+ * and its gradient, one pass each over (batch, seqlen, nheads, headdim) tensors
+ * of one element type (EMA_DTYPE_*), channel stride 1, fp32 arithmetic:
+ *   ssd_gate_fwd_launch:  out = y * z * sigmoid(z)
+ *   ssd_gate_bwd_launch:  out = dout * z * sigmoid(z)                        (dy)
+ *                         dz  = dout * y * sigmoid(z) * (1 + z (1 - sigmoid(z)))
+ * Replaces the gate mamba_ssm applies in its chunk-scan kernels (no counterpart
+ * in the reference, whose benchmark call passes no z: bench_ema_total.py:72-76). */
+typedef struct SsdGateArgs {
+  int64_t batch, seqlen, nheads, headdim;
+  int32_t dtype;
+  int32_t reserved;
+  const void* y;    int64_t y_stride[3];     /* element strides of b, l, h */
+  const void* z;    int64_t z_stride[3];
+  void* out;        int64_t out_stride[3];   /* forward: the gated output; backward: dy */
+  const void* dout; int64_t dout_stride[3];  /* backward only */
+  void* dz;         int64_t dz_stride[3];    /* backward only */
+} SsdGateArgs;
+EMA_API int ssd_gate_fwd_launch(const SsdGateArgs* args, void* stream);
+EMA_API int ssd_gate_bwd_launch(const SsdGateArgs* args, void* stream);
 
 /* Number of 64-token internal chunks of a sequence: ceil(seqlen / 64). */
 EMA_API int64_t ssd_internal_chunks(int64_t seqlen);

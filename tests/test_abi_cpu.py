@@ -58,8 +58,9 @@ def test_ssd_struct_layouts_match_header():
     import subprocess
     import tempfile
     from kernels import _lib
-    fields_f = ["final_state", "chunk_states", "out", "D"]
-    fields_b = ["d_initial_state", "dD", "ddt", "dout", "chunk_states"]
+    fields_f = ["final_state", "chunk_states", "out", "D", "dt_bias", "dt_softplus", "dt_clamp", "dt_min", "dt_max"]
+    fields_b = ["d_initial_state", "dD", "ddt", "dout", "chunk_states", "dt_bias", "dt_softplus", "dt_clamp",
+                "dt_min", "dt_max", "ddt_bias"]
     code = ('#include "ssd_b200.h"\n#include <stdio.h>\n#include <stddef.h>\nint main(){printf("%zu %zu'
             + ' %zu' * (len(fields_f) + len(fields_b)) + '\\n", sizeof(SsdFwdArgs), sizeof(SsdBwdArgs)'
             + ''.join(f', offsetof(SsdFwdArgs, {f})' for f in fields_f)

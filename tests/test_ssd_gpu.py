@@ -72,60 +72,157 @@ def test_ssd_forward_backward_match_oracle(L, H, G, with_states):
         assert e <= 2e-2, f"{name}: normwise relative error {e:.3e}"
 
 
-def test_mamba_call_form_autograd():
-    """mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D, dt_bias, dt_softplus) through
-    autograd equals the direct launchers plus the softplus chain rule."""
-    from kernels.ssd_combined import mamba_chunk_scan_combined, ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
-    B, L, H, P, N, G = 1, 192, 4, 64, 128, 1
-    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=3)
-    x, dt_raw, A, Bm, Cm, D, dy = (t.to(DEV) for t in (tx, tdt, tA, tB, tC, tD, tdy))
-    bias = torch.full((H,), -1.0, device=DEV)
-    leaves = [t.clone().requires_grad_() for t in (x, dt_raw, A, Bm, Cm, D)]
-    y = mamba_chunk_scan_combined(*leaves[:5], 256, D=leaves[5], dt_bias=bias, dt_softplus=True)
-    y.backward(dy)
-    dt = torch.nn.functional.softplus(dt_raw + bias)
-    y2, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
-    dx, ddt, dA, dB, dC, dD, _ = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dy, D)
-    assert torch.equal(y, y2)
-    torch.testing.assert_close(leaves[0].grad, dx, rtol=0, atol=0)
-    torch.testing.assert_close(leaves[1].grad, ddt * torch.sigmoid(dt_raw + bias), rtol=1e-6, atol=1e-6)
-    torch.testing.assert_close(leaves[3].grad, dB.to(torch.bfloat16), rtol=1e-2, atol=1e-2)
-    torch.testing.assert_close(leaves[2].grad, dA, rtol=1e-3, atol=1e-3)
-    torch.testing.assert_close(leaves[5].grad, dD, rtol=1e-3, atol=1e-3)
+def _dt_map_np(raw, bias, softplus, lo, hi):
+    """The kernels' dt map in float64: clamp(softplus(raw + bias), lo, hi) and its
+    derivative (torch's softplus threshold 20; 0 where the clamp is active)."""
+    v = raw + (bias[None, None, :] if bias is not None else 0.0)
+    if softplus:
+        sp = np.where(v <= 20.0, np.log1p(np.exp(np.minimum(v, 20.0))), v)
+        d = np.where(v <= 20.0, 1.0 / (1.0 + np.exp(-v)), 1.0)
+    else:
+        sp, d = v, np.ones_like(v)
+    inside = (sp >= lo) & (sp <= hi)
+    return np.clip(sp, lo, hi), d * inside
 
 
-def test_mamba_call_form_z_gating_and_dt_limit():
-    """mamba_chunk_scan_combined with z gating and a dt_limit that clamps on both
-    sides: equals the direct launchers on the clamped dt, gated by silu(z), with
-    the chain rule through the clamp, the softplus and the gate."""
-    from kernels.ssd_combined import mamba_chunk_scan_combined, ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
-    B, L, H, P, N, G = 1, 192, 4, 64, 128, 2
-    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=13)
-    x, dt_raw, A, Bm, Cm, D, dy = (t.to(DEV) for t in (tx, tdt, tA, tB, tC, tD, tdy))
-    z = torch.from_numpy(np.random.default_rng(14).standard_normal((B, L, H, P)).astype(np.float32))
-    z = z.to(torch.bfloat16).to(DEV)
-    bias = torch.full((H,), -1.0, device=DEV)
-    limit = (0.32, 0.33)  # softplus(dt_raw - 1) spans ~0.313-0.341 here: both bounds bite
-    leaves = [t.clone().requires_grad_() for t in (x, dt_raw, A, Bm, Cm, D, z)]
-    y = mamba_chunk_scan_combined(*leaves[:5], 256, D=leaves[5], z=leaves[6], dt_bias=bias, dt_softplus=True,
-                                  dt_limit=limit)
-    y.backward(dy)
-    pre = torch.nn.functional.softplus(dt_raw + bias)
-    inside = (pre >= limit[0]) & (pre <= limit[1])
-    assert 0 < int(inside.sum()) < inside.numel(), "the limit should clamp some but not all of dt"
-    dt = pre.clamp(*limit)
-    y2, cst, _ = ssd_chunk_scan_fwd(x, dt, A, Bm, Cm, D)
-    gate = torch.nn.functional.silu(z.float())
-    assert torch.equal(y, (y2.float() * gate).to(torch.bfloat16))
-    dys = (dy.float() * gate).to(torch.bfloat16)
-    dx, ddt, dA, dB, dC, dD, _ = ssd_chunk_scan_bwd(x, dt, A, Bm, Cm, cst, dys, D)
-    torch.testing.assert_close(leaves[0].grad, dx, rtol=0, atol=0)
-    torch.testing.assert_close(leaves[1].grad, ddt * inside * torch.sigmoid(dt_raw + bias), rtol=1e-6, atol=1e-6)
-    torch.testing.assert_close(leaves[2].grad, dA, rtol=1e-3, atol=1e-3)
-    torch.testing.assert_close(leaves[5].grad, dD, rtol=1e-3, atol=1e-3)
-    sg = torch.sigmoid(z.float())
-    dz = (dy.float() * y2.float() * sg * (1 + z.float() * (1 - sg))).to(torch.bfloat16)
-    torch.testing.assert_close(leaves[6].grad, dz, rtol=1e-2, atol=1e-2)
+def _limit_in_gaps(vals, q_lo, q_hi):
+    """Clamp bounds near two quantiles of vals, each in the middle of the widest
+    gap between neighbouring values there, so fp32 and float64 agree on which
+    elements the clamp touches."""
+    v = np.sort(vals.ravel())
+    out = []
+    for q in (q_lo, q_hi):
+        k = int(q * (v.size - 1))
+        w = slice(max(k - 20, 0), min(k + 20, v.size - 1))
+        gaps = np.diff(v[w.start:w.stop + 1])
+        j = w.start + int(np.argmax(gaps))
+        out.append(0.5 * (v[j] + v[j + 1]))
+    return tuple(out)
+
+
+# (H, G): 2 heads per group -> tcgen05 forward; 1 head per group -> mma.sync forward;
+# the backward is the tcgen05 kernel throughout (its mma.sync twin: the strided-dx test below)
+@pytest.mark.parametrize("H,G,softplus,clamp,gate", [(4, 1, True, False, False), (4, 2, True, True, True),
+                                                      (3, 3, False, True, True)])
+def test_mamba_call_form_dt_map_and_gate_match_oracle(H, G, softplus, clamp, gate):
+    """mamba_chunk_scan_combined with dt_bias / dt_softplus / dt_limit (mapped inside
+    the SSD kernels) and z gating (the native gate kernels), through autograd,
+    against the float64 oracle on the mapped dt: y, dx, ddt of the raw dt, the
+    dt_bias gradient, dA, dB, dC, dD and dz."""
+    from kernels.ssd_combined import mamba_chunk_scan_combined
+    B, L, P, N = 2, 192, 64, 128
+    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=13 + H + G)
+    rng = np.random.default_rng(14 + H)
+    bias = rng.uniform(-2.0, 0.5, H).astype(np.float32)
+    dt_target = tdt.double().numpy()
+    raw = (np.log(np.expm1(dt_target)) if softplus else dt_target) - bias[None, None, :]
+    raw = raw.astype(np.float32)
+    pre, _ = _dt_map_np(raw.astype(np.float64), bias.astype(np.float64), softplus, -np.inf, np.inf)
+    limit = _limit_in_gaps(pre, 0.1, 0.9) if clamp else (0.0, float("inf"))
+    dt_eff, deriv = _dt_map_np(raw.astype(np.float64), bias.astype(np.float64), softplus, *limit)
+    if clamp:
+        assert 0 < int((deriv == 0).sum()) < deriv.size, "the limit should clamp some but not all of dt"
+    z = rng.standard_normal((B, L, H, P)).astype(np.float32)
+    tz = torch.from_numpy(z).to(torch.bfloat16)
+    leaves = [t.to(DEV).requires_grad_() for t in (tx, torch.from_numpy(raw), tA, tB, tC, tD,
+                                                    torch.from_numpy(bias), tz)]
+    y = mamba_chunk_scan_combined(*leaves[:5], 256, D=leaves[5], z=leaves[7] if gate else None,
+                                  dt_bias=leaves[6], dt_softplus=softplus, dt_limit=limit)
+    y.backward(tdy.to(DEV))
+    torch.cuda.synchronize()
+    assert _device_status_clear() == 0
+
+    args = (_f64(tx), dt_eff, tA.double().numpy(), _f64(tB), _f64(tC))
+    r = so.ssd_fwd(*args, D=tD.double().numpy())
+    zf = _f64(tz)
+    sg = 1.0 / (1.0 + np.exp(-zf))
+    dout = _f64(tdy)
+    if gate:
+        assert_lowp_close(y, r["y"] * zf * sg, "gated y")
+        # the scan's incoming gradient, rounded to bf16 as the gate kernel stores it
+        dys = torch.from_numpy(dout * zf * sg).to(torch.bfloat16).double().numpy()
+        dz = dout * r["y"] * sg * (1.0 + zf * (1.0 - sg))
+        assert_lowp_close(leaves[7].grad, dz, "dz")
+    else:
+        assert_lowp_close(y, r["y"], "y")
+        dys = dout
+    g = so.ssd_bwd(*args, dys, D=tD.double().numpy())
+    ddt_raw = g["ddt"] * deriv
+    for name, k, ref in (("dx", leaves[0].grad, g["dx"]), ("ddt", leaves[1].grad, ddt_raw),
+                         ("dB", leaves[3].grad, g["dB"]), ("dC", leaves[4].grad, g["dC"])):
+        assert_lowp_close(k, ref, name)
+        assert_reference_rule(k, ref, name)
+    for name, k, ref in (("dA", leaves[2].grad, g["dA"]), ("dD", leaves[5].grad, g["dD"]),
+                         ("d dt_bias", leaves[6].grad, ddt_raw.sum(axis=(0, 1)))):
+        e = float(np.abs(k.cpu().double().numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
+        assert e <= 2e-2, f"{name}: normwise relative error {e:.3e}"
+
+
+def test_dt_map_on_the_mma_sync_backward():
+    """The dt map and the dt_bias gradient in the mma.sync backward (a dx buffer
+    whose strides the tensor-core backward cannot store into), against the
+    tensor-core backward and the oracle."""
+    from kernels.ssd_combined import ssd_chunk_scan_bwd, ssd_chunk_scan_fwd
+    B, L, H, P, N, G = 1, 160, 2, 64, 128, 1
+    tx, tdt, tA, tB, tC, tD, tdy = _inputs(B, L, H, P, N, G, seed=23)
+    x, A, Bm, Cm, D, dy = (t.to(DEV) for t in (tx, tA, tB, tC, tD, tdy))
+    bias = np.array([-1.5, 0.25], dtype=np.float32)
+    raw = (np.log(np.expm1(tdt.double().numpy())) - bias[None, None, :]).astype(np.float32)
+    pre, _ = _dt_map_np(raw.astype(np.float64), bias.astype(np.float64), True, -np.inf, np.inf)
+    limit = _limit_in_gaps(pre, 0.15, 0.85)
+    dt_eff, deriv = _dt_map_np(raw.astype(np.float64), bias.astype(np.float64), True, *limit)
+    traw, tbias = torch.from_numpy(raw).to(DEV), torch.from_numpy(bias).to(DEV)
+    opts = dict(dt_bias=tbias, dt_softplus=True, dt_limit=limit)
+    y, cst, _ = ssd_chunk_scan_fwd(x, traw, A, Bm, Cm, D, **opts)
+    pad = torch.zeros(B, L, H, P + 2, dtype=torch.bfloat16, device=DEV)  # head stride 66: the mma.sync kernel
+    db_old, db_new = (torch.empty(H, device=DEV) for _ in range(2))
+    outs_old = ssd_chunk_scan_bwd(x, traw, A, Bm, Cm, cst, dy, D, dx_out=pad[..., :P], ddt_bias_out=db_old, **opts)
+    outs_new = ssd_chunk_scan_bwd(x, traw, A, Bm, Cm, cst, dy, D, ddt_bias_out=db_new, **opts)
+    torch.cuda.synchronize()
+    assert _device_status_clear() == 0
+    args = (_f64(tx), dt_eff, tA.double().numpy(), _f64(tB), _f64(tC))
+    assert_lowp_close(y, so.ssd_fwd(*args, D=tD.double().numpy())["y"], "y")
+    g = so.ssd_bwd(*args, _f64(tdy), D=tD.double().numpy())
+    ddt_raw = g["ddt"] * deriv
+    for outs, db in ((outs_old, db_old), (outs_new, db_new)):
+        assert_lowp_close(outs[0], g["dx"], "dx")
+        assert_lowp_close(outs[1], ddt_raw, "ddt")
+        ref = ddt_raw.sum(axis=(0, 1))
+        e = float(np.abs(db.cpu().double().numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
+        assert e <= 2e-2, f"d dt_bias: normwise relative error {e:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("strided", [False, True])
+def test_gate_kernels_match_float64(dtype, strided):
+    """The native gate out = y silu(z) and its gradient (dy, dz) against float64,
+    on contiguous tensors (16-byte vector path) and on views with a head stride
+    of headdim + 2 (element path)."""
+    from kernels.ssd_combined import SsdGateFn
+    rng = np.random.default_rng(31)
+    B, L, H, P = 2, 70, 3, 64
+    mk = lambda: torch.from_numpy(rng.standard_normal((B, L, H, P + 2)).astype(np.float32) * 2).to(dtype)  # noqa: E731
+    yb, zb = (mk().to(DEV).requires_grad_() for _ in range(2))
+    dout = mk().to(DEV)[..., :P]
+    # views with head stride P + 2 (element path), or contiguous copies (vector path)
+    y, z = (yb[..., :P], zb[..., :P]) if strided else (yb[..., :P].contiguous(), zb[..., :P].contiguous())
+    if not strided:
+        dout = dout.contiguous()
+    out = SsdGateFn.apply(y, z)
+    out.backward(dout)
+    torch.cuda.synchronize()
+    yl_grad, zl_grad = yb.grad[..., :P], zb.grad[..., :P]
+    yd, zd, dd = (t.detach().double().cpu().numpy() for t in (y, z, dout))
+    sg = 1.0 / (1.0 + np.exp(-zd))
+    refs = (("out", out, yd * zd * sg), ("dy", yl_grad, dd * zd * sg),
+            ("dz", zl_grad, dd * yd * sg * (1.0 + zd * (1.0 - sg))))
+    for name, k, ref in refs:
+        assert k.dtype == dtype, name
+        if dtype == torch.float32:
+            e = float(np.abs(k.detach().double().cpu().numpy() - ref).max() / np.abs(ref).max())
+            assert e <= 1e-5, f"{name}: normwise relative error {e:.3e}"
+        else:
+            assert_lowp_close(k, ref, name)
 
 
 def test_ssd_forward_steep_decay_matches_oracle():
