@@ -407,14 +407,14 @@ class StepGraph:
     there makes the backward wait for the forward in full -- and gives the
     per-kernel times of the same step."""
 
-    def __init__(self, x, dt, A, dy, dev):
+    def __init__(self, x, dt, A, dy, dev, fq=Q):
         from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
         b_, l_, h_, _ = x.shape
-        self.qb = backward_chunk(Q)  # what the autograd op runs: 128-token backward tiles on half-chunk states
+        self.qb = backward_chunk(fq)  # what the autograd op runs: 128-token backward tiles on half-chunk states
         self.dtr = torch.empty(b_, h_, l_, dtype=torch.float32, device=dev)
 
         def fwd():
-            return ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=self.qb != Q, dt_rows=self.dtr)
+            return ema_chunk_scan_fwd(x, dt, A, fq, half_chunk_states=self.qb != fq, dt_rows=self.dtr)
 
         def bwd(states):
             return ema_chunk_scan_bwd(x, dt, A, states, dy, self.qb, dt_rows=self.dtr)
@@ -659,11 +659,16 @@ def run_ema(args, rank, world, local_rank):
 
     from kernels import _lib
     from kernels.ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
-    QB = backward_chunk(Q)
-    bwd_kernel = "ema_bwd_kernel"
-    if args.ema_backward == "tc":  # the tcgen05 backward (bf16, headdim 64, 128-token tiles)
-        _lib.check(_lib.lib.ema_set_tensor_core_path(1), "ema_set_tensor_core_path")
-        bwd_kernel = "ema_bwd_tc_kernel"
+    # tensor-core variants, for comparison (ema_set_tensor_core_path bits 0 / 1):
+    # the tcgen05 backward on 128-token tiles; the tcgen05 forward on 128-token
+    # tiles (it then runs at chunk 128, and the backward with it)
+    FQ = 128 if args.ema_forward == "tc" else Q
+    QB = backward_chunk(FQ)
+    bwd_kernel = "ema_bwd_tc_kernel" if args.ema_backward == "tc" else "ema_bwd_kernel"
+    fwd_kernel = "ema_fwd_tc_kernel" if args.ema_forward == "tc" else "ema_fwd_kernel"
+    tc_bits = (1 if args.ema_backward == "tc" else 0) | (2 if args.ema_forward == "tc" else 0)
+    if tc_bits:
+        _lib.lib.ema_set_tensor_core_path(tc_bits)
     rows, heads = _shard(world, rank)
     hx, hdt, hA, hdy = _inputs(0, dev)  # the global batch (same seed on every rank), then this rank's part
     hx, hdy = hx[rows, :, heads].contiguous(), hdy[rows, :, heads].contiguous()
@@ -673,7 +678,7 @@ def run_ema(args, rank, world, local_rank):
     if args.mode == "profile":
         dtr = torch.empty(x.shape[0], x.shape[2], L, dtype=torch.float32, device=dev)
         for _ in range(max(1, args.steps)):
-            y, states, _ = ema_chunk_scan_fwd(x, dt, A, Q, half_chunk_states=QB != Q, dt_rows=dtr)
+            y, states, _ = ema_chunk_scan_fwd(x, dt, A, FQ, half_chunk_states=QB != FQ, dt_rows=dtr)
             ema_chunk_scan_bwd(x, dt, A, states, dy, QB, dt_rows=dtr)
         torch.cuda.synchronize(dev)
         if dist is not None:
@@ -688,7 +693,7 @@ def run_ema(args, rank, world, local_rank):
         flush_rd.sum()
 
     stream = torch.cuda.current_stream(dev)
-    sg = StepGraph(x, dt, A, dy, dev)
+    sg = StepGraph(x, dt, A, dy, dev, FQ)
     clocks = ClockSampler(local_rank)
     clocks.start()
     K = args.steps
@@ -707,7 +712,7 @@ def run_ema(args, rank, world, local_rank):
     weak = None
     if world > 1:  # every rank a whole B8 batch of its own
         wx, wdt, wA, wdy = (t.to(dev) for t in _inputs(rank, dev))
-        wg = StepGraph(wx, wdt, wA, wdy, dev)
+        wg = StepGraph(wx, wdt, wA, wdy, dev, FQ)
         if dist is not None:
             dist.barrier()
         (wms, _, _) = _max_over_ranks(wg.run(K, args.warmup, flush_l2, stream), dev, dist)
@@ -747,7 +752,7 @@ def run_ema(args, rank, world, local_rank):
         xd = xd.detach().requires_grad_()
         dtd = dtd.detach().requires_grad_()
         Ad = Ad.detach().requires_grad_()
-        yd = ema_chunk_scan_combined(xd, dtd, Ad, Q)
+        yd = ema_chunk_scan_combined(xd, dtd, Ad, FQ)
         yd.backward(dyd)
         loss = (yd.detach().float() * dyd.float()).sum()
         consumed[i].record(stream)
@@ -810,8 +815,8 @@ def run_ema(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu_baseline:
             cpu = _cpu_baseline()
         cfg = _ema_config(world)
-        cfg.update({"rows_per_gpu": hx.shape[0], "heads_per_gpu": hx.shape[2], "backward_chunk": QB,
-                    "backward_kernel": bwd_kernel,
+        cfg.update({"rows_per_gpu": hx.shape[0], "heads_per_gpu": hx.shape[2], "forward_chunk": FQ,
+                    "backward_chunk": QB, "forward_kernel": fwd_kernel, "backward_kernel": bwd_kernel,
                     "timing": "one CUDA graph per step (dt transpose, forward, backward; programmatic "
                               "dependent launch between them); events around each replay on the launching "
                               "stream; the per-kernel split from a second graph of the same step with events "
@@ -825,8 +830,8 @@ def run_ema(args, rank, world, local_rank):
                          "traffic": _profile_traffic() if bwd_kernel == "ema_bwd_kernel" else None,
                          "algorithmic_bytes_per_launch": BWD_BYTES_PER_TOKEN * toks,
                          "launch_ms": bwd_launch_s * 1e3, "peak_source": f"{peak_kind} (hbm_gbs)"},
-            "kernels": {"forward (dt_rows_kernel + ema_fwd_kernel)": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs,
-                                                                      "frac": fwd_gbs / peak},
+            "kernels": {f"forward (dt_rows_kernel + {fwd_kernel})": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs,
+                                                                     "frac": fwd_gbs / peak},
                         bwd_kernel: {"ms": bwd_launch_s * 1e3, "gbs": bwd_gbs, "frac": bwd_gbs / peak}},
             "step_roofline": {"algorithmic_bytes_per_step_per_gpu": BYTES_PER_TOKEN * toks, "achieved_gbs": step_gbs,
                               "frac": step_gbs / peak, "peak_source": peak_kind},
@@ -872,6 +877,9 @@ def main():
     ap.add_argument("--ema-backward", choices=["scan", "tc"], default="scan",
                     help="EMA backward kernel: scan (CUDA-core scan, the default the autograd op runs) or tc "
                          "(the tcgen05 backward, ema_bwd_tc_kernel; for comparison)")
+    ap.add_argument("--ema-forward", choices=["scan", "tc"], default="scan",
+                    help="EMA forward kernel: scan (CUDA-core scan at chunk 256, the default) or tc (the tcgen05 "
+                         "forward, ema_fwd_tc_kernel, at chunk 128; for comparison)")
     ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
                     help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
                          "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")

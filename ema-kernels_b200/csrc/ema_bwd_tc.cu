@@ -108,19 +108,8 @@ static_assert(kSmemAlloc <= kSmemPerCtaMax, "shared memory");
 constexpr uint32_t kCols = 512;
 constexpr uint32_t kSetCols = 256;
 
-// Row i, 16-byte chunk c (8 bf16) of a 128-byte swizzled tile.
-__device__ __forceinline__ uint32_t chunk_off(int row, int c) {
-  return static_cast<uint32_t>(row) * 128u + ((static_cast<uint32_t>(c) ^ (static_cast<uint32_t>(row) & 7u)) << 4);
-}
-
-// Bounded wait of a warp group: one warp polls, the group then meets at a
-// named barrier.  False (for every thread of the group) on a timeout.
-__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint32_t* status, bool poller,
-                                           int bar_id, int nthreads, volatile uint32_t* fail) {
-  if (poller && !mbar_wait_bounded(bar, parity, status) && (threadIdx.x & 31) == 0) *fail = 1u;
-  named_sync(bar_id, nthreads);
-  return *fail == 0u;
-}
+using tc::chunk_off;
+using tc::group_wait;
 
 // 8 floats -> bf16 hi (4 words) and bf16 lo (4 words), hi + lo = v to 2^-14
 // relative: hi is v truncated to bf16, lo the (exact) remainder v - hi

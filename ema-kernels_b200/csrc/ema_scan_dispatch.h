@@ -50,8 +50,14 @@ int bwd_dispatch_f16(const BwdLaunch& l);
 // encoded (message set), otherwise a cudaError_t.
 int bwd_tc_launch(const BwdLaunch& l, int dtype, const void* x, const int64_t xs[3], const void* dy,
                   const int64_t dys[3], void* dx, const int64_t dxs[3]);
-// Whether the tensor-core kernels are used where they apply (default on).
+// Tensor-core forward (ema_fwd_tc.cu): dt form, bf16, headdim 64, 128-token
+// chunks, y requested, no seq_idx / mid-chunk states.  Same return values.
+int fwd_tc_launch(const FwdLaunch& l, int dtype, const void* x, const int64_t xs[3], void* y,
+                  const int64_t ys[3]);
+// Whether the tensor-core backward / forward are used where they apply
+// (ema_set_tensor_core_path bits 0 / 1; default off).
 bool tensor_core_path_enabled();
+bool fwd_tensor_core_path_enabled();
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
 

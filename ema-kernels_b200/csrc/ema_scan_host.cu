@@ -240,11 +240,13 @@ int map_dispatch_result(int r, const char* what) {
 void set_last_error(const char* msg) { g_last_error = msg; }
 
 namespace {
-// off by default: the tensor-core backward is exact to tolerance but not yet
-// faster than the CUDA-core kernel on the benchmark shape
+// bit 0: the tensor-core backward, bit 1: the tensor-core forward.  Off by
+// default: both agree with the CUDA-core kernels within the bf16 tolerance but
+// are slower on the benchmark shape.
 std::atomic<int> g_tensor_core_path{0};
 }
-bool tensor_core_path_enabled() { return g_tensor_core_path.load(std::memory_order_relaxed) != 0; }
+bool tensor_core_path_enabled() { return (g_tensor_core_path.load(std::memory_order_relaxed) & 1) != 0; }
+bool fwd_tensor_core_path_enabled() { return (g_tensor_core_path.load(std::memory_order_relaxed) & 2) != 0; }
 
 int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const uint64_t* dims,
                const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
@@ -385,6 +387,12 @@ int ema_fwd_launch(const EmaFwdArgs* a, void* stream) {
   r = num_sms_of_current_device(&l.num_sms);
   if (r) return r;
   l.stream = static_cast<cudaStream_t>(stream);
+  if (fwd_tensor_core_path_enabled()) {
+    r = fwd_tc_launch(l, a->dtype, a->x, a->x_stride, a->out, a->out_stride);
+    if (r == 0) return EMA_OK;
+    if (r == -3) return EMA_ERR_CUDA;
+    if (r != 1) return map_dispatch_result(r, "ema_fwd (tensor cores)");
+  }
   switch (a->dtype) {
     case EMA_DTYPE_BF16: r = fwd_dispatch_bf16(l); break;
     case EMA_DTYPE_F16: r = fwd_dispatch_f16(l); break;
@@ -546,7 +554,7 @@ int ema_workspace_clear_status(void* workspace, void* stream) {
 }
 
 int ema_set_tensor_core_path(int32_t enable) {
-  const int prev = g_tensor_core_path.exchange(enable ? 1 : 0);
+  const int prev = g_tensor_core_path.exchange(enable & 3);
   return prev;
 }
 

@@ -63,6 +63,20 @@ __device__ __forceinline__ void ld_sw16(const unsigned char* region, int row, in
   }
 }
 
+// Byte offset of row `row`, 16-byte chunk c (8 bf16) of a 128-byte swizzled tile.
+__device__ __forceinline__ uint32_t chunk_off(int row, int c) {
+  return static_cast<uint32_t>(row) * 128u + ((static_cast<uint32_t>(c) ^ (static_cast<uint32_t>(row) & 7u)) << 4);
+}
+
+// Bounded wait of a warp group: one warp polls, the group then meets at a
+// named barrier.  False (for every thread of the group) on a timeout.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint32_t* status, bool poller,
+                                           int bar_id, int nthreads, volatile uint32_t* fail) {
+  if (poller && !mbar_wait_bounded(bar, parity, status) && (threadIdx.x & 31) == 0) *fail = 1u;
+  named_sync(bar_id, nthreads);
+  return *fail == 0u;
+}
+
 // ---- descriptors -----------------------------------------------------------
 // Shared-memory matrix descriptor, 128-byte swizzle, version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {

@@ -6,9 +6,9 @@ library has not been built (``python ema-kernels_b200/build.py``).
 
 Scratch memory: the EMA scan kernels need a zero-initialised workspace for
 their inter-CTA look-back.  :func:`workspace` keeps one per (device, stream),
-allocated through PyTorch's caching allocator and grown on demand.  Buffers
-are never freed while the process lives, so CUDA graphs that captured them stay
-valid; launches on different streams never share one.
+allocated through PyTorch's caching allocator and grown by powers of two.  A
+buffer a CUDA graph capture used is never freed while the process lives, so
+captured graphs stay valid; launches on different streams never share one.
 """
 
 from __future__ import annotations
@@ -174,20 +174,31 @@ def ptr(t) -> int:
 # --------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws: dict = {}
-_ws_retired: list = []
+_ws_captured: set = set()  # keys whose current buffer was handed to a CUDA graph capture
+_ws_retired: list = []     # replaced buffers a captured graph may still launch with
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-initialised scratch of at least ``nbytes`` for the current stream of ``device``."""
+    """Zero-initialised scratch of at least ``nbytes`` for the current stream of ``device``.
+
+    Sizes grow by powers of two (at least 1 MiB), so a process replaces a
+    stream's buffer only a few times.  A replaced buffer is kept alive only if
+    a CUDA graph capture used it (the graph holds its address); otherwise it
+    returns to PyTorch's caching allocator, which reuses memory in stream order,
+    so kernels still queued on this stream finish with it first."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), stream_ptr(device))
+    capturing = torch.cuda.is_current_stream_capturing()
     with _ws_lock:
         buf = _ws.get(key)
         if buf is None or buf.numel() < nbytes:
-            if buf is not None:
+            if buf is not None and key in _ws_captured:
                 _ws_retired.append(buf)
-            size = max(nbytes, 1 << 20)
+            _ws_captured.discard(key)
+            size = 1 << max(20, (max(nbytes, 1) - 1).bit_length())
             buf = torch.zeros(size, dtype=torch.uint8, device=device)
             _ws[key] = buf
+        if capturing:
+            _ws_captured.add(key)
         return buf
 
 

@@ -203,11 +203,15 @@ EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* 
 /* Clears the workspace status word (asynchronously on `stream`). */
 EMA_API int ema_workspace_clear_status(void* workspace, void* stream);
 /* Selects whether the launchers use their tensor-core (tcgen05) kernels where
- * one applies (today: the backward for bf16, headdim 64, chunk_size 128, dx
- * requested) or always the CUDA-core kernels; process-wide, default 0 (the
- * CUDA-core kernels).  Returns the previous setting.  No counterpart in the
- * reference: the two kernels agree within the bf16 tolerance, and this switch
- * lets a caller pick one.
+ * one applies or always the CUDA-core kernels; process-wide, default 0 (the
+ * CUDA-core kernels).  Bit 0 (1): the backward, for bf16, headdim 64,
+ * chunk_size 128, dx requested.  Bit 1 (2): the forward, for the dt form, bf16,
+ * headdim 64, chunk_size 128, out given, no seq_idx and no mid_states; it
+ * rounds the decay matrix and dt x to bf16 once for y, as the reference's
+ * forward does (kernels/forward/ema_ssd_fwd.py:361-368), while the states
+ * stay fp32.  Returns the previous setting.  No counterpart in the reference:
+ * the kernels agree within the bf16 tolerance, and this switch lets a caller
+ * pick one.
  */
 EMA_API int ema_set_tensor_core_path(int32_t enable);
 /* Human-readable detail of the last error returned on the calling thread. */
