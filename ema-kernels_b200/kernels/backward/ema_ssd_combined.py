@@ -111,6 +111,41 @@ def compute_dpx(
     return dx, dA, d_issm_state
 
 
+# ---- dispatcher operators (namespace ema_b200) for the autograd pair below:
+# torch.compile traces them (shape-only "fake" implementations) -------------
+@torch.library.custom_op("ema_b200::ema_fwd_ref", mutates_args=(), device_types="cuda")
+def _fwd_ref_op(x: torch.Tensor, dA: torch.Tensor, chunk_size: int) -> tuple[torch.Tensor, torch.Tensor,
+                                                                             torch.Tensor, torch.Tensor]:
+    """ema_fwd_triton with every store: (out, states (b, nc, h, 1, p), da_cs, da_cs_sum)."""
+    out, states, da_cs, da_cs_sum = ema_fwd_triton(x, dA=dA, out=None, chunk_size=chunk_size, store_states=True,
+                                                   store_da_cs=True, store_da_cs_sum=True)
+    return out, states, da_cs, da_cs_sum
+
+
+@_fwd_ref_op.register_fake
+def _(x, dA, chunk_size):
+    b, s, h, p = x.shape
+    nc = -(-s // chunk_size)
+    return (torch.empty_like(x, memory_format=torch.contiguous_format),
+            x.new_empty((b, nc, h, 1, p), dtype=torch.float32), x.new_empty((b, h, s), dtype=torch.float32),
+            x.new_empty((b, h, nc), dtype=torch.float32))
+
+
+@torch.library.custom_op("ema_b200::ema_dpx", mutates_args=(), device_types="cuda")
+def _dpx_op(x: torch.Tensor, da_cs: torch.Tensor, da_cs_sum: torch.Tensor, SSM_States: torch.Tensor,
+            do: torch.Tensor, chunk_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """compute_dpx without the optional state terms: (dX, per-token decay gradient)."""
+    dx, dA, _ = compute_dpx(x, da_cs, da_cs_sum, SSM_States, do, chunk_size=chunk_size)
+    return dx, dA
+
+
+@_dpx_op.register_fake
+def _(x, da_cs, da_cs_sum, SSM_States, do, chunk_size):
+    b, s, h, _ = x.shape
+    return (torch.empty_like(x, memory_format=torch.contiguous_format),
+            x.new_empty((b, h, s), dtype=torch.float32))
+
+
 class _EmaFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x: torch.Tensor, A: torch.Tensor, chunk_size: int) -> torch.Tensor:
@@ -125,10 +160,7 @@ class _EmaFunction(torch.autograd.Function):
 
         dA = (A * math.log2(math.e)).to(torch.float32)
         dA = dA[:, None, :].expand(batch, nheads, seqlen).contiguous()
-        out, states, da_cs, da_cs_sum = ema_fwd_triton(
-            x, dA=dA, out=None, chunk_size=chunk_size,
-            store_states=True, store_da_cs=True, store_da_cs_sum=True,
-        )
+        out, states, da_cs, da_cs_sum = torch.ops.ema_b200.ema_fwd_ref(x, dA, chunk_size)
         # (b, nchunks, h, 1, p) -> (b, h, p, nchunks) as a view; compute_dpx takes any strides
         ssm_states = states.squeeze(3).permute(0, 2, 3, 1)
         ctx.chunk_size = chunk_size
@@ -140,8 +172,7 @@ class _EmaFunction(torch.autograd.Function):
         if grad_out is None:
             return None, None, None
         x, da_cs, da_cs_sum, ssm_states = ctx.saved_tensors
-        dx, dA, _ = compute_dpx(x, da_cs, da_cs_sum, ssm_states, grad_out, d_ossm_state=None,
-                                d_ox_state=None, chunk_size=ctx.chunk_size, has_input_state=False)
+        dx, dA = torch.ops.ema_b200.ema_dpx(x, da_cs, da_cs_sum, ssm_states, grad_out, ctx.chunk_size)
         # the decay is shared by all heads: its gradient is the head sum
         return dx, dA.sum(dim=1), None
 

@@ -182,37 +182,77 @@ def backward_chunk(chunk_size: int) -> int:
     return 128 if chunk_size == 256 else chunk_size
 
 
-class EmaChunkScanFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, dt, A, chunk_size, initial_states, return_final_states):
-        bq = backward_chunk(chunk_size)
-        B, L, H, _ = x.shape
-        dt_rows = torch.empty(B, H, L, dtype=torch.float32, device=x.device)
-        y, states, final = ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states,
-                                              return_final_states=return_final_states,
-                                              half_chunk_states=bq != chunk_size, dt_rows=dt_rows)
-        ctx.save_for_backward(x, dt, A, states, dt_rows)
-        ctx.chunk_size = bq
-        ctx.has_init = initial_states is not None
-        ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
-        if return_final_states:
-            return y, final
-        return y
+# ---- dispatcher operators (namespace ema_b200): traceable by torch.compile,
+# with shape-only ("fake") implementations and an autograd formula ----------
+@torch.library.custom_op("ema_b200::ema_scan_dt_fwd", mutates_args=(), device_types="cuda")
+def _scan_fwd_op(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int, half_chunk_states: bool,
+                 initial_states: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                  torch.Tensor]:
+    """(y, chunk start states, final state, dt as (B, H, L) rows for the backward)."""
+    B, L, H, _ = x.shape
+    dt_rows = torch.empty(B, H, L, dtype=torch.float32, device=x.device)
+    y, states, final = ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states,
+                                          return_final_states=True, half_chunk_states=half_chunk_states,
+                                          dt_rows=dt_rows)
+    return y, states, final, dt_rows
 
-    @staticmethod
-    def backward(ctx, dy, *rest):
-        x, dt, A, states, dt_rows = ctx.saved_tensors
-        dfin = rest[0] if rest else None
-        if dy is None:
-            dy = torch.zeros_like(x)
-        dx, ddt, dA, d_init = ema_chunk_scan_bwd(x, dt, A, states, dy, ctx.chunk_size,
-                                                 d_final_states=dfin, need_d_initial=ctx.has_init,
-                                                 dt_rows=dt_rows)
-        return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, d_init, None
+
+@_scan_fwd_op.register_fake
+def _(x, dt, A, chunk_size, half_chunk_states, initial_states):
+    B, L, H, P = x.shape
+    nc = -(-L // chunk_size)
+    if half_chunk_states:
+        states = x.new_empty((B, 2 * nc, H, P), dtype=torch.float32)[:, :-(-L // (chunk_size // 2))]
+    else:
+        states = x.new_empty((B, nc, H, P), dtype=torch.float32)
+    return (torch.empty_like(x, memory_format=torch.contiguous_format), states,
+            x.new_empty((B, H, P), dtype=torch.float32), x.new_empty((B, H, L), dtype=torch.float32))
+
+
+@torch.library.custom_op("ema_b200::ema_scan_dt_bwd", mutates_args=(), device_types="cuda")
+def _scan_bwd_op(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, states: torch.Tensor, dy: torch.Tensor,
+                 chunk_size: int, d_final_states: Optional[torch.Tensor], need_d_initial: bool,
+                 dt_rows: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dx, ddt, dA, d_initial_states -- empty unless ``need_d_initial``)."""
+    dx, ddt, dA, d_init = ema_chunk_scan_bwd(x, dt, A, states, dy, chunk_size, d_final_states=d_final_states,
+                                             need_d_initial=need_d_initial, dt_rows=dt_rows)
+    return dx, ddt, dA, d_init if d_init is not None else x.new_empty((0,), dtype=torch.float32)
+
+
+@_scan_bwd_op.register_fake
+def _(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial, dt_rows):
+    B, L, H, P = x.shape
+    return (torch.empty_like(x, memory_format=torch.contiguous_format),
+            x.new_empty((B, L, H), dtype=torch.float32), x.new_empty((H,), dtype=torch.float32),
+            x.new_empty((B, H, P) if need_d_initial else (0,), dtype=torch.float32))
+
+
+def _scan_setup(ctx, inputs, output):
+    x, dt, A, chunk_size, half_chunk_states, initial_states = inputs
+    ctx.save_for_backward(x, dt, A, output[1], output[3])
+    ctx.chunk_size = chunk_size // 2 if half_chunk_states else chunk_size
+    ctx.has_init = initial_states is not None
+
+
+def _scan_backward(ctx, dy, _d_states, d_final, _d_rows):
+    x, dt, A, states, dt_rows = ctx.saved_tensors
+    if dy is None:
+        dy = torch.zeros_like(x)
+    dx, ddt, dA, d_init = torch.ops.ema_b200.ema_scan_dt_bwd(x, dt, A, states, dy, ctx.chunk_size, d_final,
+                                                              ctx.has_init, dt_rows)
+    return dx, ddt.to(dt.dtype), dA.to(A.dtype), None, None, d_init if ctx.has_init else None
+
+
+torch.library.register_autograd("ema_b200::ema_scan_dt_fwd", _scan_backward, setup_context=_scan_setup)
 
 
 def ema_chunk_scan_combined(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256,
                             initial_states: Optional[torch.Tensor] = None,
                             return_final_states: bool = False):
-    """Autograd op: y (and the final state when ``return_final_states``)."""
-    return EmaChunkScanFn.apply(x, dt, A, chunk_size, initial_states, return_final_states)
+    """Autograd op: y (and the final state when ``return_final_states``).  Runs the
+    registered operator ``torch.ops.ema_b200.ema_scan_dt_fwd`` (its backward:
+    ``ema_scan_dt_bwd``), so ``torch.compile`` traces it without a graph break."""
+    _check_inputs(x, dt, A, chunk_size)
+    y, _, final, _ = torch.ops.ema_b200.ema_scan_dt_fwd(x, dt, A, chunk_size, backward_chunk(chunk_size) != chunk_size,
+                                                         initial_states)
+    return (y, final) if return_final_states else y

@@ -40,7 +40,7 @@ import torch.nn.functional as F
 
 from . import _lib
 
-__all__ = ["ssd_chunk_scan_fwd", "ssd_chunk_scan_bwd", "mamba_chunk_scan_combined"]
+__all__ = ["ssd_chunk_scan_fwd", "ssd_chunk_scan_bwd", "mamba_chunk_scan_combined", "ssd_gate"]
 
 
 def _s3(t):
@@ -176,31 +176,79 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D=None, d_final_states=
     return dx, ddt, dA, dB, dC, dD, d_init
 
 
-class SsdChunkScanFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, dt, A, B, C, D, initial_states, return_final_states, dt_bias, dt_softplus, dt_limit):
-        y, cst, fin = ssd_chunk_scan_fwd(x, dt, A, B, C, D, initial_states, return_final_states,
-                                         dt_bias=dt_bias, dt_softplus=dt_softplus, dt_limit=dt_limit)
-        ctx.save_for_backward(x, dt, A, B, C, D, cst, dt_bias)
-        ctx.has_init = initial_states is not None
-        ctx.dt_opts = (dt_softplus, dt_limit)
-        ctx.dtypes = (dt.dtype, A.dtype, B.dtype, C.dtype, None if D is None else D.dtype,
-                      None if dt_bias is None else dt_bias.dtype)
-        return (y, fin) if return_final_states else y
+# ---- dispatcher operators (namespace ema_b200): torch.compile traces them
+# (shape-only "fake" implementations), autograd through register_autograd ----
+def _empty0(like):
+    return like.new_empty((0,), dtype=torch.float32)
 
-    @staticmethod
-    def backward(ctx, dy, *rest):
-        x, dt, A, B, C, D, cst, dt_bias = ctx.saved_tensors
-        dfin = rest[0] if rest else None
-        if dy is None:
-            dy = torch.zeros_like(x)
-        dbias = None if dt_bias is None else torch.empty(dt_bias.shape, dtype=torch.float32, device=x.device)
-        dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(
-            x, dt, A, B, C, cst, dy, D, dfin, ctx.has_init, dt_bias=dt_bias, dt_softplus=ctx.dt_opts[0],
-            dt_limit=ctx.dt_opts[1], ddt_bias_out=dbias)
-        tdt, tA, tB, tC, tD, tbias = ctx.dtypes
-        return (dx, ddt.to(tdt), dA.to(tA), dB.to(tB), dC.to(tC), None if dD is None else dD.to(tD), d_init, None,
-                None if dbias is None else dbias.to(tbias), None, None)
+
+@torch.library.custom_op("ema_b200::ssd_fwd", mutates_args=(), device_types="cuda")
+def _ssd_fwd_op(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                D: Optional[torch.Tensor], initial_states: Optional[torch.Tensor], dt_bias: Optional[torch.Tensor],
+                dt_softplus: bool, dt_min: float, dt_max: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(y, the saved 64-token chunk states, the final state)."""
+    return ssd_chunk_scan_fwd(x, dt, A, B, C, D, initial_states, True, dt_bias=dt_bias, dt_softplus=dt_softplus,
+                              dt_limit=(dt_min, dt_max))
+
+
+@_ssd_fwd_op.register_fake
+def _(x, dt, A, B, C, D, initial_states, dt_bias, dt_softplus, dt_min, dt_max):
+    b_, L, H, P = x.shape
+    N = B.shape[3]
+    nci = -(-L // 64)
+    return (torch.empty(b_, L, H, P, dtype=x.dtype, device=x.device),
+            x.new_empty((b_, nci, H, P, N), dtype=torch.float32), x.new_empty((b_, H, P, N), dtype=torch.float32))
+
+
+@torch.library.custom_op("ema_b200::ssd_bwd", mutates_args=(), device_types="cuda")
+def _ssd_bwd_op(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                chunk_states: torch.Tensor, dy: torch.Tensor, D: Optional[torch.Tensor],
+                d_final_states: Optional[torch.Tensor], need_d_initial: bool, dt_bias: Optional[torch.Tensor],
+                dt_softplus: bool, dt_min: float, dt_max: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                          torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                          torch.Tensor, torch.Tensor]:
+    """(dx, ddt, dA, dB, dC, dD, d_initial_states, d dt_bias); the optional ones empty when absent."""
+    dbias = None if dt_bias is None else torch.empty(dt_bias.shape, dtype=torch.float32, device=x.device)
+    dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D, d_final_states,
+                                                         need_d_initial, dt_bias=dt_bias, dt_softplus=dt_softplus,
+                                                         dt_limit=(dt_min, dt_max), ddt_bias_out=dbias)
+    e = _empty0(x)
+    return (dx, ddt, dA, dB, dC, dD if dD is not None else e, d_init if d_init is not None else e,
+            dbias if dbias is not None else e)
+
+
+@_ssd_bwd_op.register_fake
+def _(x, dt, A, B, C, chunk_states, dy, D, d_final_states, need_d_initial, dt_bias, dt_softplus, dt_min, dt_max):
+    b_, L, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    f32 = torch.float32
+    e = _empty0(x)
+    return (torch.empty(b_, L, H, P, dtype=x.dtype, device=x.device), x.new_empty((b_, L, H), dtype=f32),
+            x.new_empty((H,), dtype=f32), x.new_empty((b_, L, G, N), dtype=f32),
+            x.new_empty((b_, L, G, N), dtype=f32), x.new_empty((H,), dtype=f32) if D is not None else e,
+            x.new_empty((b_, H, P, N), dtype=f32) if need_d_initial else e,
+            x.new_empty((H,), dtype=f32) if dt_bias is not None else e)
+
+
+def _ssd_setup(ctx, inputs, output):
+    x, dt, A, B, C, D, initial_states, dt_bias, dt_softplus, dt_min, dt_max = inputs
+    ctx.save_for_backward(x, dt, A, B, C, D, output[1], dt_bias)
+    ctx.has_init = initial_states is not None
+    ctx.opts = (dt_softplus, dt_min, dt_max)
+
+
+def _ssd_backward(ctx, dy, _d_states, d_final):
+    x, dt, A, B, C, D, cst, dt_bias = ctx.saved_tensors
+    if dy is None:
+        dy = torch.zeros_like(x)
+    dx, ddt, dA, dB, dC, dD, d_init, dbias = torch.ops.ema_b200.ssd_bwd(x, dt, A, B, C, cst, dy, D, d_final,
+                                                                        ctx.has_init, dt_bias, *ctx.opts)
+    return (dx, ddt.to(dt.dtype), dA.to(A.dtype), dB.to(B.dtype), dC.to(C.dtype),
+            None if D is None else dD.to(D.dtype), d_init if ctx.has_init else None,
+            None if dt_bias is None else dbias.to(dt_bias.dtype), None, None, None)
+
+
+torch.library.register_autograd("ema_b200::ssd_fwd", _ssd_backward, setup_context=_ssd_setup)
 
 
 def _gate_args(y, z, out):
@@ -217,35 +265,60 @@ def _last_dim_unit(t):
     return t if t.stride(-1) == 1 else t.contiguous()
 
 
-class SsdGateFn(torch.autograd.Function):
-    """out = y * silu(z) on the native gate kernels (one pass each way, fp32
-    arithmetic, one rounding to y's dtype); z is taken in y's dtype."""
+@torch.library.custom_op("ema_b200::ssd_gate_fwd", mutates_args=(), device_types="cuda")
+def _gate_fwd_op(y: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """out = y * silu(z) on the native gate kernel (y, z of one dtype)."""
+    assert y.ndim == 4 and z.shape == y.shape and z.dtype == y.dtype, "y and z: (batch, seqlen, nheads, headdim)"
+    y, z = _last_dim_unit(y), _last_dim_unit(z)
+    out = torch.empty_like(y, memory_format=torch.contiguous_format)
+    a = _gate_args(y, z, out)
+    with torch.cuda.device(y.device):
+        _lib.check(_lib.lib.ssd_gate_fwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_fwd")
+    return out
 
-    @staticmethod
-    def forward(ctx, y, z):
-        assert y.is_cuda and z.shape == y.shape and y.ndim == 4, "y and z: (batch, seqlen, nheads, headdim)"
-        y = _last_dim_unit(y)
-        zk = _last_dim_unit(z.to(y.dtype))
-        out = torch.empty_like(y, memory_format=torch.contiguous_format)
-        a = _gate_args(y, zk, out)
-        with torch.cuda.device(y.device):
-            _lib.check(_lib.lib.ssd_gate_fwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_fwd")
-        ctx.save_for_backward(y, zk)
-        ctx.z_dtype = z.dtype
-        return out
 
-    @staticmethod
-    def backward(ctx, dout):
-        y, zk = ctx.saved_tensors
-        dout = _last_dim_unit(dout.to(y.dtype))
-        dy = torch.empty_like(y, memory_format=torch.contiguous_format)
-        dz = torch.empty_like(zk, memory_format=torch.contiguous_format)
-        a = _gate_args(y, zk, dy)
-        a.dout, a.dout_stride = dout.data_ptr(), _s3(dout)
-        a.dz, a.dz_stride = dz.data_ptr(), _s3(dz)
-        with torch.cuda.device(y.device):
-            _lib.check(_lib.lib.ssd_gate_bwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_bwd")
-        return dy, dz.to(ctx.z_dtype)
+@_gate_fwd_op.register_fake
+def _(y, z):
+    return torch.empty_like(y, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("ema_b200::ssd_gate_bwd", mutates_args=(), device_types="cuda")
+def _gate_bwd_op(y: torch.Tensor, z: torch.Tensor, dout: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(dy, dz) of out = y * silu(z), one pass."""
+    y, z = _last_dim_unit(y), _last_dim_unit(z)
+    dout = _last_dim_unit(dout.to(y.dtype))
+    dy = torch.empty_like(y, memory_format=torch.contiguous_format)
+    dz = torch.empty_like(z, memory_format=torch.contiguous_format)
+    a = _gate_args(y, z, dy)
+    a.dout, a.dout_stride = dout.data_ptr(), _s3(dout)
+    a.dz, a.dz_stride = dz.data_ptr(), _s3(dz)
+    with torch.cuda.device(y.device):
+        _lib.check(_lib.lib.ssd_gate_bwd_launch(a, _lib.stream_ptr(y.device)), "ssd_gate_bwd")
+    return dy, dz
+
+
+@_gate_bwd_op.register_fake
+def _(y, z, dout):
+    return (torch.empty_like(y, memory_format=torch.contiguous_format),
+            torch.empty_like(z, memory_format=torch.contiguous_format))
+
+
+def _gate_setup(ctx, inputs, output):
+    ctx.save_for_backward(*inputs)
+
+
+def _gate_backward(ctx, dout):
+    y, z = ctx.saved_tensors
+    return torch.ops.ema_b200.ssd_gate_bwd(y, z, dout)
+
+
+torch.library.register_autograd("ema_b200::ssd_gate_fwd", _gate_backward, setup_context=_gate_setup)
+
+
+def ssd_gate(y: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    """out = y * silu(z) (mamba_chunk_scan_combined's ``z``), fp32 arithmetic rounded once
+    to y's dtype; z is taken in y's dtype (its gradient returns in z's own)."""
+    return torch.ops.ema_b200.ssd_gate_fwd(y, z.to(y.dtype))
 
 
 def _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size):
@@ -299,10 +372,11 @@ def mamba_chunk_scan_combined(x, dt, A, B, C, chunk_size, D=None, z=None, dt_bia
             dt = dt.clamp(dt_min, dt_max)
         out = _ssd_state1(x, dt, A, B, C, D, initial_states, return_final_states, chunk_size)
     else:  # the SSD kernels apply the dt map themselves
-        out = SsdChunkScanFn.apply(x, dt, A, B, C, D, initial_states, return_final_states, dt_bias,
-                                   bool(dt_softplus), (float(dt_limit[0]), float(dt_limit[1])))
+        y, _, fin = torch.ops.ema_b200.ssd_fwd(x, dt, A, B, C, D, initial_states, dt_bias, bool(dt_softplus),
+                                               float(dt_limit[0]), float(dt_limit[1]))
+        out = (y, fin) if return_final_states else y
     if z is None:
         return out
     y, fin = out if return_final_states else (out, None)
-    y = SsdGateFn.apply(y, z)
+    y = ssd_gate(y, z)
     return (y, fin) if return_final_states else y

@@ -198,7 +198,7 @@ def test_gate_kernels_match_float64(dtype, strided):
     """The native gate out = y silu(z) and its gradient (dy, dz) against float64,
     on contiguous tensors (16-byte vector path) and on views with a head stride
     of headdim + 2 (element path)."""
-    from kernels.ssd_combined import SsdGateFn
+    from kernels.ssd_combined import ssd_gate
     rng = np.random.default_rng(31)
     B, L, H, P = 2, 70, 3, 64
     mk = lambda: torch.from_numpy(rng.standard_normal((B, L, H, P + 2)).astype(np.float32) * 2).to(dtype)  # noqa: E731
@@ -208,7 +208,7 @@ def test_gate_kernels_match_float64(dtype, strided):
     y, z = (yb[..., :P], zb[..., :P]) if strided else (yb[..., :P].contiguous(), zb[..., :P].contiguous())
     if not strided:
         dout = dout.contiguous()
-    out = SsdGateFn.apply(y, z)
+    out = ssd_gate(y, z)
     out.backward(dout)
     torch.cuda.synchronize()
     yl_grad, zl_grad = yb.grad[..., :P], zb.grad[..., :P]
