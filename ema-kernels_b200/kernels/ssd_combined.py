@@ -212,9 +212,9 @@ def _ssd_bwd_op(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Ten
     dx, ddt, dA, dB, dC, dD, d_init = ssd_chunk_scan_bwd(x, dt, A, B, C, chunk_states, dy, D, d_final_states,
                                                          need_d_initial, dt_bias=dt_bias, dt_softplus=dt_softplus,
                                                          dt_limit=(dt_min, dt_max), ddt_bias_out=dbias)
-    e = _empty0(x)
-    return (dx, ddt, dA, dB, dC, dD if dD is not None else e, d_init if d_init is not None else e,
-            dbias if dbias is not None else e)
+    # an absent output is its own empty tensor: outputs of an operator may not alias
+    return (dx, ddt, dA, dB, dC, dD if dD is not None else _empty0(x), d_init if d_init is not None else _empty0(x),
+            dbias if dbias is not None else _empty0(x))
 
 
 @_ssd_bwd_op.register_fake
@@ -222,12 +222,11 @@ def _(x, dt, A, B, C, chunk_states, dy, D, d_final_states, need_d_initial, dt_bi
     b_, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
     f32 = torch.float32
-    e = _empty0(x)
     return (torch.empty(b_, L, H, P, dtype=x.dtype, device=x.device), x.new_empty((b_, L, H), dtype=f32),
             x.new_empty((H,), dtype=f32), x.new_empty((b_, L, G, N), dtype=f32),
-            x.new_empty((b_, L, G, N), dtype=f32), x.new_empty((H,), dtype=f32) if D is not None else e,
-            x.new_empty((b_, H, P, N), dtype=f32) if need_d_initial else e,
-            x.new_empty((H,), dtype=f32) if dt_bias is not None else e)
+            x.new_empty((b_, L, G, N), dtype=f32), x.new_empty((H,), dtype=f32) if D is not None else _empty0(x),
+            x.new_empty((b_, H, P, N), dtype=f32) if need_d_initial else _empty0(x),
+            x.new_empty((H,), dtype=f32) if dt_bias is not None else _empty0(x))
 
 
 def _ssd_setup(ctx, inputs, output):

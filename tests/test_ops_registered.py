@@ -82,3 +82,21 @@ def test_ssd_fake_autograd(with_opts):
         assert t.grad is not None and t.grad.shape == t.shape and t.grad.dtype == t.dtype
     if with_opts:
         assert bias.grad.shape == (H,) and z.grad.shape == z.shape
+
+
+def test_absent_outputs_are_distinct_tensors():
+    """Outputs of a dispatcher operator may not alias one another: the optional
+    gradients an SSD backward leaves empty are separate tensors."""
+    m = "meta"
+    B, L, H, P, G, N = 1, 100, 2, 64, 1, 128
+    x = torch.empty(B, L, H, P, dtype=torch.bfloat16, device=m)
+    args = (x, torch.empty(B, L, H, device=m), torch.empty(H, device=m),
+            torch.empty(B, L, G, N, dtype=torch.bfloat16, device=m),
+            torch.empty(B, L, G, N, dtype=torch.bfloat16, device=m),
+            torch.empty(B, 2, H, P, N, device=m), torch.empty_like(x), None, None, False, None, False, 0.0,
+            float("inf"))
+    outs = torch.ops.ema_b200.ssd_bwd(*args)
+    for i in range(len(outs)):
+        for j in range(i + 1, len(outs)):
+            assert outs[i] is not outs[j], (i, j)
+    assert all(o.numel() == 0 for o in outs[5:])
