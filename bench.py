@@ -14,7 +14,8 @@ rows do not divide), no collective on the data path (the per-head dA partials
 would join the model's gradient all-reduce, which this op does not own).
 Extra keys on the same line: ``weak`` (every rank a whole B8 batch),
 ``sp_config4`` (config 4, one B1 L65536 sequence split over the ranks with
-the NCCL state chain, and its error against the single-GPU op) and
+the NCCL state chain, and its error against the single-GPU op; at N > 1 also
+``sp_config4_allgather``, the same with one all_gather per direction) and
 ``ssd_config5`` (config 5, the Mamba-2 SSD at B32 L8192 H80 split by batch
 rows); rank 0 adds ``bench_ema_total``, the reference's own benchmark
 (ema_combined against its d_state-1 mamba_chunk_scan_combined call) on the
@@ -474,11 +475,12 @@ def _max_over_ranks(vals, dev, dist):
     return [float(v) for v in t.tolist()]
 
 
-def _sp_leg(args, rank, world, dev, dist):
+def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
     """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong
-    scaling) through kernels.ema_sp -- state-only pass, NCCL send/recv state
-    chain, local pass, dA all-reduce -- and its largest error against the
-    single-GPU op on the whole sequence (normwise, max over ranks)."""
+    scaling) through kernels.ema_sp -- state-only pass, span exchange (NCCL
+    send/recv state chain, or one all_gather of the span summaries), local
+    pass, dA all-reduce -- and its largest error against the single-GPU op on
+    the whole sequence (normwise, max over ranks)."""
     import torch.distributed as tdist
     from kernels import ema_sp
     from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
@@ -497,8 +499,8 @@ def _sp_leg(args, rank, world, dev, dist):
     xs, dys, dts = (t[:, sl].contiguous() for t in (fx, fdy, fdt))
 
     def step():
-        y, states, _, _ = ema_sp.sp_forward(xs, dts, A, c["Q"])
-        return (y,) + tuple(ema_sp.sp_backward(xs, dts, A, states, dys, c["Q"])[:3])
+        y, states, _, _ = ema_sp.sp_forward(xs, dts, A, c["Q"], exchange=exchange)
+        return (y,) + tuple(ema_sp.sp_backward(xs, dts, A, states, dys, c["Q"], exchange=exchange)[:3])
 
     for _ in range(args.warmup):
         out = step()
@@ -529,7 +531,9 @@ def _sp_leg(args, rank, world, dev, dist):
     return {"metric": "EMA fwd+bwd Mtokens/s, sequence parallel (config 4: B1 L65536 H32 P64 bf16)",
             "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "ms_per_step": ms, "steps": K,
             "scaling": "strong", "span_per_rank": span,
-            "parallelism": f"sequence parallel over {world} GPU(s): NCCL send/recv state chain + dA all-reduce"
+            "parallelism": (f"sequence parallel over {world} GPU(s): "
+                            + ("NCCL send/recv state chain" if exchange == "chain" else
+                               "one NCCL all_gather of the span summaries per direction") + " + dA all-reduce")
                            if world > 1 else "one GPU: the whole sequence, no chain",
             "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
             "max_rel_err_vs_single_gpu": dict(zip(("y", "dx", "ddt", "dA"), errs)),
@@ -783,12 +787,17 @@ def run_ema(args, rank, world, local_rank):
     (e2e_ms,) = _max_over_ranks([e0.elapsed_time(e1) / E], dev, dist)
     del bufs
 
-    sp = ssd5 = total = None
+    sp = sp_ag = ssd5 = total = None
     if not args.no_extra_legs:
         try:
             sp = _sp_leg(args, rank, world, dev, dist)
         except Exception as e:  # a leg's failure is reported, the headline line still prints
             sp = {"unavailable": f"{type(e).__name__}: {e}"}
+        if world > 1:
+            try:
+                sp_ag = _sp_leg(args, rank, world, dev, dist, exchange="allgather")
+            except Exception as e:
+                sp_ag = {"unavailable": f"{type(e).__name__}: {e}"}
         torch.cuda.empty_cache()
         try:
             ssd5 = _ssd5_leg(args, rank, world, dev, dist)
@@ -848,6 +857,8 @@ def run_ema(args, rank, world, local_rank):
             line["weak"] = weak
         if sp is not None:
             line["sp_config4"] = sp
+        if sp_ag is not None:
+            line["sp_config4_allgather"] = sp_ag
         if ssd5 is not None:
             line["ssd_config5"] = ssd5
         if total is not None:

@@ -27,6 +27,13 @@ Messages are (B, H, P) fp32 (8 KB at config 4); the only collective on the
 data path is the per-head dA sum.  Every rank takes the same collective steps
 in the same order.  The local passes are injectable so the host logic can be
 tested on CPU ranks (gloo) against the float64 oracle.
+
+``exchange="allgather"`` replaces each direction's chain of R - 1 dependent
+send/recv hops by one all_gather of every rank's span summary (its end state,
+or start gradient, from a zero boundary, and its decay D); each rank then
+folds the summaries before its span itself -- the same fp32 arithmetic the
+chain performs, without R - 1 message latencies in series.  The default is
+the send/recv chain.
 """
 
 from __future__ import annotations
@@ -44,6 +51,16 @@ __all__ = ["span_decay", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
 def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
     """D = exp(A_h * sum_t dt[b, t, h]) over the local span, (B, H) fp32."""
     return torch.exp(dt.to(torch.float32).sum(dim=1) * A.to(torch.float32))
+
+
+def _gather(v: torch.Tensor, D: torch.Tensor, group):
+    """Every rank's (B, H, P) vector and (B, H) decay: lists indexed by rank."""
+    world = dist.get_world_size(group)
+    msg = torch.cat([v.reshape(-1), D.reshape(-1)]).to(torch.float32).contiguous()
+    parts = [torch.empty_like(msg) for _ in range(world)]
+    dist.all_gather(parts, msg, group=group)
+    n = v.numel()
+    return [p[:n].view(v.shape) for p in parts], [p[n:].view(D.shape) for p in parts]
 
 
 def _peer(group, r):
@@ -69,12 +86,15 @@ def _kernel_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial
 
 
 def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Optional[torch.Tensor] = None,
-               state_fwd: Callable = _kernel_state_fwd, local_fwd: Callable = _kernel_fwd):
+               state_fwd: Callable = _kernel_state_fwd, local_fwd: Callable = _kernel_fwd,
+               exchange: str = "chain"):
     """Sequence-parallel forward of this rank's span.
 
     Returns (y, chunk_start_states, Sin, final): ``Sin`` is the state entering
     this span (saved for the backward), ``final`` this span's end state (the
-    sequence's final state on the last rank)."""
+    sequence's final state on the last rank).  ``exchange``: "chain" (NCCL
+    send/recv r -> r+1) or "allgather" (one all_gather of the span summaries)."""
+    assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, _, H, P = x.shape
     if world == 1:  # one span: no chain, no state-only pass
@@ -83,6 +103,20 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
         y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
         return y, states, Sin, final
     S_loc = state_fwd(x, dt, A, chunk_size)
+    if exchange == "allgather":
+        D = span_decay(dt, A)
+        if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
+            S_loc = D[..., None] * initial_states.to(torch.float32) + S_loc
+        Ss, Ds = _gather(S_loc, D, group)
+        if rank == 0:
+            Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
+                   else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+        else:
+            Sin = Ss[0].clone()
+            for q in range(1, rank):
+                Sin = Ds[q][..., None] * Sin + Ss[q]
+        y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
+        return y, states, Sin, final
     if rank == 0:
         Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
@@ -98,23 +132,38 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
 
 def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
                 d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False,
-                state_bwd: Callable = _kernel_state_bwd, local_bwd: Callable = _kernel_bwd):
+                state_bwd: Callable = _kernel_state_bwd, local_bwd: Callable = _kernel_bwd,
+                exchange: str = "chain"):
     """Sequence-parallel backward of this rank's span.
 
     ``states`` are the chunk start states of this span's forward (which
     started from its true incoming state).  Returns (dx, ddt, dA, d_initial):
     dA is summed over the group; d_initial (rank 0, when asked) is the
-    gradient w.r.t. the sequence's initial state."""
+    gradient w.r.t. the sequence's initial state.  ``exchange`` as in
+    :func:`sp_forward`, the chain running r+1 -> r."""
+    assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, _, H, P = x.shape
     G_loc = state_bwd(x, dt, A, states, dy, chunk_size) if world > 1 else None
-    if rank == world - 1:
+    if world > 1 and exchange == "allgather":
+        D = span_decay(dt, A)
+        if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient
+            G_loc = D[..., None] * d_final_states.to(torch.float32) + G_loc
+        Gs, Ds = _gather(G_loc, D, group)
+        if rank == world - 1:
+            Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
+                   else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+        else:
+            Gin = Gs[world - 1].clone()
+            for q in range(world - 2, rank, -1):
+                Gin = Ds[q][..., None] * Gin + Gs[q]
+    elif rank == world - 1:
         Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
     else:
         Gin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
         dist.recv(Gin, src=_peer(group, rank + 1), group=group)
-    if rank > 0:
+    if rank > 0 and exchange == "chain":
         Gout = span_decay(dt, A)[..., None] * Gin + G_loc
         dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
     dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial and rank == 0)
@@ -126,20 +175,23 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
 
 class _EmaChunkScanSPFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, dt, A, chunk_size, group):
-        y, states, _, _ = sp_forward(x, dt, A, chunk_size, group)
+    def forward(ctx, x, dt, A, chunk_size, group, exchange):
+        y, states, _, _ = sp_forward(x, dt, A, chunk_size, group, exchange=exchange)
         ctx.save_for_backward(x, dt, A, states)
-        ctx.chunk_size, ctx.group = chunk_size, group
+        ctx.chunk_size, ctx.group, ctx.exchange = chunk_size, group, exchange
         ctx.dt_dtype, ctx.A_dtype = dt.dtype, A.dtype
         return y
 
     @staticmethod
     def backward(ctx, dy):
         x, dt, A, states = ctx.saved_tensors
-        dx, ddt, dA, _ = sp_backward(x, dt, A, states, dy.contiguous(), ctx.chunk_size, ctx.group)
-        return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, None
+        dx, ddt, dA, _ = sp_backward(x, dt, A, states, dy.contiguous(), ctx.chunk_size, ctx.group,
+                                     exchange=ctx.exchange)
+        return dx, ddt.to(ctx.dt_dtype), dA.to(ctx.A_dtype), None, None, None
 
 
-def ema_chunk_scan_sp(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256, group=None):
-    """Autograd op over this rank's span of a sequence split across ``group``."""
-    return _EmaChunkScanSPFn.apply(x, dt, A, chunk_size, group)
+def ema_chunk_scan_sp(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256, group=None,
+                      exchange: str = "chain"):
+    """Autograd op over this rank's span of a sequence split across ``group``;
+    ``exchange``: "chain" (NCCL send/recv between neighbours) or "allgather"."""
+    return _EmaChunkScanSPFn.apply(x, dt, A, chunk_size, group, exchange)

@@ -3,7 +3,8 @@
 Each rank owns one span of the sequence; the local passes are the float64
 oracle instead of the CUDA kernels, so what is tested is the span chaining
 (send/recv order, the span decay, the incoming state and the gradient at the
-span end) and the dA all-reduce.  The spans' results must equal the oracle on
+span end -- through the send/recv chain and through one all_gather of the span
+summaries) and the dA all-reduce.  The spans' results must equal the oracle on
 the whole sequence up to the fp32 rounding of the exchanged (B, H, P) states.
 """
 
@@ -57,7 +58,7 @@ def _local_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial)
     return torch.from_numpy(r["dx"]), torch.from_numpy(r["ddt"]), torch.from_numpy(r["dA"]), d_init
 
 
-def _worker(rank, world, port, with_init, errq):
+def _worker(rank, world, port, with_init, exchange, errq):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -79,7 +80,7 @@ def _worker(rank, world, port, with_init, errq):
         tA = torch.from_numpy(A)
         tinit = torch.from_numpy(init) if init is not None else None
         y, states, Sin, final = ema_sp.sp_forward(tx, tdt, tA, Q, initial_states=tinit,
-                                                  state_fwd=_state_fwd, local_fwd=_local_fwd)
+                                                  state_fwd=_state_fwd, local_fwd=_local_fwd, exchange=exchange)
         np.testing.assert_allclose(_np(y), full_f["y"][:, sl], rtol=1e-5, atol=1e-6)
         if rank == world - 1:
             np.testing.assert_allclose(_np(final), full_f["final_state"], rtol=1e-5, atol=1e-6)
@@ -87,7 +88,7 @@ def _worker(rank, world, port, with_init, errq):
         tdfin = torch.from_numpy(dfin) if dfin is not None else None
         dx, ddt, dA, d_init = ema_sp.sp_backward(tx, tdt, tA, states, tdy, Q, d_final_states=tdfin,
                                                  need_d_initial=True, state_bwd=_state_bwd,
-                                                 local_bwd=_local_bwd)
+                                                 local_bwd=_local_bwd, exchange=exchange)
         np.testing.assert_allclose(_np(dx), full_b["dx"][:, sl], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(_np(ddt), full_b["ddt"][:, sl], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(_np(dA), full_b["dA"], rtol=1e-5, atol=1e-6)
@@ -102,11 +103,12 @@ def _worker(rank, world, port, with_init, errq):
         raise
 
 
-@pytest.mark.parametrize("world,with_init", [(2, False), (3, True)])
-def test_sequence_parallel_matches_whole_sequence(world, with_init):
+@pytest.mark.parametrize("world,with_init,exchange", [(2, False, "chain"), (3, True, "chain"),
+                                                      (3, True, "allgather"), (4, False, "allgather")])
+def test_sequence_parallel_matches_whole_sequence(world, with_init, exchange):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.start_processes(_worker, args=(world, _free_port(), with_init, errq), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), with_init, exchange, errq), nprocs=world, join=True,
                        start_method="spawn")
     assert errq.empty(), errq.get()
 
