@@ -732,17 +732,15 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     }
     fence_mbar_init();
   }
+  __syncthreads();  // barriers initialised (under programmatic launch this overlaps the previous kernel)
   grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
   grid_dep_release();
-  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  const uint32_t tag = epoch + 1u;
   const int BH = p.B * p.H;
   const int total = BH * p.nc;
 
   if (warp == NW) {
     // ------------------------------ producer ------------------------------
+    // (needs no epoch: its first ticket round trip overlaps the epoch read below)
     if (lane == 0) tma_prefetch_desc(&tm_x);
     producer_loop<S>(full, empty, tid_full, s_tile, ws.hdr, total, lane, [&](int s, int ticket) {
       const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
@@ -774,6 +772,11 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     });
     return;
   }
+  // the look-back and compute warps tag their records with the launch epoch
+  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
+  named_sync(2, NC + 32);  // every warp but the producer
+  const uint32_t epoch = s_epoch;
+  const uint32_t tag = epoch + 1u;
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
     lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Sin2, status, lane,
@@ -1148,17 +1151,15 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     }
     fence_mbar_init();
   }
+  __syncthreads();  // barriers initialised (under programmatic launch this overlaps the previous kernel)
   grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
   grid_dep_release();
-  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  const uint32_t tag = epoch + 1u;
   const int BH = p.B * p.H;
   const int total = BH * p.nc;
 
   if (warp == NW) {
     // ------------------------------ producer ------------------------------
+    // (needs no epoch: its first ticket round trip overlaps the epoch read below)
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_dy);
@@ -1208,6 +1209,11 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     });
     return;
   }
+  // the look-back and compute warps tag their records with the launch epoch
+  if (tid == 0) s_epoch = ld_volatile_u32(&ws.hdr[kHdrEpoch]) & kEpochMask;
+  named_sync(2, NC + 32);  // every warp but the producer
+  const uint32_t epoch = s_epoch;
+  const uint32_t tag = epoch + 1u;
   if (warp == NW + 1) {
     // ------------------------------ look-back ------------------------------
     lookback_loop<S, BP>(tid_full, s_tile, empty, vec_full, vec_empty, s_Gn2, status, lane,
