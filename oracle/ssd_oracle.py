@@ -3,8 +3,9 @@
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
 CPU legs of bench.py, never by the product path.
 
-Parity status: UNPINNED.  The reference does not implement SSD itself; its
-benchmark calls the third-party ``mamba_ssm`` package
+Parity status: pinned through the d_state-1 reduction, otherwise unpinned.
+The reference does not implement SSD itself; its benchmark calls the
+third-party ``mamba_ssm`` package
 (``mamba_ssm.ops.triton.ssd_combined.mamba_chunk_scan_combined``, imported at
 kernels/benchmarks/bench_ema_total.py:18 and called at :72-76 as
 ``(x, dt, A, B, C, chunk_size, seq_idx=None)``), which has no pinned version
@@ -20,7 +21,12 @@ d_state), D (nheads,) and states (batch, nheads, headdim, d_state) -- the
 layouts of ``mamba_chunk_scan_combined``.  The backward is the exact adjoint
 of the recurrence (back-propagation through the sequence), cross-checked in
 tests/test_ssd_oracle.py against torch autograd of the same recurrence and
-against finite differences.
+against finite differences.  With d_state 1, A = -1, dt = -ln(2) dA, B = 1 / dt
+(one group per head) and C = 1 the recurrence is the reference's own EMA
+(kernels/forward/ema_ssd_fwd.py:258-259), so tests/test_ssd_oracle_pinned.py
+checks this file, forward and backward, sequential and chunked, against the
+golden vectors of the reference's kernels; the d_state > 1 contractions and
+dB / dC are beyond that reduction.
 """
 
 from __future__ import annotations
