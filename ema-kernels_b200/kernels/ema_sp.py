@@ -54,13 +54,27 @@ def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
 
 
 def _gather(v: torch.Tensor, D: torch.Tensor, group):
-    """Every rank's (B, H, P) vector and (B, H) decay: lists indexed by rank."""
+    """Every rank's (B, H, P) vector and (B, H) decay, stacked by rank: one
+    all_gather into a flat buffer."""
     world = dist.get_world_size(group)
     msg = torch.cat([v.reshape(-1), D.reshape(-1)]).to(torch.float32).contiguous()
-    parts = [torch.empty_like(msg) for _ in range(world)]
-    dist.all_gather(parts, msg, group=group)
+    out = torch.empty(world * msg.numel(), dtype=torch.float32, device=msg.device)
+    dist.all_gather_into_tensor(out, msg, group=group)
+    out = out.view(world, -1)
     n = v.numel()
-    return [p[:n].view(v.shape) for p in parts], [p[n:].view(D.shape) for p in parts]
+    return out[:, :n].view(world, *v.shape), out[:, n:].view(world, *D.shape)
+
+
+def _fold(V: torch.Tensor, D: torch.Tensor) -> torch.Tensor:
+    """sum_q (prod_{j > q} D_j) V_q over the stacked summaries V (n, B, H, P) and
+    decays D (n, B, H): the chain's recurrence s <- D_q s + V_q from s = 0
+    (without the last decay), in a fixed number of launches."""
+    n = V.shape[0]
+    if n == 1:
+        return V[0].clone()
+    # w_q = D_{q+1} ... D_{n-1}, w_{n-1} = 1
+    w = torch.cat([torch.cumprod(D[1:].flip(0), dim=0).flip(0), torch.ones_like(D[:1])], dim=0)
+    return (w[..., None] * V).sum(dim=0)
 
 
 def _peer(group, r):
@@ -111,10 +125,8 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
         if rank == 0:
             Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
-        else:
-            Sin = Ss[0].clone()
-            for q in range(1, rank):
-                Sin = Ds[q][..., None] * Sin + Ss[q]
+        else:  # the spans before this one, folded in order
+            Sin = _fold(Ss[:rank], Ds[:rank])
         y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
         return y, states, Sin, final
     if rank == 0:
@@ -153,10 +165,8 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
         if rank == world - 1:
             Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
-        else:
-            Gin = Gs[world - 1].clone()
-            for q in range(world - 2, rank, -1):
-                Gin = Ds[q][..., None] * Gin + Gs[q]
+        else:  # the spans after this one, folded from the last backwards
+            Gin = _fold(Gs[rank + 1:].flip(0), Ds[rank + 1:].flip(0))
     elif rank == world - 1:
         Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
