@@ -45,7 +45,7 @@ import torch.distributed as dist
 
 from .ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
 
-__all__ = ["span_decay", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
+__all__ = ["span_decay", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
 
 
 def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
@@ -99,26 +99,71 @@ def _kernel_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial
                               need_d_initial=need_d_initial)
 
 
+def subspan_count(batch: int, nheads: int, span: int, chunk_size: int, target_chains: int = 256) -> int:
+    """Sub-spans a rank cuts its span into: the largest power of two K with
+    batch * nheads * K <= target_chains chains, span % K == 0 and at least one
+    chunk per sub-span (config 4 over 2..8 ranks: K = 8, 256 chains)."""
+    K = 1
+    while (batch * nheads * 2 * K <= target_chains and span % (2 * K) == 0
+           and span // (2 * K) >= chunk_size):
+        K *= 2
+    return K
+
+
+def _rows(t: torch.Tensor, K: int) -> torch.Tensor:
+    """(B, L, ...) -> (B K, L / K, ...): sub-span k of batch row b becomes row b K + k."""
+    B, L = t.shape[:2]
+    return t.reshape(B * K, L // K, *t.shape[2:])
+
+
+def _log_decays(dt_rows: torch.Tensor, A: torch.Tensor, B: int, K: int) -> torch.Tensor:
+    """A_h * (sum of dt over each sub-span), (B, K, H) float64: the log of its
+    decay.  The folds over sub-spans run in float64 on these few (B, K, H, P)
+    values, so exponentials of long cumulative sums add no fp32 rounding."""
+    return (dt_rows.to(torch.float64).sum(dim=1) * A.to(torch.float64)).view(B, K, -1)
+
+
+def _mask_exp(e: torch.Tensor, keep: torch.Tensor) -> torch.Tensor:
+    return torch.exp(torch.where(keep, e, torch.full_like(e, float("-inf"))))
+
+
 def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Optional[torch.Tensor] = None,
                state_fwd: Callable = _kernel_state_fwd, local_fwd: Callable = _kernel_fwd,
-               exchange: str = "chain"):
+               exchange: str = "chain", subspans: Optional[int] = None):
     """Sequence-parallel forward of this rank's span.
 
-    Returns (y, chunk_start_states, Sin, final): ``Sin`` is the state entering
-    this span (saved for the backward), ``final`` this span's end state (the
-    sequence's final state on the last rank).  ``exchange``: "chain" (NCCL
-    send/recv r -> r+1) or "allgather" (one all_gather of the span summaries)."""
+    The span is cut into K sub-spans run as extra batch rows (``subspans``;
+    default :func:`subspan_count`), so both passes -- the state-only pass and
+    the full pass -- run on K times more, K times shorter chains.  The
+    sub-spans' end states from zero and decays fold (in log space, exactly) into
+    the span's summary for the exchange, and the state entering the span into
+    each sub-span's incoming state for the full pass.
+
+    Returns (y, chunk_start_states, Sin, final): y in x's layout;
+    ``chunk_start_states`` of the sub-span rows (B K, nchunks, H, P), what
+    :func:`sp_backward` takes; ``Sin`` the state entering this span; ``final``
+    this span's end state (the sequence's final state on the last rank).
+    ``exchange``: "chain" (NCCL send/recv r -> r+1) or "allgather" (one
+    all_gather of the span summaries)."""
     assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
-    B, _, H, P = x.shape
-    if world == 1:  # one span: no chain, no state-only pass
+    B, Ls, H, P = x.shape
+    if world == 1:  # one span: no exchange, no state-only pass
         init = None if initial_states is None else initial_states.to(torch.float32)
         Sin = init if init is not None else torch.zeros(B, H, P, dtype=torch.float32, device=x.device)
         y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
         return y, states, Sin, final
-    S_loc = state_fwd(x, dt, A, chunk_size)
+    K = subspans if subspans is not None else subspan_count(B, H, Ls, chunk_size)
+    assert Ls % K == 0, "the span length must be a multiple of the sub-span count"
+    xr, dtr = _rows(x, K), _rows(dt, K)
+    # sub-span summaries: end state from zero S_k, log decay ld_k; cl_k = sum_{j<k} ld_j
+    S = state_fwd(xr, dtr, A, chunk_size).to(torch.float64).view(B, K, H, P)
+    ld = _log_decays(dtr, A, B, K)
+    cl = torch.cumsum(ld, dim=1) - ld
+    tot = cl[:, -1] + ld[:, -1]
+    S_loc = (torch.exp(tot[:, None] - cl - ld)[..., None] * S).sum(dim=1).to(torch.float32)  # span end state from 0
+    D = torch.exp(tot).to(torch.float32)
     if exchange == "allgather":
-        D = span_decay(dt, A)
         if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
             S_loc = D[..., None] * initial_states.to(torch.float32) + S_loc
         Ss, Ds = _gather(S_loc, D, group)
@@ -127,19 +172,22 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
         else:  # the spans before this one, folded in order
             Sin = _fold(Ss[:rank], Ds[:rank])
-        y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
-        return y, states, Sin, final
-    if rank == 0:
-        Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
-               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
     else:
-        Sin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
-        dist.recv(Sin, src=_peer(group, rank - 1), group=group)
-    if rank + 1 < world:
-        Sout = span_decay(dt, A)[..., None] * Sin + S_loc
-        dist.send(Sout.to(torch.float32).contiguous(), dst=_peer(group, rank + 1), group=group)
-    y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
-    return y, states, Sin, final
+        if rank == 0:
+            Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
+                   else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+        else:
+            Sin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
+            dist.recv(Sin, src=_peer(group, rank - 1), group=group)
+        if rank + 1 < world:
+            Sout = D[..., None] * Sin + S_loc
+            dist.send(Sout.to(torch.float32).contiguous(), dst=_peer(group, rank + 1), group=group)
+    # state entering sub-span k: exp(cl_k) Sin + sum_{q<k} exp(cl_k - cl_q - ld_q) S_q
+    k_idx = torch.arange(K, device=x.device)
+    W = _mask_exp(cl[:, :, None, :] - (cl + ld)[:, None, :, :], (k_idx[:, None] > k_idx[None, :])[None, :, :, None])
+    init = torch.exp(cl)[..., None] * Sin.to(torch.float64)[:, None] + torch.einsum("bkqh,bqhp->bkhp", W, S)
+    y, states, final = local_fwd(xr, dtr, A, chunk_size, init.reshape(B * K, H, P).to(torch.float32))
+    return y.reshape(B, Ls, H, P), states, Sin, final.reshape(B, K, H, P)[:, -1]
 
 
 def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
@@ -148,17 +196,30 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
                 exchange: str = "chain"):
     """Sequence-parallel backward of this rank's span.
 
-    ``states`` are the chunk start states of this span's forward (which
-    started from its true incoming state).  Returns (dx, ddt, dA, d_initial):
-    dA is summed over the group; d_initial (rank 0, when asked) is the
-    gradient w.r.t. the sequence's initial state.  ``exchange`` as in
-    :func:`sp_forward`, the chain running r+1 -> r."""
+    ``states`` are the sub-span rows' chunk start states from
+    :func:`sp_forward` (which started every sub-span from its true incoming
+    state); the sub-span count is read off their shape.  Returns (dx, ddt, dA,
+    d_initial): dx and ddt in x's and dt's layouts; dA summed over the group;
+    d_initial (rank 0, when asked) the gradient w.r.t. the sequence's initial
+    state.  ``exchange`` as in :func:`sp_forward`, running r+1 -> r."""
     assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
-    B, _, H, P = x.shape
-    G_loc = state_bwd(x, dt, A, states, dy, chunk_size) if world > 1 else None
-    if world > 1 and exchange == "allgather":
-        D = span_decay(dt, A)
+    B, Ls, H, P = x.shape
+    if world == 1:
+        Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
+               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+        dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial)
+        return dx, ddt, dA.to(torch.float32).contiguous(), d_init
+    K = states.shape[0] // B
+    xr, dtr, dyr = _rows(x, K), _rows(dt, K), _rows(dy, K)
+    # sub-span summaries: gradient w.r.t. the sub-span's start from its own dy (nothing arriving)
+    G = state_bwd(xr, dtr, A, states, dyr, chunk_size).to(torch.float64).view(B, K, H, P)
+    ld = _log_decays(dtr, A, B, K)
+    cl = torch.cumsum(ld, dim=1) - ld
+    tot = cl[:, -1] + ld[:, -1]
+    G_loc = (torch.exp(cl)[..., None] * G).sum(dim=1).to(torch.float32)  # span start gradient from its own dy
+    D = torch.exp(tot).to(torch.float32)
+    if exchange == "allgather":
         if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient
             G_loc = D[..., None] * d_final_states.to(torch.float32) + G_loc
         Gs, Ds = _gather(G_loc, D, group)
@@ -167,20 +228,29 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
         else:  # the spans after this one, folded from the last backwards
             Gin = _fold(Gs[rank + 1:].flip(0), Ds[rank + 1:].flip(0))
-    elif rank == world - 1:
-        Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
-               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
     else:
-        Gin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
-        dist.recv(Gin, src=_peer(group, rank + 1), group=group)
-    if rank > 0 and exchange == "chain":
-        Gout = span_decay(dt, A)[..., None] * Gin + G_loc
-        dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
-    dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial and rank == 0)
+        if rank == world - 1:
+            Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
+                   else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+        else:
+            Gin = torch.empty(B, H, P, dtype=torch.float32, device=x.device)
+            dist.recv(Gin, src=_peer(group, rank + 1), group=group)
+        if rank > 0:
+            Gout = D[..., None] * Gin + G_loc
+            dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
+    # gradient arriving at the end of sub-span k:
+    #   exp(tot - cl_k - ld_k) Gin + sum_{q>k} exp(cl_q - cl_k - ld_k) G_q
+    k_idx = torch.arange(K, device=x.device)
+    W = _mask_exp(cl[:, None, :, :] - (cl + ld)[:, :, None, :], (k_idx[None, :] > k_idx[:, None])[None, :, :, None])
+    dfin = (torch.exp(tot[:, None] - cl - ld)[..., None] * Gin.to(torch.float64)[:, None]
+            + torch.einsum("bkqh,bqhp->bkhp", W, G))
+    dx, ddt, dA, d_init = local_bwd(xr, dtr, A, states, dyr, chunk_size, dfin.reshape(B * K, H, P).to(torch.float32),
+                                    need_d_initial and rank == 0)
     dA = dA.to(torch.float32).contiguous()
-    if world > 1:
-        dist.all_reduce(dA, group=group)
-    return dx, ddt, dA, d_init
+    dist.all_reduce(dA, group=group)
+    if d_init is not None:
+        d_init = d_init.reshape(B, K, H, P)[:, 0]
+    return dx.reshape(B, Ls, H, P), ddt.reshape(B, Ls, H), dA, d_init
 
 
 class _EmaChunkScanSPFn(torch.autograd.Function):

@@ -1,7 +1,8 @@
 """Sequence-parallel host logic (kernels/ema_sp.py) on CPU ranks over gloo.
 
-Each rank owns one span of the sequence; the local passes are the float64
-oracle instead of the CUDA kernels, so what is tested is the span chaining
+Each rank owns one span of the sequence, cut into sub-spans run as batch rows;
+the local passes are the float64 oracle instead of the CUDA kernels, so what
+is tested is the sub-span folds, the span chaining
 (send/recv order, the span decay, the incoming state and the gradient at the
 span end -- through the send/recv chain and through one all_gather of the span
 summaries) and the dA all-reduce.  The spans' results must equal the oracle on
@@ -58,7 +59,7 @@ def _local_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial)
     return torch.from_numpy(r["dx"]), torch.from_numpy(r["ddt"]), torch.from_numpy(r["dA"]), d_init
 
 
-def _worker(rank, world, port, with_init, exchange, errq):
+def _worker(rank, world, port, with_init, exchange, subspans, errq):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -80,7 +81,8 @@ def _worker(rank, world, port, with_init, exchange, errq):
         tA = torch.from_numpy(A)
         tinit = torch.from_numpy(init) if init is not None else None
         y, states, Sin, final = ema_sp.sp_forward(tx, tdt, tA, Q, initial_states=tinit,
-                                                  state_fwd=_state_fwd, local_fwd=_local_fwd, exchange=exchange)
+                                                  state_fwd=_state_fwd, local_fwd=_local_fwd, exchange=exchange,
+                                                  subspans=subspans)
         np.testing.assert_allclose(_np(y), full_f["y"][:, sl], rtol=1e-5, atol=1e-6)
         if rank == world - 1:
             np.testing.assert_allclose(_np(final), full_f["final_state"], rtol=1e-5, atol=1e-6)
@@ -103,12 +105,15 @@ def _worker(rank, world, port, with_init, exchange, errq):
         raise
 
 
-@pytest.mark.parametrize("world,with_init,exchange", [(2, False, "chain"), (3, True, "chain"),
-                                                      (3, True, "allgather"), (4, False, "allgather")])
-def test_sequence_parallel_matches_whole_sequence(world, with_init, exchange):
+# subspans: None = the automatic choice (here 2 or 1 sub-spans per rank's span)
+@pytest.mark.parametrize("world,with_init,exchange,subspans", [
+    (2, False, "chain", None), (3, True, "chain", None), (3, True, "allgather", None), (4, False, "allgather", None),
+    (2, True, "chain", 4), (3, True, "allgather", 2), (2, True, "allgather", 3)])
+def test_sequence_parallel_matches_whole_sequence(world, with_init, exchange, subspans):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.start_processes(_worker, args=(world, _free_port(), with_init, exchange, errq), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), with_init, exchange, subspans, errq), nprocs=world,
+                       join=True,
                        start_method="spawn")
     assert errq.empty(), errq.get()
 
