@@ -369,7 +369,8 @@ def run_sp(args, rank, world, local_rank):
             "config": {"workload": "EMA dt-form fwd+bwd, one sequence split over the ranks", **c,
                        "span_per_rank": span, "parallelism": f"sequence parallel over {world} GPU(s), "
                        "NCCL send/recv state chain + dA all-reduce",
-                       "timing": "eager calls, CUDA events around K steps, max over ranks"},
+                       "timing": "one CUDA graph per step (kernels, sub-span folds, NCCL calls), L2 flushed before each replay "
+                      "outside the timed interval, CUDA events around each replay, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
                          "frac": gbs / world / peak,
                          "note": "per-GPU algorithmic bytes of one fwd+bwd (the state-only passes "
@@ -477,10 +478,11 @@ def _max_over_ranks(vals, dev, dist):
 
 def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
     """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong
-    scaling) through kernels.ema_sp -- state-only pass, span exchange (NCCL
-    send/recv state chain, or one all_gather of the span summaries), local
-    pass, dA all-reduce -- and its largest error against the single-GPU op on
-    the whole sequence (normwise, max over ranks)."""
+    scaling) through kernels.ema_sp -- each rank's span cut into sub-spans run
+    as batch rows: state-only pass, sub-span fold, span exchange (NCCL send/recv
+    state chain, or one all_gather of the span summaries), local pass, dA
+    all-reduce -- and its largest error against the single-GPU op on the whole
+    sequence (normwise, max over ranks)."""
     import torch.distributed as tdist
     from kernels import ema_sp
     from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
@@ -502,20 +504,36 @@ def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
         y, states, _, _ = ema_sp.sp_forward(xs, dts, A, c["Q"], exchange=exchange)
         return (y,) + tuple(ema_sp.sp_backward(xs, dts, A, states, dys, c["Q"], exchange=exchange)[:3])
 
-    for _ in range(args.warmup):
-        out = step()
-    torch.cuda.synchronize()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
     K = max(1, min(args.steps, 50))
-    if world > 1:
-        dist.barrier()
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(K):
-        out = step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / K
+    ms = 0.0
+    with torch.cuda.stream(side):
+        for _ in range(args.warmup):  # eager warm-up: communicators, workspaces
+            out = step()
+        side.synchronize()
+        if world > 1:
+            dist.barrier()
+        g = torch.cuda.CUDAGraph()  # the step's kernels, sub-span folds and NCCL calls, replayed as one graph
+        with torch.cuda.graph(g, stream=side):
+            out = step()
+        for _ in range(3):
+            g.replay()
+        side.synchronize()
+        if world > 1:
+            dist.barrier()
+        for _ in range(K):
+            flush.zero_()  # the L2, outside the timed interval
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(side)
+            g.replay()
+            e1.record(side)
+            e1.synchronize()
+            ms += e0.elapsed_time(e1)
+        ms /= K
+    torch.cuda.current_stream(dev).wait_stream(side)
+    del g  # (a graph holding NCCL calls is released before the process group)
     # the single-GPU op on the whole sequence, this rank's span compared
     yr, st, _ = ema_chunk_scan_fwd(fx, fdt, A, c["Q"])
     dxr, ddtr, dAr, _ = ema_chunk_scan_bwd(fx, fdt, A, st, fdy, c["Q"])
@@ -537,7 +555,8 @@ def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
                            if world > 1 else "one GPU: the whole sequence, no chain",
             "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
             "max_rel_err_vs_single_gpu": dict(zip(("y", "dx", "ddt", "dA"), errs)),
-            "timing": "eager calls, CUDA events around K steps, max over ranks"}
+            "timing": "one CUDA graph per step (kernels, sub-span folds, NCCL calls), L2 flushed before each replay "
+                      "outside the timed interval, CUDA events around each replay, max over ranks"}
 
 
 SSD5_CFG = dict(B=32, L=8192, H=80, P=64, N=128, G=1)

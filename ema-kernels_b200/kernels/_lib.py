@@ -118,6 +118,14 @@ class SsdGateArgs(ctypes.Structure):
     ]
 
 
+class EmaSpanFoldArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("subspans", _i64), ("nheads", _i64), ("headdim", _i64),
+        ("direction", _i32), ("reserved", _i32),
+        ("log_decay", _ptr), ("values", _ptr), ("boundary", _ptr), ("out", _ptr), ("span_decay", _ptr),
+    ]
+
+
 lib.ema_scan_workspace_size.restype = ctypes.c_size_t
 lib.ema_scan_workspace_size.argtypes = [_i64] * 5
 lib.ema_fwd_launch.restype = ctypes.c_int
@@ -145,6 +153,10 @@ lib.ssd_gate_fwd_launch.restype = ctypes.c_int
 lib.ssd_gate_fwd_launch.argtypes = [ctypes.POINTER(SsdGateArgs), _ptr]
 lib.ssd_gate_bwd_launch.restype = ctypes.c_int
 lib.ssd_gate_bwd_launch.argtypes = [ctypes.POINTER(SsdGateArgs), _ptr]
+lib.ema_span_summary.restype = ctypes.c_int
+lib.ema_span_summary.argtypes = [ctypes.POINTER(EmaSpanFoldArgs), _ptr]
+lib.ema_span_expand.restype = ctypes.c_int
+lib.ema_span_expand.argtypes = [ctypes.POINTER(EmaSpanFoldArgs), _ptr]
 lib.ssd_device_status.restype = ctypes.c_int
 lib.ssd_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p

@@ -43,7 +43,8 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+from . import _lib
+from .ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
 
 __all__ = ["span_decay", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
 
@@ -87,16 +88,43 @@ def _kernel_state_fwd(x, dt, A, chunk_size):
 
 
 def _kernel_fwd(x, dt, A, chunk_size, initial_states):
-    return ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states, return_final_states=True)
+    # the autograd op's pair: 256-token forward tiles hand the backward 128-token chunk states
+    return ema_chunk_scan_fwd(x, dt, A, chunk_size, initial_states=initial_states, return_final_states=True,
+                              half_chunk_states=backward_chunk(chunk_size) != chunk_size)
 
 
 def _kernel_state_bwd(x, dt, A, states, dy, chunk_size):
-    return ema_chunk_scan_bwd(x, dt, A, states, dy, chunk_size, state_only=True)[3]
+    return ema_chunk_scan_bwd(x, dt, A, states, dy, backward_chunk(chunk_size), state_only=True)[3]
 
 
 def _kernel_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial):
-    return ema_chunk_scan_bwd(x, dt, A, states, dy, chunk_size, d_final_states=d_final_states,
+    return ema_chunk_scan_bwd(x, dt, A, states, dy, backward_chunk(chunk_size), d_final_states=d_final_states,
                               need_d_initial=need_d_initial)
+
+
+def _kernel_fold(direction: int, expand: bool, ld: torch.Tensor, V: torch.Tensor,
+                 boundary: Optional[torch.Tensor] = None):
+    """The sub-span folds on the GPU (ema_span_summary / ema_span_expand).
+    ld (B, K, H) float64, V (B K, H, P) float32.  Summary: (span value (B, H, P),
+    span decay (B, H)); expansion (``boundary`` (B, H, P)): (B K, H, P)."""
+    B, K, H = ld.shape
+    P = V.shape[-1]
+    ld, V = ld.contiguous(), V.to(torch.float32).contiguous()
+    a = _lib.EmaSpanFoldArgs()
+    a.batch, a.subspans, a.nheads, a.headdim, a.direction = B, K, H, P, direction
+    a.log_decay, a.values = ld.data_ptr(), V.data_ptr()
+    with torch.cuda.device(V.device):
+        if expand:
+            bnd = boundary.to(torch.float32).contiguous()
+            out = torch.empty(B * K, H, P, dtype=torch.float32, device=V.device)
+            a.boundary, a.out = bnd.data_ptr(), out.data_ptr()
+            _lib.check(_lib.lib.ema_span_expand(a, _lib.stream_ptr(V.device)), "ema_span_expand")
+            return out
+        out = torch.empty(B, H, P, dtype=torch.float32, device=V.device)
+        dspan = torch.empty(B, H, dtype=torch.float32, device=V.device)
+        a.out, a.span_decay = out.data_ptr(), dspan.data_ptr()
+        _lib.check(_lib.lib.ema_span_summary(a, _lib.stream_ptr(V.device)), "ema_span_summary")
+        return out, dspan
 
 
 def subspan_count(batch: int, nheads: int, span: int, chunk_size: int, target_chains: int = 256) -> int:
@@ -120,24 +148,21 @@ def _log_decays(dt_rows: torch.Tensor, A: torch.Tensor, B: int, K: int) -> torch
     """A_h * (sum of dt over each sub-span), (B, K, H) float64: the log of its
     decay.  The folds over sub-spans run in float64 on these few (B, K, H, P)
     values, so exponentials of long cumulative sums add no fp32 rounding."""
-    return (dt_rows.to(torch.float64).sum(dim=1) * A.to(torch.float64)).view(B, K, -1)
-
-
-def _mask_exp(e: torch.Tensor, keep: torch.Tensor) -> torch.Tensor:
-    return torch.exp(torch.where(keep, e, torch.full_like(e, float("-inf"))))
+    return (dt_rows.sum(dim=1, dtype=torch.float64) * A.to(torch.float64)).view(B, K, -1)
 
 
 def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Optional[torch.Tensor] = None,
                state_fwd: Callable = _kernel_state_fwd, local_fwd: Callable = _kernel_fwd,
-               exchange: str = "chain", subspans: Optional[int] = None):
+               exchange: str = "chain", subspans: Optional[int] = None, fold: Callable = _kernel_fold):
     """Sequence-parallel forward of this rank's span.
 
     The span is cut into K sub-spans run as extra batch rows (``subspans``;
     default :func:`subspan_count`), so both passes -- the state-only pass and
     the full pass -- run on K times more, K times shorter chains.  The
-    sub-spans' end states from zero and decays fold (in log space, exactly) into
-    the span's summary for the exchange, and the state entering the span into
-    each sub-span's incoming state for the full pass.
+    sub-spans' end states from zero and decays fold (in log space, float64,
+    ``fold``: the ema_span_summary / ema_span_expand kernels) into the span's
+    summary for the exchange, and the state entering the span into each
+    sub-span's incoming state for the full pass.
 
     Returns (y, chunk_start_states, Sin, final): y in x's layout;
     ``chunk_start_states`` of the sub-span rows (B K, nchunks, H, P), what
@@ -156,13 +181,10 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     K = subspans if subspans is not None else subspan_count(B, H, Ls, chunk_size)
     assert Ls % K == 0, "the span length must be a multiple of the sub-span count"
     xr, dtr = _rows(x, K), _rows(dt, K)
-    # sub-span summaries: end state from zero S_k, log decay ld_k; cl_k = sum_{j<k} ld_j
-    S = state_fwd(xr, dtr, A, chunk_size).to(torch.float64).view(B, K, H, P)
+    # sub-span summaries (end states from zero, log decays) -> the span's end state from zero, its decay
+    S = state_fwd(xr, dtr, A, chunk_size)
     ld = _log_decays(dtr, A, B, K)
-    cl = torch.cumsum(ld, dim=1) - ld
-    tot = cl[:, -1] + ld[:, -1]
-    S_loc = (torch.exp(tot[:, None] - cl - ld)[..., None] * S).sum(dim=1).to(torch.float32)  # span end state from 0
-    D = torch.exp(tot).to(torch.float32)
+    S_loc, D = fold(0, False, ld, S)
     if exchange == "allgather":
         if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
             S_loc = D[..., None] * initial_states.to(torch.float32) + S_loc
@@ -182,18 +204,16 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
         if rank + 1 < world:
             Sout = D[..., None] * Sin + S_loc
             dist.send(Sout.to(torch.float32).contiguous(), dst=_peer(group, rank + 1), group=group)
-    # state entering sub-span k: exp(cl_k) Sin + sum_{q<k} exp(cl_k - cl_q - ld_q) S_q
-    k_idx = torch.arange(K, device=x.device)
-    W = _mask_exp(cl[:, :, None, :] - (cl + ld)[:, None, :, :], (k_idx[:, None] > k_idx[None, :])[None, :, :, None])
-    init = torch.exp(cl)[..., None] * Sin.to(torch.float64)[:, None] + torch.einsum("bkqh,bqhp->bkhp", W, S)
-    y, states, final = local_fwd(xr, dtr, A, chunk_size, init.reshape(B * K, H, P).to(torch.float32))
+    # the state entering every sub-span, from the state entering the span
+    init = fold(0, True, ld, S, Sin)
+    y, states, final = local_fwd(xr, dtr, A, chunk_size, init)
     return y.reshape(B, Ls, H, P), states, Sin, final.reshape(B, K, H, P)[:, -1]
 
 
 def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
                 d_final_states: Optional[torch.Tensor] = None, need_d_initial: bool = False,
                 state_bwd: Callable = _kernel_state_bwd, local_bwd: Callable = _kernel_bwd,
-                exchange: str = "chain"):
+                exchange: str = "chain", fold: Callable = _kernel_fold):
     """Sequence-parallel backward of this rank's span.
 
     ``states`` are the sub-span rows' chunk start states from
@@ -212,13 +232,10 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
         return dx, ddt, dA.to(torch.float32).contiguous(), d_init
     K = states.shape[0] // B
     xr, dtr, dyr = _rows(x, K), _rows(dt, K), _rows(dy, K)
-    # sub-span summaries: gradient w.r.t. the sub-span's start from its own dy (nothing arriving)
-    G = state_bwd(xr, dtr, A, states, dyr, chunk_size).to(torch.float64).view(B, K, H, P)
+    # sub-span summaries (start gradients from their own dy, nothing arriving) -> the span's
+    G = state_bwd(xr, dtr, A, states, dyr, chunk_size)
     ld = _log_decays(dtr, A, B, K)
-    cl = torch.cumsum(ld, dim=1) - ld
-    tot = cl[:, -1] + ld[:, -1]
-    G_loc = (torch.exp(cl)[..., None] * G).sum(dim=1).to(torch.float32)  # span start gradient from its own dy
-    D = torch.exp(tot).to(torch.float32)
+    G_loc, D = fold(1, False, ld, G)
     if exchange == "allgather":
         if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient
             G_loc = D[..., None] * d_final_states.to(torch.float32) + G_loc
@@ -238,14 +255,9 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
         if rank > 0:
             Gout = D[..., None] * Gin + G_loc
             dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
-    # gradient arriving at the end of sub-span k:
-    #   exp(tot - cl_k - ld_k) Gin + sum_{q>k} exp(cl_q - cl_k - ld_k) G_q
-    k_idx = torch.arange(K, device=x.device)
-    W = _mask_exp(cl[:, None, :, :] - (cl + ld)[:, :, None, :], (k_idx[None, :] > k_idx[:, None])[None, :, :, None])
-    dfin = (torch.exp(tot[:, None] - cl - ld)[..., None] * Gin.to(torch.float64)[:, None]
-            + torch.einsum("bkqh,bqhp->bkhp", W, G))
-    dx, ddt, dA, d_init = local_bwd(xr, dtr, A, states, dyr, chunk_size, dfin.reshape(B * K, H, P).to(torch.float32),
-                                    need_d_initial and rank == 0)
+    # the gradient arriving at every sub-span's end, from the one arriving at the span's end
+    dfin = fold(1, True, ld, G, Gin)
+    dx, ddt, dA, d_init = local_bwd(xr, dtr, A, states, dyr, chunk_size, dfin, need_d_initial and rank == 0)
     dA = dA.to(torch.float32).contiguous()
     dist.all_reduce(dA, group=group)
     if d_init is not None:

@@ -197,6 +197,40 @@ EMA_API int ema_noalloc_status(uint32_t* status, int32_t clear, void* stream);
 EMA_API int ema_dt_rows_launch(const float* dt, float* dt_rows, int64_t batch, int64_t seqlen, int64_t nheads,
                                void* stream);
 
+/* ---- sequence-parallel sub-span folds -------------------------------------
+ * No counterpart in the reference (its sequence-parallel hooks are the
+ * d_ossm_state / d_issm_state terms of compute_dpx, ema_ssd_bwd.py:111-117,
+ * 293-295).  A rank's span of every (batch, head) chain is cut into
+ * `subspans` sub-spans run as batch rows; `log_decay` (batch, subspans,
+ * nheads) float64 holds ld_k = A_h * sum of dt over sub-span k, `values`
+ * (batch * subspans, nheads, headdim) each sub-span's boundary value from its
+ * own inputs -- direction 0: its end state from a zero start; direction 1: the
+ * gradient w.r.t. its start state from its own dy.  With cl_k = sum_{j<k} ld_j
+ * and tot = sum_k ld_k (all folds in float64):
+ *   ema_span_summary: out (batch, nheads, headdim) = the span's boundary value
+ *     -- direction 0: sum_k exp(tot - cl_k - ld_k) V_k; direction 1:
+ *     sum_k exp(cl_k) V_k -- and span_decay (batch, nheads) = exp(tot), or NULL.
+ *   ema_span_expand: out (batch * subspans, nheads, headdim) = every
+ *     sub-span's boundary value given the span's `boundary` (batch, nheads,
+ *     headdim) -- direction 0 (the state entering the span): the state entering
+ *     sub-span k, exp(cl_k) S + sum_{q<k} exp(cl_k - cl_q - ld_q) V_q;
+ *     direction 1 (the gradient arriving at the span's end): the gradient
+ *     arriving at sub-span k's end, exp(tot - cl_k - ld_k) G +
+ *     sum_{q>k} exp(cl_q - cl_k - ld_k) V_q.
+ * All tensors contiguous; at most 64 sub-spans.  Nothing is allocated. */
+typedef struct EmaSpanFoldArgs {
+  int64_t batch, subspans, nheads, headdim;
+  int32_t direction;
+  int32_t reserved;
+  const double* log_decay;
+  const float* values;
+  const float* boundary;  /* expansion input */
+  float* out;
+  float* span_decay;      /* summary output, or NULL */
+} EmaSpanFoldArgs;
+EMA_API int ema_span_summary(const EmaSpanFoldArgs* args, void* stream);
+EMA_API int ema_span_expand(const EmaSpanFoldArgs* args, void* stream);
+
 /* ---- utilities ------------------------------------------------------------ */
 /* Copies the workspace status word to *status (synchronises with `stream`). */
 EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);

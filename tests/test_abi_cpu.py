@@ -53,6 +53,28 @@ def test_struct_layouts_match_header():
     assert sizes[3] == _lib.EmaBwdArgs.workspace.offset
 
 
+@pytest.mark.parametrize("header,struct", [("ema_ssd_b200.h", "EmaSpanFoldArgs"), ("ssd_b200.h", "SsdGateArgs")])
+def test_every_field_offset_matches_header(header, struct):
+    """The ctypes mirror of `struct` has the C size and every field at the C offset."""
+    import subprocess
+    import tempfile
+    from kernels import _lib
+    mirror = getattr(_lib, struct)
+    fields = [f[0] for f in mirror._fields_]
+    code = (f'#include "{header}"\n#include <stdio.h>\n#include <stddef.h>\nint main(){{printf("%zu'
+            + ' %zu' * len(fields) + f'\\n", sizeof({struct})'
+            + ''.join(f', offsetof({struct}, {f})' for f in fields) + ');return 0;}\n')
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        open(c, "w").write(code)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        out = [int(v) for v in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(mirror)
+    for k, f in enumerate(fields):
+        assert out[1 + k] == getattr(mirror, f).offset, f
+
+
 def test_ssd_struct_layouts_match_header():
     """ctypes mirrors of SsdFwdArgs / SsdBwdArgs have the C sizes and field offsets."""
     import subprocess

@@ -1,8 +1,9 @@
 """Sequence-parallel host logic (kernels/ema_sp.py) on CPU ranks over gloo.
 
 Each rank owns one span of the sequence, cut into sub-spans run as batch rows;
-the local passes are the float64 oracle instead of the CUDA kernels, so what
-is tested is the sub-span folds, the span chaining
+the local passes are the float64 oracle and the sub-span folds the float64
+torch restatement (tests/_sp_fold_ref.py) instead of the CUDA kernels, so what
+is tested is the sub-span bookkeeping, the span chaining
 (send/recv order, the span decay, the incoming state and the gradient at the
 span end -- through the send/recv chain and through one all_gather of the span
 summaries) and the dA all-reduce.  The spans' results must equal the oracle on
@@ -80,9 +81,10 @@ def _worker(rank, world, port, with_init, exchange, subspans, errq):
         tx, tdt, tdy = (torch.from_numpy(np.ascontiguousarray(a[:, sl])) for a in (x, dt, dy))
         tA = torch.from_numpy(A)
         tinit = torch.from_numpy(init) if init is not None else None
+        from _sp_fold_ref import torch_fold
         y, states, Sin, final = ema_sp.sp_forward(tx, tdt, tA, Q, initial_states=tinit,
                                                   state_fwd=_state_fwd, local_fwd=_local_fwd, exchange=exchange,
-                                                  subspans=subspans)
+                                                  subspans=subspans, fold=torch_fold)
         np.testing.assert_allclose(_np(y), full_f["y"][:, sl], rtol=1e-5, atol=1e-6)
         if rank == world - 1:
             np.testing.assert_allclose(_np(final), full_f["final_state"], rtol=1e-5, atol=1e-6)
@@ -90,7 +92,7 @@ def _worker(rank, world, port, with_init, exchange, subspans, errq):
         tdfin = torch.from_numpy(dfin) if dfin is not None else None
         dx, ddt, dA, d_init = ema_sp.sp_backward(tx, tdt, tA, states, tdy, Q, d_final_states=tdfin,
                                                  need_d_initial=True, state_bwd=_state_bwd,
-                                                 local_bwd=_local_bwd, exchange=exchange)
+                                                 local_bwd=_local_bwd, exchange=exchange, fold=torch_fold)
         np.testing.assert_allclose(_np(dx), full_b["dx"][:, sl], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(_np(ddt), full_b["ddt"][:, sl], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(_np(dA), full_b["dA"], rtol=1e-5, atol=1e-6)
