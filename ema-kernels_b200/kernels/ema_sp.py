@@ -127,13 +127,14 @@ def _kernel_fold(direction: int, expand: bool, ld: torch.Tensor, V: torch.Tensor
         return out, dspan
 
 
-def subspan_count(batch: int, nheads: int, span: int, chunk_size: int, target_chains: int = 256) -> int:
-    """Sub-spans a rank cuts its span into: the largest power of two K with
-    batch * nheads * K <= target_chains chains, span % K == 0 and at least one
-    chunk per sub-span (config 4 over 2..8 ranks: K = 8, 256 chains)."""
+def subspan_count(batch: int, nheads: int, span: int, chunk_size: int) -> int:
+    """Sub-spans a rank cuts its span into: the largest power of two K <= 64
+    with span % K == 0, at least four chunks per sub-span (measured fastest at
+    config 4: K = 32 / 16 / 8 over 2 / 4 / 8 ranks) and at most 2048 chains
+    (batch * nheads * K)."""
     K = 1
-    while (batch * nheads * 2 * K <= target_chains and span % (2 * K) == 0
-           and span // (2 * K) >= chunk_size):
+    while (2 * K <= 64 and span % (2 * K) == 0 and span // (2 * K) >= 4 * chunk_size
+           and batch * nheads * 2 * K <= 2048):
         K *= 2
     return K
 
