@@ -318,66 +318,34 @@ SP_CFG = dict(B=1, L=65536, H=32, P=64, Q=256)
 
 
 def run_sp(args, rank, world, local_rank):
-    """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong scaling);
-    fwd+bwd through kernels.ema_sp (state-only pass, NCCL send/recv chain, local pass)."""
-    from oracle.ema_oracle import make_dt_inputs
-    from kernels import ema_sp
+    """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong
+    scaling), fwd+bwd through kernels.ema_sp -- the same graph-timed step as the
+    ``sp_config4`` leg of the default run (``--exchange`` picks the span exchange)."""
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    import torch.distributed as dist
+    dist = None
     if world > 1:
+        import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    else:
-        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
-    c = SP_CFG
-    span = c["L"] // world
-    x, dt, A, dy = make_dt_inputs(c["B"], c["L"], c["H"], c["P"], seed=21)
-    sl = slice(rank * span, (rank + 1) * span)
-    x = torch.from_numpy(np.ascontiguousarray(x[:, sl])).to(torch.bfloat16).to(dev)
-    dy = torch.from_numpy(np.ascontiguousarray(dy[:, sl])).to(torch.bfloat16).to(dev)
-    dt = torch.from_numpy(np.ascontiguousarray(dt[:, sl])).to(dev)
-    A = torch.from_numpy(A).to(dev)
-    def step():
-        y, states, Sin, _ = ema_sp.sp_forward(x, dt, A, c["Q"])
-        ema_sp.sp_backward(x, dt, A, states, dy, c["Q"])
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    K = max(1, min(args.steps, 200))
-    dist.barrier()
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(K):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev if world > 1 else "cpu")
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+    leg = _sp_leg(args, rank, world, dev, dist, exchange=args.exchange)
     if rank == 0:
-        peak, _ = _peaks()
-        tokens = c["B"] * c["L"]
-        gbs = BYTES_PER_TOKEN * tokens / (ms * 1e-3) / 1e9
+        c = SP_CFG
         print(json.dumps({
-            "metric": "EMA fwd+bwd Mtokens/s, sequence parallel (config 4: B1 L65536 H32 P64 bf16)",
-            "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "metric": leg["metric"], "value": leg["value"], "unit": "Mtokens/s", "n_gpus": world,
+            "steps": leg["steps"], "warmup": args.warmup, "ms_per_step": leg["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
             "config": {"workload": "EMA dt-form fwd+bwd, one sequence split over the ranks", **c,
-                       "span_per_rank": span, "parallelism": f"sequence parallel over {world} GPU(s), "
-                       "NCCL send/recv state chain + dA all-reduce",
-                       "timing": "one CUDA graph per step (kernels, sub-span folds, NCCL calls), L2 flushed before each replay "
-                      "outside the timed interval, CUDA events around each replay, max over ranks"},
-            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / world / peak,
-                         "note": "per-GPU algorithmic bytes of one fwd+bwd (the state-only passes "
-                                 "re-read x and dy)"},
-            "gpu_launches": K * (4 if world > 1 else 2),  # state-only passes only when split
+                       "span_per_rank": leg["span_per_rank"], "parallelism": leg["parallelism"],
+                       "timing": leg["timing"]},
+            "roofline": leg["roofline"], "max_rel_err_vs_single_gpu": leg["max_rel_err_vs_single_gpu"],
+            # per step: 4 of this library's kernels on one GPU (dt transpose + scan, each direction);
+            # split: state-only and full passes (transpose + scan each) and two span folds per direction
+            "gpu_launches": leg["steps"] * (12 if world > 1 else 4),
         }), flush=True)
-    dist.destroy_process_group()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def _tc_peak():
@@ -910,6 +878,8 @@ def main():
     ap.add_argument("--ema-forward", choices=["scan", "tc"], default="scan",
                     help="EMA forward kernel: scan (CUDA-core scan at chunk 256, the default) or tc (the tcgen05 "
                          "forward, ema_fwd_tc_kernel, at chunk 128; for comparison)")
+    ap.add_argument("--exchange", choices=["chain", "allgather"], default="chain",
+                    help="with --workload sp: the span exchange (NCCL send/recv chain or one all_gather)")
     ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
                     help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
                          "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")

@@ -126,6 +126,15 @@ class EmaSpanFoldArgs(ctypes.Structure):
     ]
 
 
+class EmaSpanStateArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64),
+        ("dtype", _i32), ("direction", _i32),
+        ("x", _ptr), ("x_stride", _i64 * 3),
+        ("dt", _ptr), ("A", _ptr), ("out", _ptr),
+    ]
+
+
 lib.ema_scan_workspace_size.restype = ctypes.c_size_t
 lib.ema_scan_workspace_size.argtypes = [_i64] * 5
 lib.ema_fwd_launch.restype = ctypes.c_int
@@ -157,6 +166,8 @@ lib.ema_span_summary.restype = ctypes.c_int
 lib.ema_span_summary.argtypes = [ctypes.POINTER(EmaSpanFoldArgs), _ptr]
 lib.ema_span_expand.restype = ctypes.c_int
 lib.ema_span_expand.argtypes = [ctypes.POINTER(EmaSpanFoldArgs), _ptr]
+lib.ema_span_state_launch.restype = ctypes.c_int
+lib.ema_span_state_launch.argtypes = [ctypes.POINTER(EmaSpanStateArgs), _ptr]
 lib.ssd_device_status.restype = ctypes.c_int
 lib.ssd_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p

@@ -11,7 +11,7 @@ D = exp(A_h sum_span dt) and S the span's end state from a zero start.
 
 Forward:
   1. state-only pass over the local span (reads x once, writes nothing but
-     S_r, (B, H, P) fp32);
+     S_r, (B, H, P) fp32; a weighted column sum, ``span_state``);
   2. chain the spans with NCCL send/recv, r -> r+1: rank r receives its
      incoming state Sin_r and sends D_r Sin_r + S_r on;
   3. the local pass from the true incoming state (y, chunk start states).
@@ -46,7 +46,7 @@ import torch.distributed as dist
 from . import _lib
 from .ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
 
-__all__ = ["span_decay", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
+__all__ = ["span_decay", "span_state", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
 
 
 def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
@@ -83,7 +83,32 @@ def _peer(group, r):
     return r if group is None else dist.get_global_rank(group, r)
 
 
+def span_state(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, direction: int) -> torch.Tensor:
+    """Per (row, head) of x (rows, L, H, P): direction 0, the row's end state from
+    a zero start; direction 1 (x = dy), the gradient w.r.t. the row's start state
+    from its own dy -- as weighted column sums (ema_span_state_launch), (rows, H, P)
+    fp32.  headdim 32, 64 or 128."""
+    rows, L, H, P = x.shape
+    xk = _lib.tma_ready(x)
+    dtk = dt.to(torch.float32).contiguous()
+    Ak = A.to(torch.float32).contiguous()
+    out = torch.empty(rows, H, P, dtype=torch.float32, device=x.device)
+    a = _lib.EmaSpanStateArgs()
+    a.rows, a.seqlen, a.nheads, a.headdim = rows, L, H, P
+    a.dtype, a.direction = _lib.DTYPE_CODES[x.dtype], direction
+    a.x, a.x_stride = xk.data_ptr(), _lib.strides3(xk)
+    a.dt, a.A, a.out = dtk.data_ptr(), Ak.data_ptr(), out.data_ptr()
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib.ema_span_state_launch(a, _lib.stream_ptr(x.device)), "ema_span_state")
+    return out
+
+
+_SPAN_STATE_P = (32, 64, 128)
+
+
 def _kernel_state_fwd(x, dt, A, chunk_size):
+    if x.shape[-1] in _SPAN_STATE_P:  # a reduction: no scan, no look-back
+        return span_state(x, dt, A, 0)
     return ema_chunk_scan_fwd(x, dt, A, chunk_size, state_only=True)[2]
 
 
@@ -94,6 +119,8 @@ def _kernel_fwd(x, dt, A, chunk_size, initial_states):
 
 
 def _kernel_state_bwd(x, dt, A, states, dy, chunk_size):
+    if dy.shape[-1] in _SPAN_STATE_P:
+        return span_state(dy if dy.dtype == x.dtype else dy.to(x.dtype), dt, A, 1)
     return ema_chunk_scan_bwd(x, dt, A, states, dy, backward_chunk(chunk_size), state_only=True)[3]
 
 

@@ -231,6 +231,29 @@ typedef struct EmaSpanFoldArgs {
 EMA_API int ema_span_summary(const EmaSpanFoldArgs* args, void* stream);
 EMA_API int ema_span_expand(const EmaSpanFoldArgs* args, void* stream);
 
+/* The state-only passes of the sequence-parallel EMA (dt form) as weighted
+ * column sums, per (row, head) of a (rows, seqlen, nheads, headdim) tensor
+ * with cs_t = A_h * sum_{u <= t} dt_u over the row:
+ *   direction 0: out = sum_t exp(cs_end - cs_t) dt_t x_t  (the row's end state
+ *                from a zero start; `x` is the input x);
+ *   direction 1: out = sum_t exp(cs_t) dy_t               (the gradient w.r.t. the
+ *                row's start state from the row's own dy; `x` is dy).
+ * out (rows, nheads, headdim) float32; headdim 32, 64 or 128; x channel stride 1,
+ * other strides multiples of 16 bytes, 16-byte aligned; dt (rows, seqlen,
+ * nheads) float32 contiguous.  Same results as ema_fwd_launch /
+ * ema_bwd_launch in their state-only modes, without their look-back. */
+typedef struct EmaSpanStateArgs {
+  int64_t rows, seqlen, nheads, headdim;
+  int32_t dtype;      /* EMA_DTYPE_* of x */
+  int32_t direction;
+  const void* x;
+  int64_t x_stride[3];  /* element strides of row, token, head */
+  const float* dt;
+  const float* A;
+  float* out;
+} EmaSpanStateArgs;
+EMA_API int ema_span_state_launch(const EmaSpanStateArgs* args, void* stream);
+
 /* ---- utilities ------------------------------------------------------------ */
 /* Copies the workspace status word to *status (synchronises with `stream`). */
 EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);

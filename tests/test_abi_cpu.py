@@ -53,7 +53,8 @@ def test_struct_layouts_match_header():
     assert sizes[3] == _lib.EmaBwdArgs.workspace.offset
 
 
-@pytest.mark.parametrize("header,struct", [("ema_ssd_b200.h", "EmaSpanFoldArgs"), ("ssd_b200.h", "SsdGateArgs")])
+@pytest.mark.parametrize("header,struct", [("ema_ssd_b200.h", "EmaSpanFoldArgs"), ("ema_ssd_b200.h", "EmaSpanStateArgs"),
+                                           ("ssd_b200.h", "SsdGateArgs")])
 def test_every_field_offset_matches_header(header, struct):
     """The ctypes mirror of `struct` has the C size and every field at the C offset."""
     import subprocess

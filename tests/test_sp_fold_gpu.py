@@ -37,3 +37,33 @@ def test_fold_refuses_more_than_64_subspans():
     V = torch.randn(65, 2, 8, device=DEV)
     with pytest.raises(_lib.EmaLaunchError, match="64 sub-spans"):
         _kernel_fold(0, False, ld, V)
+
+
+@pytest.mark.parametrize("P,dtype", [(64, torch.bfloat16), (32, torch.float32), (128, torch.float16)])
+@pytest.mark.parametrize("L,dt_range", [(1000, (1e-3, 1e-1)), (4096, (1e-2, 1.0)), (300, (1e-4, 1e-3))])
+def test_span_state_matches_scan_state_only_passes_and_oracle(P, dtype, L, dt_range):
+    """The state-only passes as weighted column sums (ema_span_state_launch)
+    against the scan kernels' state-only modes and the float64 oracle: the end
+    state from zero (direction 0) and the start-state gradient from dy
+    (direction 1), ragged lengths, steep and slow decays."""
+    import numpy as np
+    from kernels.ema_chunk_scan import ema_chunk_scan_bwd, ema_chunk_scan_fwd
+    from kernels.ema_sp import span_state
+    from oracle import ema_oracle as eo
+    x, dt, A, dy = eo.make_dt_inputs(3, L, 4, P, seed=L + P, dt_range=dt_range)
+    tx, tdy = (torch.from_numpy(a).to(dtype).to(DEV) for a in (x, dy))
+    tdt, tA = torch.from_numpy(dt).to(DEV), torch.from_numpy(A).to(DEV)
+    s_end = span_state(tx, tdt, tA, 0)
+    g_start = span_state(tdy, tdt, tA, 1)
+    s_scan = ema_chunk_scan_fwd(tx, tdt, tA, 128, state_only=True)[2]
+    _, states, _ = ema_chunk_scan_fwd(tx, tdt, tA, 128)
+    g_scan = ema_chunk_scan_bwd(tx, tdt, tA, states, tdy, 128, state_only=True)[3]
+    xf, dyf = tx.float().cpu().numpy(), tdy.float().cpu().numpy()
+    r = eo.ema_dt_fwd(xf, dt, A)
+    g = eo.ema_dt_bwd(xf, dt, A, dyf)
+    for got, scan, ref, what in ((s_end, s_scan, r["final_state"], "end state"),
+                                 (g_start, g_scan, g["d_initial_state"], "start gradient")):
+        ref = np.asarray(ref)
+        e = float(np.abs(got.double().cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
+        assert e <= 1e-4, f"{what}: normwise relative error {e:.3e} against the oracle"
+        torch.testing.assert_close(got, scan, rtol=1e-4, atol=1e-5 * float(scan.abs().max()), msg=what)
