@@ -10,14 +10,16 @@
 //
 // Neither needs the recurrence's sequential scan or a look-back between
 // tiles: every token's weight follows from the within-row cumsum of dt A, and
-// the sum over tokens is a reduction.  One CTA per (row, head) walks its row in
-// 256-token blocks: a block scan of dt A, then warp c accumulates channels
-// [8 c, 8 c + 8) (one 16-byte vector per token) over the block's tokens, one
-// token per lane, and reduces over the lanes with shuffles; blocks combine
-// through the block decay (direction 0: S <- exp(ld_block) S + block sum;
-// direction 1: G <- G + exp(cs before the block) block sum).  fp32 arithmetic,
-// as the scan kernels.  HBM-bound: x (or dy) is read once, 8 KB per CTA in
-// flight per 256 threads.
+// the sum over tokens is a reduction.  One CTA of 8 warps per (row, head) walks
+// its row in 1024-token blocks: a block scan of dt A (the block's first x loads
+// and the next block's dt in flight meanwhile), then the block's tokens stream
+// in sub-blocks: each lane issues sixteen 16-byte loads before its FMAs, a warp
+// load covering 512 bytes of whole token rows (lane l: 16 bytes of channels of
+// one row); a lane's running sum combines over the blocks through the block decay (direction 0:
+// S <- exp(ld_block) S + block sum; direction 1: G <- G + block sum, the
+// weights carrying exp(cs before the block)), and the lanes' and warps' sums --
+// disjoint tokens -- add up at the end.  fp32 arithmetic, as the scan kernels.
+// HBM-bound: x (or dy) is read once, coalesced.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -34,7 +36,10 @@ void set_last_error(const char* msg);
 
 namespace spstate {
 
-constexpr int kBlock = 256;  // tokens per block (one per thread in the scan)
+constexpr int kBlock = 1024;  // tokens per block
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTPT = kBlock / kThreads;  // tokens per thread in the block scan
 
 struct Params {
   int L, H;
@@ -47,32 +52,58 @@ struct Params {
 };
 
 template <typename T, int P>
-__global__ void __launch_bounds__(32 * (P / 8)) span_state_kernel(const Params p) {
-  constexpr int NW = P / 8;  // warps: one per 8-channel group
-  constexpr int NT = 32 * NW;
-  __shared__ float s_w[kBlock];   // the block's per-token weights
-  __shared__ float s_wsum[32];    // per-warp scan totals
+__global__ void __launch_bounds__(kThreads, 2) span_state_kernel(const Params p) {
+  constexpr int EPL = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte lane load
+  constexpr int LPR = P / EPL;                           // lanes per token row
+  constexpr int RPW = 32 / LPR;                          // token rows per warp load
+  constexpr int NL = 16;                                 // loads in flight per lane
+  constexpr int SUB = kWarps * RPW * NL;                 // tokens per sub-block
+  static_assert(LPR >= 1 && LPR <= 32 && 32 % LPR == 0, "headdim");
+  static_assert(kBlock % SUB == 0, "sub-blocks tile the block");
+  __shared__ float s_w[kBlock];          // the block's per-token weights
+  __shared__ float s_wsum[kWarps];       // per-warp scan totals
+  __shared__ float s_red[kWarps][P];     // per-warp sums, reduced at the end
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = blockIdx.x / p.H, h = blockIdx.x % p.H;
   const float Ah = p.A[h];
-  const T* xbase = static_cast<const T*>(p.x) + row * p.sr + h * p.sh + 8 * warp;
+  const int rsub = lane / LPR;  // this lane's token within a warp load
+  const T* xbase = static_cast<const T*>(p.x) + row * p.sr + h * p.sh + EPL * (lane % LPR);
   const float* dtbase = p.dt + static_cast<size_t>(row) * p.L * p.H + h;
-  float acc[8];
+  float acc[EPL];  // this lane's tokens, weighted, combined over the blocks so far
 #pragma unroll
-  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+  for (int k = 0; k < EPL; ++k) acc[k] = 0.f;
   float before = 0.f;  // direction 1: the cumsum of dt A before the block
+  float dn[kTPT];      // dt of the next block, fetched while this block's x streams
+#pragma unroll
+  for (int k = 0; k < kTPT; ++k) {
+    const int t = tid * kTPT + k;
+    dn[k] = (t < p.L) ? dtbase[static_cast<size_t>(t) * p.H] : 0.f;
+  }
+  uint4 raw[NL];
+  auto load_sub = [&](int t0, int s0, int n) {
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      const int t = s0 + (i * kWarps + warp) * RPW + rsub;
+      raw[i] = (t < n) ? __ldg(reinterpret_cast<const uint4*>(xbase + static_cast<long long>(t0 + t) * p.sl))
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
   for (int t0 = 0; t0 < p.L; t0 += kBlock) {
     const int n = min(kBlock, p.L - t0);
-    // ---- block scan of dt A (kBlock tokens over NT threads, kBlock / NT per thread) ----
-    constexpr int TPT = (kBlock + NT - 1) / NT;
-    float d[TPT], v[TPT];
+    load_sub(t0, 0, n);  // the block's first x in flight through the scan
+    // ---- block scan of dt A -------------------------------------------------------
+    float d[kTPT], v[kTPT];
     float run = 0.f;
 #pragma unroll
-    for (int k = 0; k < TPT; ++k) {
-      const int t = tid * TPT + k;
-      d[k] = (t < n) ? dtbase[static_cast<size_t>(t0 + t) * p.H] : 0.f;
+    for (int k = 0; k < kTPT; ++k) {
+      d[k] = dn[k];
       run += d[k] * Ah;
-      v[k] = run;  // inclusive within this thread's tokens
+      v[k] = run;
+    }
+#pragma unroll
+    for (int k = 0; k < kTPT; ++k) {  // the next block's dt
+      const int t = t0 + kBlock + tid * kTPT + k;
+      dn[k] = (t < p.L) ? dtbase[static_cast<size_t>(t) * p.H] : 0.f;
     }
     float incl = run;
 #pragma unroll
@@ -83,53 +114,59 @@ __global__ void __launch_bounds__(32 * (P / 8)) span_state_kernel(const Params p
     if (lane == 31) s_wsum[warp] = incl;
     __syncthreads();
     float wpre = 0.f, total = 0.f;
-    for (int w = 0; w < NW; ++w) {
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
       const float sw = s_wsum[w];
       if (w < warp) wpre += sw;
       total += sw;
     }
     const float excl = wpre + incl - run;  // cumsum before this thread's first token
 #pragma unroll
-    for (int k = 0; k < TPT; ++k) {
-      const int t = tid * TPT + k;
-      if (t < kBlock) {
-        const float cs = excl + v[k];  // within the block, through token t
-        s_w[t] = (t >= n) ? 0.f : (p.dir == 0 ? __expf(total - cs) * d[k] : __expf(before + cs));
-      }
+    for (int k = 0; k < kTPT; ++k) {
+      const int t = tid * kTPT + k;
+      const float cs = excl + v[k];  // within the block, through token t
+      s_w[t] = (t >= n) ? 0.f : (p.dir == 0 ? __expf(total - cs) * d[k] : __expf(before + cs));
     }
     __syncthreads();
-    // ---- weighted column sums: warp = 8-channel group, lane = token ----------------
-    float bs[8];
+    // ---- weighted column sums: NL 16-byte loads in flight per lane, then the FMAs ----
+    float bs[EPL];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) bs[k] = 0.f;
-#pragma unroll 4
-    for (int t = lane; t < n; t += 32) {
-      float xv[8];
-      load_pack<T, 8>(xbase + static_cast<long long>(t0 + t) * p.sl, xv);
-      const float w = s_w[t];
+    for (int k = 0; k < EPL; ++k) bs[k] = 0.f;
+    for (int s0 = 0; s0 < n; s0 += SUB) {
+      if (s0 > 0) load_sub(t0, s0, n);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) bs[k] = fmaf(w, xv[k], bs[k]);
-    }
+      for (int i = 0; i < NL; ++i) {
+        const float w = s_w[s0 + (i * kWarps + warp) * RPW + rsub];  // 0 past the row's end
+        const T* e = reinterpret_cast<const T*>(&raw[i]);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) bs[k] += __shfl_xor_sync(0xffffffffu, bs[k], o);
+        for (int k = 0; k < EPL; ++k) bs[k] = fmaf(w, to_f32(e[k]), bs[k]);
+      }
     }
     if (p.dir == 0) {
       const float dec = __expf(total);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = fmaf(dec, acc[k], bs[k]);
+      for (int k = 0; k < EPL; ++k) acc[k] = fmaf(dec, acc[k], bs[k]);
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] += bs[k];
+      for (int k = 0; k < EPL; ++k) acc[k] += bs[k];
       before += total;
     }
     __syncthreads();  // s_w / s_wsum are rewritten by the next block
   }
-  if (lane == 0) {
-    float* o = p.out + (static_cast<size_t>(row) * p.H + h) * P + 8 * warp;
+  // ---- the lanes' and warps' sums (linear combinations of disjoint tokens) ----------
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = acc[k];
+  for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
+  if (lane < LPR)
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) s_red[warp][EPL * lane + k] = acc[k];
+  __syncthreads();
+  for (int c = tid; c < P; c += kThreads) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) sum += s_red[w][c];
+    p.out[(static_cast<size_t>(row) * p.H + h) * P + c] = sum;
   }
 }
 
@@ -145,7 +182,7 @@ int fail(int code, const char* fmt, ...) {
 
 template <typename T, int P>
 int launch_t(const Params& p, long long rows, cudaStream_t s) {
-  span_state_kernel<T, P><<<static_cast<unsigned>(rows * p.H), 32 * (P / 8), 0, s>>>(p);
+  span_state_kernel<T, P><<<static_cast<unsigned>(rows * p.H), kThreads, 0, s>>>(p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(EMA_ERR_CUDA, "ema_span_state launch failed: %s", cudaGetErrorString(e));
   return EMA_OK;
