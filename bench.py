@@ -79,15 +79,19 @@ def _peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def _profile_traffic():
-    """DRAM bytes per backward launch from the committed ncu summary, or None."""
+def _profile_traffic(tokens=None):
+    """DRAM bytes per backward launch from the committed ncu summary (captured on
+    the whole config-2 batch), scaled to a launch over ``tokens`` tokens -- the
+    traffic grows with the rows processed -- or None."""
     path = os.path.join(ROOT, "profiles", "ema_bwd_kernel_cfg2.md")
     try:
         txt = open(path).read()
     except OSError:
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) if m else None
+    if not m:
+        return None
+    return float(m.group(1)) * (1.0 if tokens is None else tokens / TOKENS)
 
 
 class ClockSampler:
@@ -823,7 +827,7 @@ def run_ema(args, rank, world, local_rank):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "kernel": bwd_kernel, "achieved": bwd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": bwd_gbs / peak,
-                         "traffic": _profile_traffic() if bwd_kernel == "ema_bwd_kernel" else None,
+                         "traffic": _profile_traffic(toks) if bwd_kernel == "ema_bwd_kernel" else None,
                          "algorithmic_bytes_per_launch": BWD_BYTES_PER_TOKEN * toks,
                          "launch_ms": bwd_launch_s * 1e3, "peak_source": f"{peak_kind} (hbm_gbs)"},
             "kernels": {f"forward (dt_rows_kernel + {fwd_kernel})": {"ms": fwd_launch_s * 1e3, "gbs": fwd_gbs,

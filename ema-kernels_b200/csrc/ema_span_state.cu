@@ -18,7 +18,8 @@
 // one row); a lane's running sum combines over the blocks through the block decay (direction 0:
 // S <- exp(ld_block) S + block sum; direction 1: G <- G + block sum, the
 // weights carrying exp(cs before the block)), and the lanes' and warps' sums --
-// disjoint tokens -- add up at the end.  fp32 arithmetic, as the scan kernels.
+// disjoint tokens -- add up at the end.  fp32 arithmetic, as the scan kernels;
+// optionally the row's log decay A_h sum dt, summed in float64, for the folds.
 // HBM-bound: x (or dy) is read once, coalesced.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -48,6 +49,7 @@ struct Params {
   const float* dt;       // (rows, L, H)
   const float* A;
   float* out;            // (rows, H, P)
+  double* ld;            // (rows, H) A_h sum dt, or null
   int dir;
 };
 
@@ -63,6 +65,7 @@ __global__ void __launch_bounds__(kThreads, 2) span_state_kernel(const Params p)
   __shared__ float s_w[kBlock];          // the block's per-token weights
   __shared__ float s_wsum[kWarps];       // per-warp scan totals
   __shared__ float s_red[kWarps][P];     // per-warp sums, reduced at the end
+  __shared__ double s_dsum[kWarps];      // per-warp float64 sums of dt
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = blockIdx.x / p.H, h = blockIdx.x % p.H;
   const float Ah = p.A[h];
@@ -73,6 +76,7 @@ __global__ void __launch_bounds__(kThreads, 2) span_state_kernel(const Params p)
 #pragma unroll
   for (int k = 0; k < EPL; ++k) acc[k] = 0.f;
   float before = 0.f;  // direction 1: the cumsum of dt A before the block
+  double dsum = 0.0;   // this thread's dt, summed in float64 (the row's log decay)
   float dn[kTPT];      // dt of the next block, fetched while this block's x streams
 #pragma unroll
   for (int k = 0; k < kTPT; ++k) {
@@ -97,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 2) span_state_kernel(const Params p)
 #pragma unroll
     for (int k = 0; k < kTPT; ++k) {
       d[k] = dn[k];
+      dsum += static_cast<double>(d[k]);
       run += d[k] * Ah;
       v[k] = run;
     }
@@ -161,7 +166,16 @@ __global__ void __launch_bounds__(kThreads, 2) span_state_kernel(const Params p)
   if (lane < LPR)
 #pragma unroll
     for (int k = 0; k < EPL; ++k) s_red[warp][EPL * lane + k] = acc[k];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+  if (lane == 0) s_dsum[warp] = dsum;
   __syncthreads();
+  if (p.ld != nullptr && tid == 0) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += s_dsum[w];
+    p.ld[static_cast<size_t>(row) * p.H + h] = t * static_cast<double>(Ah);
+  }
   for (int c = tid; c < P; c += kThreads) {
     float sum = 0.f;
 #pragma unroll
@@ -221,12 +235,15 @@ extern "C" EMA_API int ema_span_state_launch(const EmaSpanStateArgs* a, void* st
     if ((a->x_stride[i] * es) % 16 != 0)
       return fail(EMA_ERR_INVALID_ARGUMENT, "ema_span_state: x strides must be multiples of 16 bytes");
   if (a->rows == 0 || a->seqlen == 0) {
-    const size_t bytes = static_cast<size_t>(a->rows) * a->nheads * a->headdim * sizeof(float);
-    const cudaError_t e = bytes ? cudaMemsetAsync(a->out, 0, bytes, static_cast<cudaStream_t>(stream)) : cudaSuccess;
+    const size_t n = static_cast<size_t>(a->rows) * a->nheads;
+    cudaError_t e = n ? cudaMemsetAsync(a->out, 0, n * a->headdim * sizeof(float), static_cast<cudaStream_t>(stream))
+                      : cudaSuccess;
+    if (e == cudaSuccess && n && a->log_decay != nullptr)
+      e = cudaMemsetAsync(a->log_decay, 0, n * sizeof(double), static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? EMA_OK : fail(EMA_ERR_CUDA, "ema_span_state: %s", cudaGetErrorString(e));
   }
   Params p{static_cast<int>(a->seqlen), static_cast<int>(a->nheads), a->x, a->x_stride[0], a->x_stride[1],
-           a->x_stride[2], a->dt, a->A, a->out, a->direction};
+           a->x_stride[2], a->dt, a->A, a->out, a->log_decay, a->direction};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int P = static_cast<int>(a->headdim);
   switch (a->dtype) {

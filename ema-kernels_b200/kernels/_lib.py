@@ -131,7 +131,7 @@ class EmaSpanStateArgs(ctypes.Structure):
         ("rows", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64),
         ("dtype", _i32), ("direction", _i32),
         ("x", _ptr), ("x_stride", _i64 * 3),
-        ("dt", _ptr), ("A", _ptr), ("out", _ptr),
+        ("dt", _ptr), ("A", _ptr), ("out", _ptr), ("log_decay", _ptr),
     ]
 
 

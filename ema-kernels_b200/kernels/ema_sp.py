@@ -83,32 +83,38 @@ def _peer(group, r):
     return r if group is None else dist.get_global_rank(group, r)
 
 
-def span_state(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, direction: int) -> torch.Tensor:
+def span_state(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, direction: int, log_decay: bool = False):
     """Per (row, head) of x (rows, L, H, P): direction 0, the row's end state from
     a zero start; direction 1 (x = dy), the gradient w.r.t. the row's start state
     from its own dy -- as weighted column sums (ema_span_state_launch), (rows, H, P)
-    fp32.  headdim 32, 64 or 128."""
+    fp32.  headdim 32, 64 or 128.  With ``log_decay`` also the rows' log decays
+    A_h sum dt, (rows, H) float64, from the same launch: returns (out, ld)."""
     rows, L, H, P = x.shape
     xk = _lib.tma_ready(x)
     dtk = dt.to(torch.float32).contiguous()
     Ak = A.to(torch.float32).contiguous()
     out = torch.empty(rows, H, P, dtype=torch.float32, device=x.device)
+    ld = torch.empty(rows, H, dtype=torch.float64, device=x.device) if log_decay else None
     a = _lib.EmaSpanStateArgs()
     a.rows, a.seqlen, a.nheads, a.headdim = rows, L, H, P
     a.dtype, a.direction = _lib.DTYPE_CODES[x.dtype], direction
     a.x, a.x_stride = xk.data_ptr(), _lib.strides3(xk)
     a.dt, a.A, a.out = dtk.data_ptr(), Ak.data_ptr(), out.data_ptr()
+    a.log_decay = ld.data_ptr() if ld is not None else None
     with torch.cuda.device(x.device):
         _lib.check(_lib.lib.ema_span_state_launch(a, _lib.stream_ptr(x.device)), "ema_span_state")
-    return out
+    return (out, ld) if log_decay else out
 
 
 _SPAN_STATE_P = (32, 64, 128)
 
 
+# The state callables of sp_forward / sp_backward return the sub-span rows'
+# boundary values (B K, H, P), or (values, log decays (B K, H) float64) when the
+# same launch gives the log decays.
 def _kernel_state_fwd(x, dt, A, chunk_size):
     if x.shape[-1] in _SPAN_STATE_P:  # a reduction: no scan, no look-back
-        return span_state(x, dt, A, 0)
+        return span_state(x, dt, A, 0, log_decay=True)
     return ema_chunk_scan_fwd(x, dt, A, chunk_size, state_only=True)[2]
 
 
@@ -120,13 +126,21 @@ def _kernel_fwd(x, dt, A, chunk_size, initial_states):
 
 def _kernel_state_bwd(x, dt, A, states, dy, chunk_size):
     if dy.shape[-1] in _SPAN_STATE_P:
-        return span_state(dy if dy.dtype == x.dtype else dy.to(x.dtype), dt, A, 1)
+        return span_state(dy if dy.dtype == x.dtype else dy.to(x.dtype), dt, A, 1, log_decay=True)
     return ema_chunk_scan_bwd(x, dt, A, states, dy, backward_chunk(chunk_size), state_only=True)[3]
 
 
 def _kernel_bwd(x, dt, A, states, dy, chunk_size, d_final_states, need_d_initial):
     return ema_chunk_scan_bwd(x, dt, A, states, dy, backward_chunk(chunk_size), d_final_states=d_final_states,
                               need_d_initial=need_d_initial)
+
+
+def _values_and_logs(r, dt_rows: torch.Tensor, A: torch.Tensor, B: int, K: int):
+    """A state callable's result -> (values, log decays (B, K, H) float64)."""
+    if isinstance(r, tuple):
+        V, ld = r
+        return V, ld.view(B, K, -1)
+    return r, _log_decays(dt_rows, A, B, K)
 
 
 def _kernel_fold(direction: int, expand: bool, ld: torch.Tensor, V: torch.Tensor,
@@ -210,8 +224,7 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     assert Ls % K == 0, "the span length must be a multiple of the sub-span count"
     xr, dtr = _rows(x, K), _rows(dt, K)
     # sub-span summaries (end states from zero, log decays) -> the span's end state from zero, its decay
-    S = state_fwd(xr, dtr, A, chunk_size)
-    ld = _log_decays(dtr, A, B, K)
+    S, ld = _values_and_logs(state_fwd(xr, dtr, A, chunk_size), dtr, A, B, K)
     S_loc, D = fold(0, False, ld, S)
     if exchange == "allgather":
         if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
@@ -261,8 +274,7 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     K = states.shape[0] // B
     xr, dtr, dyr = _rows(x, K), _rows(dt, K), _rows(dy, K)
     # sub-span summaries (start gradients from their own dy, nothing arriving) -> the span's
-    G = state_bwd(xr, dtr, A, states, dyr, chunk_size)
-    ld = _log_decays(dtr, A, B, K)
+    G, ld = _values_and_logs(state_bwd(xr, dtr, A, states, dyr, chunk_size), dtr, A, B, K)
     G_loc, D = fold(1, False, ld, G)
     if exchange == "allgather":
         if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient

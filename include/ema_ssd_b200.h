@@ -241,7 +241,9 @@ EMA_API int ema_span_expand(const EmaSpanFoldArgs* args, void* stream);
  * out (rows, nheads, headdim) float32; headdim 32, 64 or 128; x channel stride 1,
  * other strides multiples of 16 bytes, 16-byte aligned; dt (rows, seqlen,
  * nheads) float32 contiguous.  Same results as ema_fwd_launch /
- * ema_bwd_launch in their state-only modes, without their look-back. */
+ * ema_bwd_launch in their state-only modes, without their look-back.
+ * log_decay (optional, (rows, nheads) float64): A_h * sum_t dt_t per row, the
+ * log of the row's decay, summed in float64 (what the sub-span folds take). */
 typedef struct EmaSpanStateArgs {
   int64_t rows, seqlen, nheads, headdim;
   int32_t dtype;      /* EMA_DTYPE_* of x */
@@ -251,6 +253,7 @@ typedef struct EmaSpanStateArgs {
   const float* dt;
   const float* A;
   float* out;
+  double* log_decay;  /* or NULL */
 } EmaSpanStateArgs;
 EMA_API int ema_span_state_launch(const EmaSpanStateArgs* args, void* stream);
 

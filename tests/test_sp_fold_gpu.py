@@ -15,10 +15,13 @@ DEV = "cuda"
 @pytest.mark.parametrize("K", [1, 3, 8, 64])
 @pytest.mark.parametrize("direction", [0, 1])
 @pytest.mark.parametrize("scale", [0.05, 30.0, 2000.0])
-def test_fold_kernels_match_float64(K, direction, scale):
+@pytest.mark.parametrize("P", [48, 7])
+def test_fold_kernels_match_float64(K, direction, scale, P):
+    """P = 7: an expansion CTA's 256 outputs span many sub-spans (rows of
+    weights); P = 48: a sub-span's channels straddle two CTAs."""
     from kernels.ema_sp import _kernel_fold
     g = torch.Generator().manual_seed(K * 10 + direction)
-    B, H, P = 2, 5, 48
+    B, H = 2, 5
     ld = (-torch.rand(B, K, H, generator=g, dtype=torch.float64) * scale).to(DEV)
     V = torch.randn(B * K, H, P, generator=g).to(DEV)
     bnd = torch.randn(B, H, P, generator=g).to(DEV)
@@ -53,8 +56,13 @@ def test_span_state_matches_scan_state_only_passes_and_oracle(P, dtype, L, dt_ra
     x, dt, A, dy = eo.make_dt_inputs(3, L, 4, P, seed=L + P, dt_range=dt_range)
     tx, tdy = (torch.from_numpy(a).to(dtype).to(DEV) for a in (x, dy))
     tdt, tA = torch.from_numpy(dt).to(DEV), torch.from_numpy(A).to(DEV)
-    s_end = span_state(tx, tdt, tA, 0)
-    g_start = span_state(tdy, tdt, tA, 1)
+    s_end, ld0 = span_state(tx, tdt, tA, 0, log_decay=True)
+    g_start, ld1 = span_state(tdy, tdt, tA, 1, log_decay=True)
+    ld_ref = tdt.double().sum(dim=1) * tA.double()  # the rows' log decays, float64
+    for ld in (ld0, ld1):
+        assert ld.dtype == torch.float64
+        torch.testing.assert_close(ld, ld_ref, rtol=1e-12, atol=0.0)
+    torch.testing.assert_close(span_state(tx, tdt, tA, 0), s_end, rtol=0, atol=0)
     s_scan = ema_chunk_scan_fwd(tx, tdt, tA, 128, state_only=True)[2]
     _, states, _ = ema_chunk_scan_fwd(tx, tdt, tA, 128)
     g_scan = ema_chunk_scan_bwd(tx, tdt, tA, states, tdy, 128, state_only=True)[3]
