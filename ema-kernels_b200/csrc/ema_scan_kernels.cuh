@@ -733,15 +733,27 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised (under programmatic launch this overlaps the previous kernel)
-  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
-  grid_dep_release();
   const int BH = p.B * p.H;
   const int total = BH * p.nc;
+  auto prefetch_tile = [&](int ticket) {
+    const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
+    const int b = fast_div(bh, p.div_h), h = bh - b * p.H;
+    tma_prefetch_l2_4d(&tm_x, 0, h, c * Q, b);
+  };
+  if (warp == NW && lane == 0) {
+    // The first tickets' x tiles, asked into L2 while the previous kernel
+    // drains: a hint only (L2 is coherent with that kernel's writes), so it
+    // needs no ordering; the CTA's first tickets are about blockIdx.x and
+    // blockIdx.x + gridDim.x.
+    tma_prefetch_desc(&tm_x);
+    for (int t = blockIdx.x; t < total && t < 2 * static_cast<int>(gridDim.x); t += gridDim.x) prefetch_tile(t);
+  }
+  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
+  grid_dep_release();
 
   if (warp == NW) {
     // ------------------------------ producer ------------------------------
     // (needs no epoch: its first ticket round trip overlaps the epoch read below)
-    if (lane == 0) tma_prefetch_desc(&tm_x);
     producer_loop<S>(full, empty, tid_full, s_tile, ws.hdr, total, lane, [&](int s, int ticket) {
       const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
       const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
@@ -765,11 +777,7 @@ __global__ void __launch_bounds__(FwdCfg<T, BP, Q>::NT, FwdCfg<T, BP, Q>::CTAS)
         gather_col(raw, src, p.H, n, lane);  // dt column of head h (stride H)
       }
       if (MODE == kFwdDt && lane == 0) cp_async_4(raw + Q, p.A + h);
-    }, [&](int ticket) {
-      const int c = fast_div(ticket, p.div_bh), bh = ticket - c * BH;
-      const int b = fast_div(bh, p.div_h), h = bh - b * p.H;
-      tma_prefetch_l2_4d(&tm_x, 0, h, c * Q, b);
-    });
+    }, prefetch_tile);
     return;
   }
   // the look-back and compute warps tag their records with the launch epoch
@@ -1152,18 +1160,30 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised (under programmatic launch this overlaps the previous kernel)
-  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
-  grid_dep_release();
   const int BH = p.B * p.H;
   const int total = BH * p.nc;
+  auto prefetch_tile = [&](int ticket) {
+    const int cr = fast_div(ticket, p.div_bh), bh = ticket - cr * BH;
+    const int c = p.nc - 1 - cr;
+    const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
+    if (p.dx != nullptr) tma_prefetch_l2_4d(&tm_x, 0, h, t0, b);
+    tma_prefetch_l2_4d(&tm_dy, 0, h, t0, b);
+  };
+  if (warp == NW && lane == 0) {
+    // The first tickets' x and dy tiles, asked into L2 while the previous
+    // kernel drains: a hint only (L2 is coherent with that kernel's writes),
+    // so it needs no ordering; the CTA's first tickets are about blockIdx.x
+    // and blockIdx.x + gridDim.x.
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_dy);
+    for (int t = blockIdx.x; t < total && t < 2 * static_cast<int>(gridDim.x); t += gridDim.x) prefetch_tile(t);
+  }
+  grid_dep_wait();  // the previous kernel's writes (and its workspace reset) are visible from here
+  grid_dep_release();
 
   if (warp == NW) {
     // ------------------------------ producer ------------------------------
     // (needs no epoch: its first ticket round trip overlaps the epoch read below)
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_x);
-      tma_prefetch_desc(&tm_dy);
-    }
     producer_loop<S>(full, empty, tid_full, s_tile, ws.hdr, total, lane, [&](int s, int ticket) {
       const int cr = fast_div(ticket, p.div_bh), bh = ticket - cr * BH;
       const int c = p.nc - 1 - cr;
@@ -1200,13 +1220,7 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       } else if (full_pass) {
         for (int i = lane; i < p.P; i += 32) cp_async_4(sst + i, srow + static_cast<long long>(i) * p.st_p);
       }
-    }, [&](int ticket) {
-      const int cr = fast_div(ticket, p.div_bh), bh = ticket - cr * BH;
-      const int c = p.nc - 1 - cr;
-      const int b = fast_div(bh, p.div_h), h = bh - b * p.H, t0 = c * Q;
-      if (p.dx != nullptr) tma_prefetch_l2_4d(&tm_x, 0, h, t0, b);
-      tma_prefetch_l2_4d(&tm_dy, 0, h, t0, b);
-    });
+    }, prefetch_tile);
     return;
   }
   // the look-back and compute warps tag their records with the launch epoch
@@ -1501,7 +1515,9 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
       if (tid == 0) pslot = (static_cast<size_t>(h) * p.nc + c) * p.B + b;
     }
   }
-  if (lane == 0 && p.dx != nullptr) bulk_wait_all();  // this warp's dx stores have landed
+  // this warp's dx stores have read their stage (nothing in this launch reads dx
+  // back; the stores complete with the grid)
+  if (lane == 0 && p.dx != nullptr) bulk_wait_read<0>();
   if (pend >= 0 && lane == 0) mbar_arrive(&empty[pend]);
   named_sync(1, NC);
   if (tid == 0) s_last = count_cta_done(ws) ? 1u : 0u;
