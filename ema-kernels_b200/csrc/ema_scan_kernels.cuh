@@ -229,10 +229,16 @@ __device__ __forceinline__ bool count_cta_done(const ScanWorkspace& ws) {
 // Every CTA's producer draws exactly one ticket past the last tile, so a
 // launch that started from reset counters ends at total + gridDim.x; anything
 // else means the workspace was shared by overlapping launches.
-__device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t epoch, int total) {
-  __threadfence();
-  if (ld_volatile_u32(&ws.hdr[kHdrTicket]) != static_cast<uint32_t>(total) + gridDim.x)
-    atomicOr(&ws.hdr[kHdrStatus], kStatusBadTicket);
+// `tickets`: the ticket counter as read after a fence that follows this CTA's
+// done count (kTicketsUnread: read it here).
+constexpr uint32_t kTicketsUnread = 0xffffffffu;
+__device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t epoch, int total,
+                                               uint32_t tickets = kTicketsUnread) {
+  if (tickets == kTicketsUnread) {
+    __threadfence();
+    tickets = ld_volatile_u32(&ws.hdr[kHdrTicket]);
+  }
+  if (tickets != static_cast<uint32_t>(total) + gridDim.x) atomicOr(&ws.hdr[kHdrStatus], kStatusBadTicket);
   ws.hdr[kHdrTicket] = 0u;
   ws.hdr[kHdrDone] = 0u;
   __threadfence();
@@ -247,14 +253,14 @@ __device__ __forceinline__ void reset_counters(const ScanWorkspace& ws, uint32_t
 // epoch therefore clears every record word of the workspace first (a few
 // microseconds, once per 2^30 launches).
 __device__ __forceinline__ void finish_launch(const ScanWorkspace& ws, uint32_t epoch, int total, int tid,
-                                              int nthreads, int bar) {
+                                              int nthreads, int bar, uint32_t tickets = kTicketsUnread) {
   if (((epoch + 1u) & kEpochMask) == 0u) {
     const size_t n = static_cast<size_t>(ws.rec_end - ws.agg);
     for (size_t i = tid; i < n; i += nthreads) ws.agg[i] = 0ull;
     __threadfence();
     named_sync(bar, nthreads);
   }
-  if (tid == 0) reset_counters(ws, epoch, total);
+  if (tid == 0) reset_counters(ws, epoch, total, tickets);
 }
 
 // Producer-side end of stream: mark the stage as "no more tiles" with the
@@ -1524,12 +1530,17 @@ __global__ void __launch_bounds__(BwdCfg<T, BP, Q>::NT, BwdCfg<T, BP, Q>::CTAS)
   named_sync(1, NC);
   if (s_last) {
     if (MODE == kBwdDt && p.dx != nullptr) {
-      // dA[h] = sum of head h's nc * B per-tile partials
+      // dA[h] = sum of head h's nc * B per-tile partials.  The ticket count
+      // (checked by the counter reset) is read behind the same fence, so its
+      // round trip overlaps the sums; the reset touches neither the partials
+      // nor dA, so it follows without a barrier.
       __threadfence();
+      const uint32_t tickets = tid == 0 ? ld_volatile_u32(&ws.hdr[kHdrTicket]) : kTicketsUnread;
       sum_head_partials<NC>(ws.partial, p.H, p.nc * p.B, p.dA_out, tid);
-      named_sync(1, NC);
+      finish_launch(ws, epoch, total, tid, NC, 1, tickets);
+    } else {
+      finish_launch(ws, epoch, total, tid, NC, 1);
     }
-    finish_launch(ws, epoch, total, tid, NC, 1);
   }
 }
 
