@@ -343,9 +343,10 @@ def run_sp(args, rank, world, local_rank):
                        "span_per_rank": leg["span_per_rank"], "parallelism": leg["parallelism"],
                        "timing": leg["timing"]},
             "roofline": leg["roofline"], "max_rel_err_vs_single_gpu": leg["max_rel_err_vs_single_gpu"],
-            # per step: 4 of this library's kernels on one GPU (dt transpose + scan, each direction);
-            # split: state-only and full passes (transpose + scan each) and two span folds per direction
-            "gpu_launches": leg["steps"] * (12 if world > 1 else 4),
+            # per step and direction: the column-sum state pass, the span summary fold (ranks > 1),
+            # the expansion fold and the full pass (dt transpose + scan); the whole sequence as
+            # 32 chains (no sub-spans): dt transpose + scan per direction
+            "gpu_launches": leg["steps"] * _sp_launches_per_step(world),
         }), flush=True)
     if dist is not None:
         dist.barrier()
@@ -448,6 +449,15 @@ def _max_over_ranks(vals, dev, dist):
     return [float(v) for v in t.tolist()]
 
 
+def _sp_launches_per_step(world):
+    """This library's kernels per config-4 SP step (see run_sp)."""
+    from kernels import ema_sp
+    c = SP_CFG
+    if world == 1 and ema_sp.subspan_count(c["B"], c["H"], c["L"], c["Q"], 1) == 1:
+        return 4
+    return 2 * (4 + (world > 1))
+
+
 def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
     """Config 4: one B1 L65536 H32 P64 sequence split over the ranks (strong
     scaling) through kernels.ema_sp -- each rank's span cut into sub-spans run
@@ -524,7 +534,8 @@ def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
             "parallelism": (f"sequence parallel over {world} GPU(s): "
                             + ("NCCL send/recv state chain" if exchange == "chain" else
                                "one NCCL all_gather of the span summaries per direction") + " + dA all-reduce")
-                           if world > 1 else "one GPU: the whole sequence, no chain",
+                           if world > 1 else (f"one GPU: the sequence cut into {ema_sp.subspan_count(c['B'], c['H'], c['L'], c['Q'], 1)} "
+                                              "sub-spans run as batch rows, no exchange"),
             "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
             "max_rel_err_vs_single_gpu": dict(zip(("y", "dx", "ddt", "dA"), errs)),
             "timing": "one CUDA graph per step (kernels, sub-span folds, NCCL calls), L2 flushed before each replay "

@@ -168,14 +168,19 @@ def _kernel_fold(direction: int, expand: bool, ld: torch.Tensor, V: torch.Tensor
         return out, dspan
 
 
-def subspan_count(batch: int, nheads: int, span: int, chunk_size: int) -> int:
+def subspan_count(batch: int, nheads: int, span: int, chunk_size: int, ranks: int = 2) -> int:
     """Sub-spans a rank cuts its span into: the largest power of two K <= 64
-    with span % K == 0, at least four chunks per sub-span (measured fastest at
-    config 4: K = 32 / 16 / 8 over 2 / 4 / 8 ranks) and at most 2048 chains
-    (batch * nheads * K)."""
+    with span % K == 0 and, over several ranks, at least four chunks per
+    sub-span and at most 2048 chains (batch * nheads * K) -- measured fastest at
+    config 4: K = 32 / 16 / 8 over 2 / 4 / 8 ranks; on one GPU (``ranks`` 1,
+    where the sub-spans only add parallelism) at least sixteen chunks per
+    sub-span and at most 512 chains -- K = 16 at config 4 (383.6 against 462.7
+    us for the whole sequence as 32 chains; 402 / 388 / 400 us at K = 8 / 32 /
+    64).  K = 1 means the span runs whole."""
+    min_chunks, max_chains = (16, 512) if ranks == 1 else (4, 2048)
     K = 1
-    while (2 * K <= 64 and span % (2 * K) == 0 and span // (2 * K) >= 4 * chunk_size
-           and batch * nheads * 2 * K <= 2048):
+    while (2 * K <= 64 and span % (2 * K) == 0 and span // (2 * K) >= min_chunks * chunk_size
+           and batch * nheads * 2 * K <= max_chains):
         K *= 2
     return K
 
@@ -215,18 +220,21 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, Ls, H, P = x.shape
-    if world == 1:  # one span: no exchange, no state-only pass
+    K = subspans if subspans is not None else subspan_count(B, H, Ls, chunk_size, world)
+    if world == 1 and K == 1:  # one span, whole: no state-only pass
         init = None if initial_states is None else initial_states.to(torch.float32)
         Sin = init if init is not None else torch.zeros(B, H, P, dtype=torch.float32, device=x.device)
         y, states, final = local_fwd(x, dt, A, chunk_size, Sin)
         return y, states, Sin, final
-    K = subspans if subspans is not None else subspan_count(B, H, Ls, chunk_size)
     assert Ls % K == 0, "the span length must be a multiple of the sub-span count"
     xr, dtr = _rows(x, K), _rows(dt, K)
     # sub-span summaries (end states from zero, log decays) -> the span's end state from zero, its decay
     S, ld = _values_and_logs(state_fwd(xr, dtr, A, chunk_size), dtr, A, B, K)
-    S_loc, D = fold(0, False, ld, S)
-    if exchange == "allgather":
+    if world == 1:  # one span cut into sub-spans: nothing to exchange
+        Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
+               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    elif exchange == "allgather":
+        S_loc, D = fold(0, False, ld, S)
         if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
             S_loc = D[..., None] * initial_states.to(torch.float32) + S_loc
         Ss, Ds = _gather(S_loc, D, group)
@@ -236,6 +244,7 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
         else:  # the spans before this one, folded in order
             Sin = _fold(Ss[:rank], Ds[:rank])
     else:
+        S_loc, D = fold(0, False, ld, S)
         if rank == 0:
             Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
@@ -266,7 +275,7 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, Ls, H, P = x.shape
-    if world == 1:
+    if world == 1 and states.shape[0] == B:  # one span, whole
         Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
         dx, ddt, dA, d_init = local_bwd(x, dt, A, states, dy, chunk_size, Gin, need_d_initial)
@@ -275,8 +284,11 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     xr, dtr, dyr = _rows(x, K), _rows(dt, K), _rows(dy, K)
     # sub-span summaries (start gradients from their own dy, nothing arriving) -> the span's
     G, ld = _values_and_logs(state_bwd(xr, dtr, A, states, dyr, chunk_size), dtr, A, B, K)
-    G_loc, D = fold(1, False, ld, G)
-    if exchange == "allgather":
+    if world == 1:  # one span cut into sub-spans: nothing to exchange
+        Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
+               else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    elif exchange == "allgather":
+        G_loc, D = fold(1, False, ld, G)
         if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient
             G_loc = D[..., None] * d_final_states.to(torch.float32) + G_loc
         Gs, Ds = _gather(G_loc, D, group)
@@ -286,6 +298,7 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
         else:  # the spans after this one, folded from the last backwards
             Gin = _fold(Gs[rank + 1:].flip(0), Ds[rank + 1:].flip(0))
     else:
+        G_loc, D = fold(1, False, ld, G)
         if rank == world - 1:
             Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                    else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
@@ -299,7 +312,8 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     dfin = fold(1, True, ld, G, Gin)
     dx, ddt, dA, d_init = local_bwd(xr, dtr, A, states, dyr, chunk_size, dfin, need_d_initial and rank == 0)
     dA = dA.to(torch.float32).contiguous()
-    dist.all_reduce(dA, group=group)
+    if world > 1:
+        dist.all_reduce(dA, group=group)
     if d_init is not None:
         d_init = d_init.reshape(B, K, H, P)[:, 0]
     return dx.reshape(B, Ls, H, P), ddt.reshape(B, Ls, H), dA, d_init

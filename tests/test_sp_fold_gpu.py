@@ -75,3 +75,36 @@ def test_span_state_matches_scan_state_only_passes_and_oracle(P, dtype, L, dt_ra
         e = float(np.abs(got.double().cpu().numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
         assert e <= 1e-4, f"{what}: normwise relative error {e:.3e} against the oracle"
         torch.testing.assert_close(got, scan, rtol=1e-4, atol=1e-5 * float(scan.abs().max()), msg=what)
+
+
+@pytest.mark.parametrize("K", [4, 8])
+def test_one_gpu_subspans_match_oracle(K):
+    """One GPU, one long sequence cut into K sub-spans run as batch rows (what
+    kernels/ema_sp.py does at world size 1 for long sequences: column-sum state
+    pass, expansion fold, full passes on the rows) against the float64 oracle
+    on the same bf16 inputs."""
+    import torch.distributed as dist
+    from _tol import assert_lowp_close
+    from kernels import ema_sp
+    from oracle import ema_oracle as eo
+    own = not dist.is_initialized()
+    if own:  # a one-rank group, as bench.py's config-4 leg uses on one GPU
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    try:
+        B, L, H, P, Q = 1, 8192, 4, 64, 256
+        x, dt, A, dy = eo.make_dt_inputs(B, L, H, P, seed=31)
+        tx, tdy = (torch.from_numpy(a).to(torch.bfloat16).to(DEV) for a in (x, dy))
+        tdt, tA = torch.from_numpy(dt).to(DEV), torch.from_numpy(A).to(DEV)
+        y, states, _, _ = ema_sp.sp_forward(tx, tdt, tA, Q, subspans=K)
+        assert states.shape[0] == B * K
+        dx, ddt, dA, _ = ema_sp.sp_backward(tx, tdt, tA, states, tdy, Q)
+        xf, dyf = tx.float().cpu().numpy(), tdy.float().cpu().numpy()
+        r = eo.ema_dt_fwd(xf, dt, A)
+        g = eo.ema_dt_bwd(xf, dt, A, dyf)
+        assert_lowp_close(y, r["y"], "y")
+        assert_lowp_close(dx, g["dx"], "dx")
+        assert_lowp_close(ddt, g["ddt"], "ddt")
+        assert_lowp_close(dA, g["dA"], "dA")
+    finally:
+        if own:
+            dist.destroy_process_group()

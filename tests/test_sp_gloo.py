@@ -107,10 +107,12 @@ def _worker(rank, world, port, with_init, exchange, subspans, errq):
         raise
 
 
-# subspans: None = the automatic choice (here 2 or 1 sub-spans per rank's span)
+# subspans: None = the automatic choice (here 2 or 1 sub-spans per rank's span);
+# world 1 with sub-spans: one GPU's sequence cut into sub-spans, nothing exchanged
 @pytest.mark.parametrize("world,with_init,exchange,subspans", [
     (2, False, "chain", None), (3, True, "chain", None), (3, True, "allgather", None), (4, False, "allgather", None),
-    (2, True, "chain", 4), (3, True, "allgather", 2), (2, True, "allgather", 3)])
+    (2, True, "chain", 4), (3, True, "allgather", 2), (2, True, "allgather", 3),
+    (1, True, "chain", 4), (1, False, "allgather", 3)])
 def test_sequence_parallel_matches_whole_sequence(world, with_init, exchange, subspans):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
@@ -129,3 +131,17 @@ def test_span_decay_composes():
     x, dt, A, _ = eo.make_dt_inputs(1, 128, 2, 4, seed=3)
     D = span_decay(torch.from_numpy(dt), torch.from_numpy(A)).double().numpy()
     np.testing.assert_allclose(D, np.exp(dt.sum(1) * A), rtol=1e-6)
+
+
+def test_subspan_counts_at_config_4():
+    """The sub-span rule at config 4 (B1 L65536 H32, chunk 256): 16 on one GPU,
+    32 / 16 / 8 per rank over 2 / 4 / 8 ranks; config 2 (B8 L4096) on one GPU
+    runs whole."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "ema-kernels_b200"))
+    from kernels.ema_sp import subspan_count
+
+    assert subspan_count(1, 32, 65536, 256, 1) == 16
+    assert [subspan_count(1, 32, 65536 // r, 256, r) for r in (2, 4, 8)] == [32, 16, 8]
+    assert subspan_count(8, 32, 4096, 256, 1) == 1
