@@ -15,7 +15,9 @@ would join the model's gradient all-reduce, which this op does not own).
 Extra keys on the same line: ``weak`` (every rank a whole B8 batch),
 ``sp_config4`` (config 4, one B1 L65536 sequence split over the ranks with
 the NCCL state chain, and its error against the single-GPU op; at N > 1 also
-``sp_config4_allgather``, the same with one all_gather per direction) and
+``sp_config4_allgather``, the same with one all_gather per direction, and
+``sp_config4_p2p``, the same with the exchange and both sub-span folds as one
+kernel over NVLink peer memory) and
 ``ssd_config5`` (config 5, the Mamba-2 SSD at B32 L8192 H80 split by batch
 rows); rank 0 adds ``bench_ema_total``, the reference's own benchmark
 (ema_combined against its d_state-1 mamba_chunk_scan_combined call) on the
@@ -344,9 +346,10 @@ def run_sp(args, rank, world, local_rank):
                        "timing": leg["timing"]},
             "roofline": leg["roofline"], "max_rel_err_vs_single_gpu": leg["max_rel_err_vs_single_gpu"],
             # per step and direction: the column-sum state pass, the span summary fold (ranks > 1),
-            # the expansion fold and the full pass (dt transpose + scan); the whole sequence as
-            # 32 chains (no sub-spans): dt transpose + scan per direction
-            "gpu_launches": leg["steps"] * _sp_launches_per_step(world),
+            # the expansion fold and the full pass (dt transpose + scan), or with "p2p" the
+            # column sums, the exchange kernel and the full pass; the whole sequence as 32 chains
+            # (no sub-spans): dt transpose + scan per direction
+            "gpu_launches": leg["steps"] * _sp_launches_per_step(world, args.exchange),
         }), flush=True)
     if dist is not None:
         dist.barrier()
@@ -449,12 +452,14 @@ def _max_over_ranks(vals, dev, dist):
     return [float(v) for v in t.tolist()]
 
 
-def _sp_launches_per_step(world):
+def _sp_launches_per_step(world, exchange="chain"):
     """This library's kernels per config-4 SP step (see run_sp)."""
     from kernels import ema_sp
     c = SP_CFG
     if world == 1 and ema_sp.subspan_count(c["B"], c["H"], c["L"], c["Q"], 1) == 1:
         return 4
+    if world > 1 and exchange == "p2p":  # column sums, the exchange kernel, dt transpose, scan
+        return 8
     return 2 * (4 + (world > 1))
 
 
@@ -532,8 +537,10 @@ def _sp_leg(args, rank, world, dev, dist, exchange="chain"):
             "value": tokens / (ms * 1e-3) / 1e6, "unit": "Mtokens/s", "ms_per_step": ms, "steps": K,
             "scaling": "strong", "span_per_rank": span,
             "parallelism": (f"sequence parallel over {world} GPU(s): "
-                            + ("NCCL send/recv state chain" if exchange == "chain" else
-                               "one NCCL all_gather of the span summaries per direction") + " + dA all-reduce")
+                            + {"chain": "NCCL send/recv state chain",
+                               "allgather": "one NCCL all_gather of the span summaries per direction",
+                               "p2p": "summary, exchange and expansion in one kernel over NVLink peer memory "
+                                      "(ema_span_exchange) per direction"}[exchange] + " + dA all-reduce")
                            if world > 1 else (f"one GPU: the sequence cut into {ema_sp.subspan_count(c['B'], c['H'], c['L'], c['Q'], 1)} "
                                               "sub-spans run as batch rows, no exchange"),
             "roofline": {"bound": "hbm", "achieved_per_gpu": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
@@ -789,7 +796,7 @@ def run_ema(args, rank, world, local_rank):
     (e2e_ms,) = _max_over_ranks([e0.elapsed_time(e1) / E], dev, dist)
     del bufs
 
-    sp = sp_ag = ssd5 = total = None
+    sp = sp_ag = sp_p2p = ssd5 = total = None
     if not args.no_extra_legs:
         try:
             sp = _sp_leg(args, rank, world, dev, dist)
@@ -800,6 +807,10 @@ def run_ema(args, rank, world, local_rank):
                 sp_ag = _sp_leg(args, rank, world, dev, dist, exchange="allgather")
             except Exception as e:
                 sp_ag = {"unavailable": f"{type(e).__name__}: {e}"}
+            try:
+                sp_p2p = _sp_leg(args, rank, world, dev, dist, exchange="p2p")
+            except Exception as e:
+                sp_p2p = {"unavailable": f"{type(e).__name__}: {e}"}
         torch.cuda.empty_cache()
         try:
             ssd5 = _ssd5_leg(args, rank, world, dev, dist)
@@ -861,6 +872,8 @@ def run_ema(args, rank, world, local_rank):
             line["sp_config4"] = sp
         if sp_ag is not None:
             line["sp_config4_allgather"] = sp_ag
+        if sp_p2p is not None:
+            line["sp_config4_p2p"] = sp_p2p
         if ssd5 is not None:
             line["ssd_config5"] = ssd5
         if total is not None:
@@ -893,8 +906,9 @@ def main():
     ap.add_argument("--ema-forward", choices=["scan", "tc"], default="scan",
                     help="EMA forward kernel: scan (CUDA-core scan at chunk 256, the default) or tc (the tcgen05 "
                          "forward, ema_fwd_tc_kernel, at chunk 128; for comparison)")
-    ap.add_argument("--exchange", choices=["chain", "allgather"], default="chain",
-                    help="with --workload sp: the span exchange (NCCL send/recv chain or one all_gather)")
+    ap.add_argument("--exchange", choices=["chain", "allgather", "p2p"], default="chain",
+                    help="with --workload sp: the span exchange (NCCL send/recv chain, one all_gather, or one "
+                         "kernel over NVLink peer memory)")
     ap.add_argument("--workload", choices=["ema", "ssd", "sp"], default="ema",
                     help="ema: config 2 (the headline); ssd: config 3 (Mamba-2 SSD B8 L4096 H64 P64 N128 G1); "
                          "sp: config 4 (EMA B1 L65536 H32 P64, the sequence split over the ranks)")

@@ -126,6 +126,19 @@ class EmaSpanFoldArgs(ctypes.Structure):
     ]
 
 
+SPAN_EXCHANGE_MAX_RANKS = 8
+P2P_HANDLE_BYTES = 64
+
+
+class EmaSpanExchangeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("subspans", _i64), ("nheads", _i64), ("headdim", _i64),
+        ("direction", _i32), ("rank", _i32), ("world", _i32), ("reserved", _i32),
+        ("log_decay", _ptr), ("values", _ptr), ("boundary", _ptr), ("span_in", _ptr), ("out", _ptr),
+        ("buffer_bytes", ctypes.c_uint64), ("buffers", _ptr * SPAN_EXCHANGE_MAX_RANKS),
+    ]
+
+
 class EmaSpanStateArgs(ctypes.Structure):
     _fields_ = [
         ("rows", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64),
@@ -168,6 +181,22 @@ lib.ema_span_expand.restype = ctypes.c_int
 lib.ema_span_expand.argtypes = [ctypes.POINTER(EmaSpanFoldArgs), _ptr]
 lib.ema_span_state_launch.restype = ctypes.c_int
 lib.ema_span_state_launch.argtypes = [ctypes.POINTER(EmaSpanStateArgs), _ptr]
+lib.ema_span_exchange_bytes.restype = ctypes.c_size_t
+lib.ema_span_exchange_bytes.argtypes = [_i64, _i64, _i64]
+lib.ema_span_exchange.restype = ctypes.c_int
+lib.ema_span_exchange.argtypes = [ctypes.POINTER(EmaSpanExchangeArgs), _ptr]
+lib.ema_span_exchange_status.restype = ctypes.c_int
+lib.ema_span_exchange_status.argtypes = [_ptr, ctypes.POINTER(ctypes.c_uint32), _i32]
+lib.ema_p2p_alloc.restype = ctypes.c_int
+lib.ema_p2p_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+lib.ema_p2p_free.restype = ctypes.c_int
+lib.ema_p2p_free.argtypes = [_ptr]
+lib.ema_p2p_handle.restype = ctypes.c_int
+lib.ema_p2p_handle.argtypes = [_ptr, ctypes.POINTER(ctypes.c_ubyte)]
+lib.ema_p2p_open.restype = ctypes.c_int
+lib.ema_p2p_open.argtypes = [ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_void_p)]
+lib.ema_p2p_close.restype = ctypes.c_int
+lib.ema_p2p_close.argtypes = [_ptr]
 lib.ssd_device_status.restype = ctypes.c_int
 lib.ssd_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _ptr]
 lib.ema_last_error.restype = ctypes.c_char_p

@@ -46,7 +46,8 @@ import torch.distributed as dist
 from . import _lib
 from .ema_chunk_scan import backward_chunk, ema_chunk_scan_bwd, ema_chunk_scan_fwd
 
-__all__ = ["span_decay", "span_state", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp"]
+__all__ = ["span_decay", "span_state", "subspan_count", "sp_forward", "sp_backward", "ema_chunk_scan_sp",
+           "p2p_exchange_status"]
 
 
 def span_decay(dt: torch.Tensor, A: torch.Tensor) -> torch.Tensor:
@@ -78,6 +79,101 @@ def _fold(V: torch.Tensor, D: torch.Tensor) -> torch.Tensor:
     return (w[..., None] * V).sum(dim=0)
 
 
+class _P2PExchange:
+    """Exchange buffers of one process group for the "p2p" span exchange
+    (ema_span_exchange): this rank's buffer (ema_p2p_alloc, zeroed) and every
+    peer's, mapped through CUDA IPC.  Built on the first exchange of a
+    (group, device, batch x heads, headdim) -- outside CUDA graph capture --
+    and kept for the life of the process.  The ranks must sit on different
+    GPUs: the kernel of every rank waits for the others' flags, which two
+    launches on one GPU cannot be relied on to satisfy."""
+    _cache = {}
+
+    @classmethod
+    def get(cls, group, device, bh: int, P: int):
+        key = (id(group), device.index, bh, P)
+        ex = cls._cache.get(key)
+        if ex is None:
+            assert not torch.cuda.is_current_stream_capturing(), \
+                "the p2p span exchange sets up its buffers on its first call, outside CUDA graph capture"
+            ex = cls._cache[key] = cls(group, device, bh, P)
+        return ex
+
+    def __init__(self, group, device, bh: int, P: int):
+        import ctypes
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > _lib.SPAN_EXCHANGE_MAX_RANKS:
+            raise ValueError(f"the p2p span exchange takes at most {_lib.SPAN_EXCHANGE_MAX_RANKS} ranks")
+        uuids = [None] * self.world
+        dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(device).uuid), group=group)
+        if len(set(uuids)) != self.world:
+            raise ValueError("the p2p span exchange needs every rank on its own GPU")
+        self.nbytes = int(_lib.lib.ema_span_exchange_bytes(self.world, bh, P))
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.P2P_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            _lib.check(_lib.lib.ema_p2p_alloc(self.nbytes, ctypes.byref(own)), "ema_p2p_alloc")
+            _lib.check(_lib.lib.ema_p2p_handle(own, handle), "ema_p2p_handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self.ptrs = []
+            for q, hb in enumerate(handles):
+                if q == self.rank:
+                    self.ptrs.append(own.value)
+                    continue
+                peer = ctypes.c_void_p()
+                hq = (ctypes.c_ubyte * _lib.P2P_HANDLE_BYTES).from_buffer_copy(hb)
+                _lib.check(_lib.lib.ema_p2p_open(hq, ctypes.byref(peer)), "ema_p2p_open")
+                self.ptrs.append(peer.value)
+        dist.barrier(group=group)  # every buffer zeroed and mapped everywhere before the first exchange
+
+    def status(self, clear: bool = False) -> int:
+        """The own buffer's status word (bit 1: a wait for a peer's flag passed 1 s)."""
+        import ctypes
+        word = ctypes.c_uint32()
+        _lib.check(_lib.lib.ema_span_exchange_status(ctypes.c_void_p(self.ptrs[self.rank]), ctypes.byref(word),
+                                                     int(clear)), "ema_span_exchange_status")
+        return int(word.value)
+
+
+def _p2p_exchange(direction: int, ld: torch.Tensor, V: torch.Tensor, boundary: Optional[torch.Tensor], group):
+    """The span exchange in one kernel over NVLink peer memory (ema_span_exchange):
+    the summary of this rank's sub-spans, the exchange, the fold of the spans
+    before (direction 0) / after (direction 1) this one and its expansion over
+    the sub-spans.  ld (B, K, H) float64, V (B K, H, P) fp32, ``boundary`` the
+    sequence's initial state (direction 0) / final-state gradient (direction 1)
+    or None.  Returns (span boundary value (B, H, P), per sub-span (B K, H, P))."""
+    B, K, H = ld.shape
+    P = V.shape[-1]
+    ex = _P2PExchange.get(group, V.device, B * H, P)
+    ld, V = ld.contiguous(), V.to(torch.float32).contiguous()
+    bnd = None if boundary is None else boundary.to(torch.float32).contiguous()
+    span_in = torch.empty(B, H, P, dtype=torch.float32, device=V.device)
+    out = torch.empty(B * K, H, P, dtype=torch.float32, device=V.device)
+    a = _lib.EmaSpanExchangeArgs()
+    a.batch, a.subspans, a.nheads, a.headdim = B, K, H, P
+    a.direction, a.rank, a.world = direction, ex.rank, ex.world
+    a.log_decay, a.values = ld.data_ptr(), V.data_ptr()
+    a.boundary = None if bnd is None else bnd.data_ptr()
+    a.span_in, a.out = span_in.data_ptr(), out.data_ptr()
+    a.buffer_bytes = ex.nbytes
+    for q, ptr in enumerate(ex.ptrs):
+        a.buffers[q] = ptr
+    with torch.cuda.device(V.device):
+        _lib.check(_lib.lib.ema_span_exchange(a, _lib.stream_ptr(V.device)), "ema_span_exchange")
+    return span_in, out
+
+
+def p2p_exchange_status(group=None, device=None, clear: bool = False) -> int:
+    """OR of the status words of this process's p2p exchange buffers for
+    ``group`` (0: every wait saw its peers' flags in time)."""
+    st = 0
+    for (gid, dev, _, _), ex in _P2PExchange._cache.items():
+        if gid == id(group) and (device is None or dev == torch.device(device).index):
+            st |= ex.status(clear)
+    return st
+
+
 def _peer(group, r):
     """Global rank of group rank ``r`` (send/recv address global ranks)."""
     return r if group is None else dist.get_global_rank(group, r)
@@ -107,6 +203,7 @@ def span_state(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, direction: in
 
 
 _SPAN_STATE_P = (32, 64, 128)
+_EXCHANGES = ("chain", "allgather", "p2p")
 
 
 # The state callables of sp_forward / sp_backward return the sub-span rows'
@@ -215,9 +312,11 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     ``chunk_start_states`` of the sub-span rows (B K, nchunks, H, P), what
     :func:`sp_backward` takes; ``Sin`` the state entering this span; ``final``
     this span's end state (the sequence's final state on the last rank).
-    ``exchange``: "chain" (NCCL send/recv r -> r+1) or "allgather" (one
-    all_gather of the span summaries)."""
-    assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
+    ``exchange``: "chain" (NCCL send/recv r -> r+1), "allgather" (one
+    all_gather of the span summaries) or "p2p" (summary, exchange, fold and
+    expansion in one kernel over NVLink peer memory, ema_span_exchange; every
+    rank on its own GPU, headdim <= 128)."""
+    assert exchange in _EXCHANGES, "exchange must be 'chain', 'allgather' or 'p2p'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, Ls, H, P = x.shape
     K = subspans if subspans is not None else subspan_count(B, H, Ls, chunk_size, world)
@@ -230,9 +329,12 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
     xr, dtr = _rows(x, K), _rows(dt, K)
     # sub-span summaries (end states from zero, log decays) -> the span's end state from zero, its decay
     S, ld = _values_and_logs(state_fwd(xr, dtr, A, chunk_size), dtr, A, B, K)
+    init = None
     if world == 1:  # one span cut into sub-spans: nothing to exchange
         Sin = (initial_states.to(torch.float32).clone() if initial_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    elif exchange == "p2p":  # summary, exchange, fold and expansion in one kernel
+        Sin, init = _p2p_exchange(0, ld, S, initial_states if rank == 0 else None, group)
     elif exchange == "allgather":
         S_loc, D = fold(0, False, ld, S)
         if rank == 0 and initial_states is not None:  # rank 0's summary includes the initial state
@@ -255,7 +357,8 @@ def sp_forward(x, dt, A, chunk_size: int = 256, group=None, initial_states: Opti
             Sout = D[..., None] * Sin + S_loc
             dist.send(Sout.to(torch.float32).contiguous(), dst=_peer(group, rank + 1), group=group)
     # the state entering every sub-span, from the state entering the span
-    init = fold(0, True, ld, S, Sin)
+    if init is None:
+        init = fold(0, True, ld, S, Sin)
     y, states, final = local_fwd(xr, dtr, A, chunk_size, init)
     return y.reshape(B, Ls, H, P), states, Sin, final.reshape(B, K, H, P)[:, -1]
 
@@ -272,7 +375,7 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     d_initial): dx and ddt in x's and dt's layouts; dA summed over the group;
     d_initial (rank 0, when asked) the gradient w.r.t. the sequence's initial
     state.  ``exchange`` as in :func:`sp_forward`, running r+1 -> r."""
-    assert exchange in ("chain", "allgather"), "exchange must be 'chain' or 'allgather'"
+    assert exchange in _EXCHANGES, "exchange must be 'chain', 'allgather' or 'p2p'"
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, Ls, H, P = x.shape
     if world == 1 and states.shape[0] == B:  # one span, whole
@@ -284,9 +387,12 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
     xr, dtr, dyr = _rows(x, K), _rows(dt, K), _rows(dy, K)
     # sub-span summaries (start gradients from their own dy, nothing arriving) -> the span's
     G, ld = _values_and_logs(state_bwd(xr, dtr, A, states, dyr, chunk_size), dtr, A, B, K)
+    dfin = None
     if world == 1:  # one span cut into sub-spans: nothing to exchange
         Gin = (d_final_states.to(torch.float32).clone() if d_final_states is not None
                else torch.zeros(B, H, P, dtype=torch.float32, device=x.device))
+    elif exchange == "p2p":  # summary, exchange, fold and expansion in one kernel
+        Gin, dfin = _p2p_exchange(1, ld, G, d_final_states if rank == world - 1 else None, group)
     elif exchange == "allgather":
         G_loc, D = fold(1, False, ld, G)
         if rank == world - 1 and d_final_states is not None:  # the last summary includes the final gradient
@@ -309,7 +415,8 @@ def sp_backward(x, dt, A, states, dy, chunk_size: int = 256, group=None,
             Gout = D[..., None] * Gin + G_loc
             dist.send(Gout.to(torch.float32).contiguous(), dst=_peer(group, rank - 1), group=group)
     # the gradient arriving at every sub-span's end, from the one arriving at the span's end
-    dfin = fold(1, True, ld, G, Gin)
+    if dfin is None:
+        dfin = fold(1, True, ld, G, Gin)
     dx, ddt, dA, d_init = local_bwd(xr, dtr, A, states, dyr, chunk_size, dfin, need_d_initial and rank == 0)
     dA = dA.to(torch.float32).contiguous()
     if world > 1:
@@ -339,5 +446,6 @@ class _EmaChunkScanSPFn(torch.autograd.Function):
 def ema_chunk_scan_sp(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, chunk_size: int = 256, group=None,
                       exchange: str = "chain"):
     """Autograd op over this rank's span of a sequence split across ``group``;
-    ``exchange``: "chain" (NCCL send/recv between neighbours) or "allgather"."""
+    ``exchange``: "chain" (NCCL send/recv between neighbours), "allgather" or
+    "p2p" (one kernel over NVLink peer memory)."""
     return _EmaChunkScanSPFn.apply(x, dt, A, chunk_size, group, exchange)

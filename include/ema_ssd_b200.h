@@ -257,6 +257,54 @@ typedef struct EmaSpanStateArgs {
 } EmaSpanStateArgs;
 EMA_API int ema_span_state_launch(const EmaSpanStateArgs* args, void* stream);
 
+/* The span exchange of the sequence-parallel EMA over NVLink peer memory, in
+ * one kernel: each rank's span summary from its sub-spans (as
+ * ema_span_summary), the summaries written into every rank's exchange buffer
+ * with a flag per (rank, batch x head), a bounded wait for every rank's flags,
+ * the fold of the spans before this one (direction 0) / after it (direction
+ * 1) into `span_in`, and its expansion into every sub-span (as
+ * ema_span_expand) into `out`.  No counterpart in the reference (its
+ * sequence-parallel hooks are the d_ossm_state / d_issm_state arguments of
+ * compute_dpx, kernels/backward/ema_ssd_bwd.py:111-117, :293-295); it replaces
+ * the NCCL exchange of kernels/ema_sp.py for groups whose ranks are on
+ * different GPUs of one NVLink domain.
+ * Collective: every rank of the group calls it with the same shapes in the
+ * same order.  `buffers[q]` is rank q's exchange buffer as mapped in this
+ * process (buffers[rank] its own, from ema_p2p_alloc; the others from
+ * ema_p2p_open of the owners' ema_p2p_handle), all of `buffer_bytes` >=
+ * ema_span_exchange_bytes(world, batch * nheads, headdim), zeroed before the
+ * group's first call.  `boundary` (optional, (batch, nheads, headdim)): the
+ * sequence's initial state (direction 0, used on rank 0) or the gradient
+ * w.r.t. its final state (direction 1, used on the last rank).  headdim <=
+ * 128, at most 64 sub-spans, at most EMA_SPAN_EXCHANGE_MAX_RANKS ranks, and
+ * batch * nheads CTAs that fit on the GPU at once (refused otherwise).  A wait
+ * that passes 1 s sets bit 1 of the buffer's status word
+ * (ema_span_exchange_status) and the kernel finishes with wrong values. */
+#define EMA_SPAN_EXCHANGE_MAX_RANKS 8
+#define EMA_P2P_HANDLE_BYTES 64
+typedef struct EmaSpanExchangeArgs {
+  int64_t batch, subspans, nheads, headdim;
+  int32_t direction, rank, world, reserved;
+  const double* log_decay; /* (batch, subspans, nheads) */
+  const float* values;     /* (batch subspans, nheads, headdim): the sub-spans' boundary values */
+  const float* boundary;   /* or NULL */
+  float* span_in;          /* (batch, nheads, headdim) */
+  float* out;              /* (batch subspans, nheads, headdim) */
+  uint64_t buffer_bytes;
+  void* buffers[EMA_SPAN_EXCHANGE_MAX_RANKS];
+} EmaSpanExchangeArgs;
+EMA_API size_t ema_span_exchange_bytes(int64_t world, int64_t batch_heads, int64_t headdim);
+EMA_API int ema_span_exchange(const EmaSpanExchangeArgs* args, void* stream);
+EMA_API int ema_span_exchange_status(void* own_buffer, uint32_t* status, int32_t clear);
+/* Exchange buffers: cudaMalloc + zero (ema_p2p_alloc / ema_p2p_free) and their
+ * CUDA IPC handles (ema_p2p_handle fills EMA_P2P_HANDLE_BYTES bytes; a peer
+ * process maps the buffer with ema_p2p_open and unmaps it with ema_p2p_close). */
+EMA_API int ema_p2p_alloc(size_t bytes, void** ptr);
+EMA_API int ema_p2p_free(void* ptr);
+EMA_API int ema_p2p_handle(void* ptr, unsigned char* handle);
+EMA_API int ema_p2p_open(const unsigned char* handle, void** ptr);
+EMA_API int ema_p2p_close(void* ptr);
+
 /* ---- utilities ------------------------------------------------------------ */
 /* Copies the workspace status word to *status (synchronises with `stream`). */
 EMA_API int ema_workspace_status(const void* workspace, uint32_t* status, void* stream);

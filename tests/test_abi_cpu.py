@@ -54,6 +54,7 @@ def test_struct_layouts_match_header():
 
 
 @pytest.mark.parametrize("header,struct", [("ema_ssd_b200.h", "EmaSpanFoldArgs"), ("ema_ssd_b200.h", "EmaSpanStateArgs"),
+                                           ("ema_ssd_b200.h", "EmaSpanExchangeArgs"),
                                            ("ssd_b200.h", "SsdGateArgs")])
 def test_every_field_offset_matches_header(header, struct):
     """The ctypes mirror of `struct` has the C size and every field at the C offset."""
