@@ -190,3 +190,37 @@ def test_chunk_cumsum_validation_without_gpu():
     assert _lib.lib.chunk_cumsum_launch(None, st, None, st, None, st, 1, 1, 1, 64, 0, None) == 1
     fake = 1 << 20
     assert _lib.lib.chunk_cumsum_launch(fake, st, fake, st, fake, st, 1, 1, 1, 2048, 0, None) == 2
+
+
+def test_span_exchange_sizing_and_validation_without_gpu():
+    """ema_span_exchange (the sequence-parallel exchange over NVLink peer
+    memory): buffer sizing, and the argument checks that run before any CUDA
+    call -- shape, rank, headdim, sub-span and buffer limits."""
+    import ctypes
+    from kernels import _lib
+    L = _lib.lib
+    assert L.ema_span_exchange_bytes(0, 32, 64) == 0 and L.ema_span_exchange_bytes(9, 32, 64) == 0
+    n2, n4 = L.ema_span_exchange_bytes(2, 32, 64), L.ema_span_exchange_bytes(4, 32, 64)
+    # header 256 + flags (8 ranks x 32 words, 256-aligned) + 2 parities x ranks x 32 x 65 floats
+    assert n2 == 256 + 1024 + 2 * 2 * 32 * 65 * 4 and n4 == 256 + 1024 + 2 * 4 * 32 * 65 * 4
+
+    def args(**kw):
+        a = _lib.EmaSpanExchangeArgs()
+        a.batch, a.subspans, a.nheads, a.headdim = 1, 8, 32, 64
+        a.direction, a.rank, a.world = 0, 0, 2
+        a.log_decay = a.values = a.span_in = a.out = 16  # never dereferenced: the checks fail first
+        a.buffer_bytes = n2
+        a.buffers[0] = a.buffers[1] = 16
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    cases = [(dict(headdim=256), 2, b"headdim"), (dict(subspans=65), 2, b"sub-spans"),
+             (dict(rank=2), 1, b"rank"), (dict(world=9, rank=0), 1, b"rank"), (dict(direction=2), 1, b"direction"),
+             (dict(values=None), 1, b"required"), (dict(buffer_bytes=n2 - 4), 3, b"buffers hold"),
+             (dict(batch=0), 1, b"shape")]
+    for kw, code, text in cases:
+        assert L.ema_span_exchange(ctypes.byref(args(**kw)), None) == code, kw
+        assert text in L.ema_last_error(), (kw, L.ema_last_error())
+    assert L.ema_span_exchange(None, None) == 1
+    assert L.ema_p2p_alloc(0, ctypes.byref(ctypes.c_void_p())) == 1
