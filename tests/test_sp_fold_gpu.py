@@ -108,3 +108,87 @@ def test_one_gpu_subspans_match_oracle(K):
     finally:
         if own:
             dist.destroy_process_group()
+
+
+def _exchange_args(_lib, B, K, H, P, direction, rank, world, ld, V, bnd, span_in, out, bufs, nbytes):
+    a = _lib.EmaSpanExchangeArgs()
+    a.batch, a.subspans, a.nheads, a.headdim = B, K, H, P
+    a.direction, a.rank, a.world = direction, rank, world
+    a.log_decay, a.values = ld.data_ptr(), V.data_ptr()
+    a.boundary = None if bnd is None else bnd.data_ptr()
+    a.span_in, a.out = span_in.data_ptr(), out.data_ptr()
+    a.buffer_bytes = nbytes
+    for q, b in enumerate(bufs):
+        a.buffers[q] = b.value
+    return a
+
+
+@pytest.mark.parametrize("direction", [0, 1])
+def test_exchange_kernel_one_rank_expands_like_the_fold(direction):
+    """The peer-memory exchange kernel (ema_span_exchange) as a one-rank group
+    on one GPU: no peer to wait for, the span's boundary value is the given
+    one, and its expansion over the sub-spans (a float64 recurrence) matches
+    the float64 pairwise fold; three calls in a row on the same buffer."""
+    import ctypes
+    from kernels import _lib
+    L = _lib.lib
+    B, K, H, P = 2, 8, 5, 48
+    g = torch.Generator().manual_seed(40 + direction)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nbytes = L.ema_span_exchange_bytes(1, B * H, P)
+    buf = ctypes.c_void_p()
+    _lib.check(L.ema_p2p_alloc(nbytes, ctypes.byref(buf)), "ema_p2p_alloc")
+    try:
+        for call in range(3):
+            ld = (-torch.rand(B, K, H, generator=g, dtype=torch.float64) * (0.05, 30.0, 2.0)[call]).to(dev)
+            V = torch.randn(B * K, H, P, generator=g).to(dev)
+            bnd = torch.randn(B, H, P, generator=g).to(dev)
+            span_in = torch.empty(B, H, P, device=dev)
+            out = torch.empty(B * K, H, P, device=dev)
+            a = _exchange_args(_lib, B, K, H, P, direction, 0, 1, ld, V, bnd, span_in, out, [buf], nbytes)
+            _lib.check(L.ema_span_exchange(ctypes.byref(a), _lib.stream_ptr(dev)), "ema_span_exchange")
+            torch.testing.assert_close(span_in, bnd, rtol=0, atol=0)
+            torch.testing.assert_close(out, torch_fold(direction, True, ld, V, bnd), rtol=1e-6, atol=1e-6)
+        word = ctypes.c_uint32()
+        _lib.check(L.ema_span_exchange_status(buf, ctypes.byref(word), 0), "ema_span_exchange_status")
+        assert word.value == 0
+    finally:
+        L.ema_p2p_free(buf)
+
+
+def test_exchange_wait_for_a_missing_rank_runs_out_and_reports():
+    """Failure detection of the exchange kernel without a second GPU: rank 0 of
+    a two-rank group whose rank 1 never calls (its flags are never set; both
+    buffers are local).  The bounded wait gives up after about 1 s, sets bit 1
+    of the buffer's status word and the launch finishes; clearing the word
+    leaves it at zero."""
+    import ctypes
+    import time
+    from kernels import _lib
+    L = _lib.lib
+    B, K, H, P = 1, 4, 2, 64
+    dev = torch.device("cuda", torch.cuda.current_device())
+    nbytes = L.ema_span_exchange_bytes(2, B * H, P)
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in bufs:
+        _lib.check(L.ema_p2p_alloc(nbytes, ctypes.byref(b)), "ema_p2p_alloc")
+    try:
+        ld = -torch.rand(B, K, H, dtype=torch.float64, device=dev)
+        V = torch.randn(B * K, H, P, device=dev)
+        span_in = torch.empty(B, H, P, device=dev)
+        out = torch.empty(B * K, H, P, device=dev)
+        a = _exchange_args(_lib, B, K, H, P, 0, 0, 2, ld, V, None, span_in, out, bufs, nbytes)
+        torch.cuda.synchronize(dev)
+        t0 = time.monotonic()
+        _lib.check(L.ema_span_exchange(ctypes.byref(a), _lib.stream_ptr(dev)), "ema_span_exchange")
+        torch.cuda.synchronize(dev)
+        waited = time.monotonic() - t0
+        word = ctypes.c_uint32()
+        _lib.check(L.ema_span_exchange_status(bufs[0], ctypes.byref(word), 1), "ema_span_exchange_status")
+        assert word.value == 1, f"status word {word.value}"
+        assert 0.9 <= waited < 20.0, f"the wait ended after {waited:.2f} s"
+        _lib.check(L.ema_span_exchange_status(bufs[0], ctypes.byref(word), 0), "ema_span_exchange_status")
+        assert word.value == 0
+    finally:
+        for b in bufs:
+            L.ema_p2p_free(b)
